@@ -1,0 +1,413 @@
+// Blackwell (sm_100a) additive-attention forward for bf16/fp16 inputs, head dim 64 or 128.
+//
+// Per CTA: 128 query rows of one (batch, head), one thread per row, 4 warps; two CTAs per SM.
+//   * K and V tiles of 64 keys stream into shared memory with TMA (3-D tensor maps over
+//     [BH, N, D], no multicast), 2-3 stages, completion on mbarriers.
+//   * Scores are an FMA/MUFU elementwise reduction, not a GEMM: each thread keeps its q row in
+//     fp32 registers and, for every key, accumulates w'[d] * tanh.approx(q[d] + k[d]) with
+//     fp32 FADD / MUFU / FFMA (w' = w * log2(e) / sqrt(D), so scores are in log2 units). K is
+//     read from shared memory with warp-broadcast 16-byte loads. On B200 the packed
+//     tanh.approx.{f16x2,bf16x2} forms deliver the same elements per second as the f32 form,
+//     so fp32 costs nothing and keeps full accumulation precision.
+//   * Softmax: each thread owns a whole row, so no cross-thread reduction. The row keeps a
+//     reference max m fixed from its first key tile; P = exp2(s - m). Only if a later tile's
+//     max exceeds m by more than 8 (P would exceed 256) is the row rescaled, which needs the
+//     accumulator in TMEM to be read, scaled and written back (rare: the scores of this
+//     operator are bounded by sum|w|/sqrt(D)).
+//   * P (bf16/fp16, the dtype of V) is written by the threads into a K-major 128-byte-swizzled
+//     shared tile; one elected thread issues tcgen05.mma (M=128, N=D, K=16 steps) with V as an
+//     MN-major operand, accumulating O in TMEM. MMA completion (tcgen05.commit -> mbarrier)
+//     gates the reuse of the P and V buffers, so the tensor core runs one tile behind the
+//     score computation.
+//   * Epilogue: tcgen05.ld of the row, scale by 1/l, store; lse = (m + log2 l) * ln 2.
+// Every mbarrier wait is bounded; a wait that gives up records an error code in the error
+// word (workspace) and the kernel still releases its TMEM and exits.
+#include "common.cuh"
+#include "sm100.cuh"
+#include "tma_host.cuh"
+
+namespace flb {
+
+namespace {
+
+constexpr float kLog2e = 1.4426950408889634f;
+constexpr float kLn2 = 0.6931471805599453f;
+constexpr uint32_t kWaitLimit = 1u << 22;
+constexpr float kRescaleThreshold = 8.f;  // log2 units
+
+template <int D>
+struct FwdCfg {
+  static constexpr int BM = 128, BN = 64;
+  static constexpr int STAGES = (D == 64) ? 3 : 2;
+  static constexpr int KTILE = BN * D * 2;   // bytes, bf16/fp16
+  static constexpr int VTILE = BN * D * 2;
+  static constexpr int PTILE = BM * BN * 2;  // 16 KB
+  static constexpr int OFF_V = 0;                          // 1024-aligned (swizzled)
+  static constexpr int OFF_P = OFF_V + STAGES * VTILE;     // 1024-aligned (swizzled)
+  static constexpr int OFF_K = OFF_P + 2 * PTILE;
+  static constexpr int OFF_W = OFF_K + STAGES * KTILE;
+  static constexpr int SMEM = OFF_W + D * 4 + 1024;        // + slack for 1024-alignment
+  static constexpr int TMEM_COLS = D;                      // 64 or 128 (power of two >= 32)
+};
+
+template <typename T> struct Unpack;
+template <> struct Unpack<__nv_bfloat16> {
+  static __device__ __forceinline__ void run(uint32_t v, float& a, float& b) {
+    a = __uint_as_float(v << 16);
+    b = __uint_as_float(v & 0xFFFF0000u);
+  }
+  static __device__ __forceinline__ uint32_t pack(float a, float b, float& ra, float& rb) {
+    __nv_bfloat162 h = __floats2bfloat162_rn(a, b);
+    ra = __low2float(h);
+    rb = __high2float(h);
+    return *reinterpret_cast<uint32_t*>(&h);
+  }
+  static constexpr int is_bf16 = 1;
+};
+template <> struct Unpack<__half> {
+  static __device__ __forceinline__ void run(uint32_t v, float& a, float& b) {
+    __half2 h = *reinterpret_cast<__half2*>(&v);
+    float2 f = __half22float2(h);
+    a = f.x;
+    b = f.y;
+  }
+  static __device__ __forceinline__ uint32_t pack(float a, float b, float& ra, float& rb) {
+    __half2 h = __floats2half2_rn(a, b);
+    float2 f = __half22float2(h);
+    ra = f.x;
+    rb = f.y;
+    return *reinterpret_cast<uint32_t*>(&h);
+  }
+  static constexpr int is_bf16 = 0;
+};
+
+__device__ __forceinline__ float ex2_approx(float x) {
+  float y;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
+
+template <int D, typename T>
+__global__ void __launch_bounds__(128, 2)
+attn_fwd_tc_kernel(const __grid_constant__ CUtensorMap tmK, const __grid_constant__ CUtensorMap tmV,
+                   const T* __restrict__ q, T* __restrict__ out, float* __restrict__ lse,
+                   float* __restrict__ scores, const float* __restrict__ w,
+                   const int32_t* __restrict__ w_index, int N, int causal, int* __restrict__ err) {
+  using namespace sm100;
+  using C = FwdCfg<D>;
+  using U = Unpack<T>;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* sm = (uint8_t*)(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
+  __shared__ __align__(8) uint64_t full_bar[C::STAGES];
+  __shared__ __align__(8) uint64_t mma_bar[2];
+  __shared__ uint32_t tmem_slot;
+
+  const int tid = threadIdx.x, warp = tid >> 5;
+  const int nqb = gridDim.x;
+  const int qb = causal ? (nqb - 1 - (int)blockIdx.x) : (int)blockIdx.x;  // heavy blocks first
+  const int bh = blockIdx.y;
+  const int m0 = qb * C::BM;
+  const int row = m0 + tid;
+  const bool row_ok = row < N;
+  const int kend = causal ? min(N, m0 + C::BM) : N;
+  const int ntiles = (kend + C::BN - 1) / C::BN;
+  const int warp_last_row = m0 + warp * 32 + 31;
+
+  float* sW = reinterpret_cast<float*>(sm + C::OFF_W);
+  if (tid < D) sW[tid] = w[(int64_t)w_index[bh] * D + tid] * (kLog2e * rsqrtf((float)D));
+  if (tid == 0) {
+    for (int s = 0; s < C::STAGES; ++s) mbar_init(&full_bar[s], 1);
+    mbar_init(&mma_bar[0], 1);
+    mbar_init(&mma_bar[1], 1);
+    fence_mbar_init();
+  }
+  if (warp == 0) {
+    tmem_alloc(&tmem_slot, C::TMEM_COLS);
+    tmem_relinquish();
+  }
+  // q row -> fp32 registers
+  float qr[D];
+  {
+    const uint4* src = reinterpret_cast<const uint4*>(q + ((int64_t)bh * N + (row_ok ? row : 0)) * D);
+#pragma unroll
+    for (int c = 0; c < D / 8; ++c) {
+      uint4 v = row_ok ? src[c] : make_uint4(0, 0, 0, 0);
+      U::run(v.x, qr[8 * c + 0], qr[8 * c + 1]);
+      U::run(v.y, qr[8 * c + 2], qr[8 * c + 3]);
+      U::run(v.z, qr[8 * c + 4], qr[8 * c + 5]);
+      U::run(v.w, qr[8 * c + 6], qr[8 * c + 7]);
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = tmem_slot;
+  const uint32_t tmem_row = tmem + ((uint32_t)(warp * 32) << 16);
+
+  auto issue_tile = [&](int t) {
+    const int s = t % C::STAGES;
+    mbar_arrive_expect_tx(&full_bar[s], C::KTILE + C::VTILE);
+    tma_load_3d(sm + C::OFF_K + s * C::KTILE, &tmK, &full_bar[s], 0, t * C::BN, bh);
+#pragma unroll
+    for (int vb = 0; vb < D / 64; ++vb)
+      tma_load_3d(sm + C::OFF_V + s * C::VTILE + vb * (C::BN * 128), &tmV, &full_bar[s], vb * 64,
+                  t * C::BN, bh);
+  };
+  if (tid == 0) {
+    tma_prefetch_desc(&tmK);
+    tma_prefetch_desc(&tmV);
+    for (int t = 0; t < min(ntiles, C::STAGES - 1); ++t) issue_tile(t);
+  }
+
+  float m_ref = 0.f, l = 0.f;
+  const uint32_t idesc = make_idesc_f16(128, D, U::is_bf16, 0, 1);
+
+  for (int t = 0; t < ntiles; ++t) {
+    const int s = t % C::STAGES;
+    const int j0 = t * C::BN;
+    if (!mbar_wait(&full_bar[s], (uint32_t)(t / C::STAGES) & 1u, kWaitLimit)) atomicExch(err, 1);
+    const uint8_t* sK = sm + C::OFF_K + s * C::KTILE;
+    const int b = t & 1;
+    // P buffer b was last read by MMA t-2
+    if (t >= 2 && !mbar_wait(&mma_bar[b], (uint32_t)((t - 2) >> 1) & 1u, kWaitLimit))
+      atomicExch(err, 3);
+    uint8_t* sP = sm + C::OFF_P + b * C::PTILE;
+
+    // Streaming over groups of 8 keys: scores (log2 units) -> P chunk of 16 bytes.
+#pragma unroll 1
+    for (int g = 0; g < C::BN / 8; ++g) {
+      const int jg = j0 + g * 8;
+      float s8[8];
+      if (causal && jg > warp_last_row) {  // warp-uniform: all 8 keys masked for every row
+#pragma unroll
+        for (int e = 0; e < 8; ++e) s8[e] = -INFINITY;
+      } else {
+        float acc[8][2];
+#pragma unroll
+        for (int e = 0; e < 8; ++e) acc[e][0] = acc[e][1] = 0.f;
+        const uint8_t* kg = sK + (g * 8) * D * 2;
+#pragma unroll
+        for (int c = 0; c < D / 8; ++c) {
+          const float4 w0 = reinterpret_cast<const float4*>(sW)[2 * c];
+          const float4 w1 = reinterpret_cast<const float4*>(sW)[2 * c + 1];
+#pragma unroll
+          for (int e = 0; e < 8; ++e) {
+            const uint4 kk = reinterpret_cast<const uint4*>(kg + e * D * 2)[c];
+            float k0, k1, k2, k3, k4, k5, k6, k7;
+            U::run(kk.x, k0, k1);
+            U::run(kk.y, k2, k3);
+            U::run(kk.z, k4, k5);
+            U::run(kk.w, k6, k7);
+            acc[e][0] = fmaf(w0.x, tanh_approx(qr[8 * c + 0] + k0), acc[e][0]);
+            acc[e][1] = fmaf(w0.y, tanh_approx(qr[8 * c + 1] + k1), acc[e][1]);
+            acc[e][0] = fmaf(w0.z, tanh_approx(qr[8 * c + 2] + k2), acc[e][0]);
+            acc[e][1] = fmaf(w0.w, tanh_approx(qr[8 * c + 3] + k3), acc[e][1]);
+            acc[e][0] = fmaf(w1.x, tanh_approx(qr[8 * c + 4] + k4), acc[e][0]);
+            acc[e][1] = fmaf(w1.y, tanh_approx(qr[8 * c + 5] + k5), acc[e][1]);
+            acc[e][0] = fmaf(w1.z, tanh_approx(qr[8 * c + 6] + k6), acc[e][0]);
+            acc[e][1] = fmaf(w1.w, tanh_approx(qr[8 * c + 7] + k7), acc[e][1]);
+          }
+        }
+#pragma unroll
+        for (int e = 0; e < 8; ++e) {
+          const int key = jg + e;
+          const bool ok = key < N && (!causal || key <= row);
+          s8[e] = ok ? (acc[e][0] + acc[e][1]) : -INFINITY;
+        }
+      }
+      if (scores != nullptr && row_ok) {
+        float* dst = scores + ((int64_t)bh * N + row) * N + jg;
+#pragma unroll
+        for (int e = 0; e < 8; ++e)
+          if (jg + e < N && (!causal || jg + e <= row)) dst[e] = s8[e] * kLn2;
+      }
+      float gm = s8[0];
+#pragma unroll
+      for (int e = 1; e < 8; ++e) gm = fmaxf(gm, s8[e]);
+
+      // reference max: fixed by the first group of the row; raised (rarely) when a group's max
+      // exceeds it by more than the threshold
+      if (t == 0 && g == 0) {
+        m_ref = row_ok ? gm : 0.f;
+      } else {
+        const bool need = row_ok && gm > m_ref + kRescaleThreshold;
+        if (__any_sync(0xffffffffu, need)) {
+          const float alpha = need ? ex2_approx(m_ref - gm) : 1.f;
+          if (need) {
+            l *= alpha;
+            m_ref = gm;
+            // chunks 0..g-1 of this tile's P row were written with the old reference
+            for (int c = 0; c < g; ++c) {
+              uint4* pc = reinterpret_cast<uint4*>(sP + sw128_offset(tid, c));
+              uint4 v = *pc;
+              uint32_t* vv = reinterpret_cast<uint32_t*>(&v);
+              float lo, hi, r0, r1;
+              for (int e = 0; e < 4; ++e) {
+                U::run(vv[e], lo, hi);
+                vv[e] = U::pack(lo * alpha, hi * alpha, r0, r1);
+              }
+              *pc = v;
+            }
+          }
+          if (t > 0) {
+            // the accumulator holds tiles < t: wait for the last issued MMA (tile t-1)
+            if (!mbar_wait(&mma_bar[(t - 1) & 1], (uint32_t)((t - 1) >> 1) & 1u, kWaitLimit))
+              atomicExch(err, 2);
+            tc_fence_after();
+#pragma unroll
+            for (int cb = 0; cb < D / 32; ++cb) {
+              uint32_t r[32];
+              tmem_ld32(tmem_row + cb * 32, r);
+              tmem_wait_ld();
+#pragma unroll
+              for (int i = 0; i < 32; ++i) r[i] = __float_as_uint(__uint_as_float(r[i]) * alpha);
+              tmem_st32(tmem_row + cb * 32, r);
+            }
+            tmem_wait_st();
+          }
+        }
+      }
+      uint32_t pk[4];
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        const float p0 = row_ok ? ex2_approx(s8[2 * e] - m_ref) : 0.f;
+        const float p1 = row_ok ? ex2_approx(s8[2 * e + 1] - m_ref) : 0.f;
+        float r0, r1;
+        pk[e] = U::pack(p0, p1, r0, r1);
+        l += r0 + r1;
+      }
+      *reinterpret_cast<uint4*>(sP + sw128_offset(tid, g)) = make_uint4(pk[0], pk[1], pk[2], pk[3]);
+    }
+    fence_async_shared();
+    tc_fence_before();
+    __syncthreads();
+
+    // ---- one thread: O += P @ V on the tensor core, then refill the freed stage ----------
+    if (tid == 0) {
+      tc_fence_after();
+      const uint32_t pa = smem_u32(sP);
+      const uint32_t vbase = smem_u32(sm + C::OFF_V + s * C::VTILE);
+#pragma unroll
+      for (int kk = 0; kk < C::BN / 16; ++kk) {
+        const uint64_t adesc = make_smem_desc(pa + kk * 32, 16, 1024, kSwizzle128B);
+        const uint64_t bdesc = make_smem_desc(vbase + kk * 2048, C::BN * 128, 1024, kSwizzle128B);
+        umma_f16(tmem, adesc, bdesc, idesc, (t > 0 || kk > 0) ? 1u : 0u);
+      }
+      umma_commit(&mma_bar[b]);
+      const int tn = t + C::STAGES - 1;
+      if (tn < ntiles) {
+        // stage tn % STAGES was last read by tile t-1 (K by all threads before this tile's
+        // barrier, V by MMA t-1)
+        if (t >= 1 && !mbar_wait(&mma_bar[(t - 1) & 1], (uint32_t)((t - 1) >> 1) & 1u, kWaitLimit))
+          atomicExch(err, 4);
+        fence_async_shared();
+        issue_tile(tn);
+      }
+    }
+    __syncwarp();
+  }
+
+  // ---- epilogue --------------------------------------------------------------------------
+  {
+    const int tl = ntiles - 1;
+    if (!mbar_wait(&mma_bar[tl & 1], (uint32_t)(tl >> 1) & 1u, kWaitLimit)) atomicExch(err, 5);
+  }
+  tc_fence_after();
+  const float inv_l = (row_ok && l > 0.f) ? 1.f / l : 0.f;
+  T* orow = out + ((int64_t)bh * N + (row_ok ? row : 0)) * D;
+#pragma unroll
+  for (int cb = 0; cb < D / 32; ++cb) {
+    uint32_t r[32];
+    tmem_ld32(tmem_row + cb * 32, r);
+    tmem_wait_ld();
+    if (row_ok) {
+#pragma unroll
+      for (int g = 0; g < 4; ++g) {
+        uint32_t pk[4];
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+          float r0, r1;
+          pk[e] = U::pack(__uint_as_float(r[8 * g + 2 * e]) * inv_l,
+                          __uint_as_float(r[8 * g + 2 * e + 1]) * inv_l, r0, r1);
+        }
+        reinterpret_cast<uint4*>(orow + cb * 32)[g] = make_uint4(pk[0], pk[1], pk[2], pk[3]);
+      }
+    }
+  }
+  if (row_ok) lse[(int64_t)bh * N + row] = (m_ref + __log2f(l)) * kLn2;
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 0) tmem_dealloc(tmem, C::TMEM_COLS);
+}
+
+template <int D, typename T>
+int launch_fwd_tc(const void* q, const void* k, const void* v, const float* w, const int32_t* wi,
+                  void* out, float* lse, float* scores, int64_t BH, int N, int causal, int* err,
+                  cudaStream_t s) {
+  using C = FwdCfg<D>;
+  const CUtensorMapDataType dt =
+      Unpack<T>::is_bf16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
+  CUtensorMap tmK, tmV;
+  const uint64_t dims[3] = {(uint64_t)D, (uint64_t)N, (uint64_t)BH};
+  const uint64_t strides[2] = {(uint64_t)D * 2, (uint64_t)N * D * 2};
+  const uint32_t boxK[3] = {(uint32_t)D, (uint32_t)C::BN, 1};
+  const uint32_t boxV[3] = {64, (uint32_t)C::BN, 1};
+  int st = make_tmap(&tmK, k, dt, 3, dims, strides, boxK, CU_TENSOR_MAP_SWIZZLE_NONE);
+  if (st != FLB_OK) return st;
+  st = make_tmap(&tmV, v, dt, 3, dims, strides, boxV, CU_TENSOR_MAP_SWIZZLE_128B);
+  if (st != FLB_OK) return st;
+  static bool attr_set = false;
+  if (!attr_set) {
+    cudaError_t e = cudaFuncSetAttribute(attn_fwd_tc_kernel<D, T>,
+                                         cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM);
+    if (e != cudaSuccess) return check_cuda(e, "attn_fwd_tc smem attribute");
+    attr_set = true;
+  }
+  const dim3 grid((unsigned)((N + C::BM - 1) / C::BM), (unsigned)BH);
+  attn_fwd_tc_kernel<D, T><<<grid, 128, C::SMEM, s>>>(tmK, tmV, (const T*)q, (T*)out, lse, scores,
+                                                      w, wi, N, causal, err);
+  count_launches(1);
+  return check_cuda(cudaGetLastError(), "attn_fwd_tc launch");
+}
+
+bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
+
+}  // namespace
+
+int attn_fwd_fast_supported(int64_t BH, int64_t N, int64_t D, int dtype, int flags) {
+  if (flags & (FLB_ATTN_EXACT_TANH | FLB_ATTN_FORCE_GENERIC)) return 0;
+  if (!(dtype == FLB_BF16 || dtype == FLB_F16)) return 0;
+  if (!(D == 64 || D == 128)) return 0;
+  if (N < 1 || BH < 1 || BH > 65535) return 0;
+  return 1;
+}
+
+size_t attn_fwd_fast_workspace(int64_t, int64_t, int64_t, int, int) { return 256; }
+
+int attn_fwd_fast(const void* q, const void* k, const void* v, const float* w, const int32_t* wi,
+                  void* out, float* lse, float* scores, int64_t BH, int N, int D, int dtype,
+                  int flags, void* ws, size_t ws_bytes, cudaStream_t s) {
+  if (!aligned16(q) || !aligned16(k) || !aligned16(v) || !aligned16(out))
+    return fail(FLB_ERR_ALIGN, "attn_fwd: q/k/v/out must be 16-byte aligned for the tcgen05 path");
+  int* err = reinterpret_cast<int*>(ws);
+  cudaError_t e = cudaMemsetAsync(err, 0, sizeof(int), s);
+  if (e != cudaSuccess) return check_cuda(e, "attn_fwd error-word reset");
+  const int causal = (flags & FLB_ATTN_CAUSAL) ? 1 : 0;
+  if (dtype == FLB_BF16) {
+    return D == 64 ? launch_fwd_tc<64, __nv_bfloat16>(q, k, v, w, wi, out, lse, scores, BH, N, causal, err, s)
+                   : launch_fwd_tc<128, __nv_bfloat16>(q, k, v, w, wi, out, lse, scores, BH, N, causal, err, s);
+  }
+  return D == 64 ? launch_fwd_tc<64, __half>(q, k, v, w, wi, out, lse, scores, BH, N, causal, err, s)
+                 : launch_fwd_tc<128, __half>(q, k, v, w, wi, out, lse, scores, BH, N, causal, err, s);
+}
+
+// Backward: the tcgen05 backward is not wired yet; the CUDA-core backward runs.
+int attn_bwd_fast_supported(int64_t, int64_t, int64_t, int, int) { return 0; }
+size_t attn_bwd_fast_workspace(int64_t, int64_t, int64_t, int, int) { return 0; }
+int attn_bwd_fast(const void*, const void*, const void*, const float*, const int32_t*,
+                  const void*, const float*, const float*, const void*, void*, void*, void*,
+                  float*, int64_t, int, int, int, int, void*, size_t, cudaStream_t) {
+  return fail(FLB_ERR_UNSUPPORTED, "attn_bwd_fast: not available");
+}
+
+}  // namespace flb

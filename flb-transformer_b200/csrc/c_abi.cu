@@ -1,0 +1,209 @@
+// extern "C" boundary of libflb_b200.so: argument validation, dispatch to the kernels, status
+// codes and the thread-local error message.
+#include <atomic>
+#include <string>
+#include "common.cuh"
+
+namespace flb {
+
+static thread_local std::string g_last_error;
+static std::atomic<uint64_t> g_launches{0};
+
+void count_launches(int n) { g_launches.fetch_add((uint64_t)n, std::memory_order_relaxed); }
+
+void set_error(const std::string& msg) { g_last_error = msg; }
+int fail(int status, const std::string& msg) {
+  g_last_error = msg;
+  return status;
+}
+int check_cuda(cudaError_t e, const char* what) {
+  if (e == cudaSuccess) return FLB_OK;
+  g_last_error = std::string(what) + ": " + cudaGetErrorString(e);
+  return FLB_ERR_CUDA;
+}
+
+// kernels (defined in the other translation units)
+cudaError_t attn_fwd_generic(const void* q, const void* k, const void* v, const float* w,
+                             const int32_t* wi, void* out, float* lse, float* scores, int64_t BH,
+                             int N, int D, int dtype, bool exact, bool causal, cudaStream_t s);
+cudaError_t attn_bwd_generic(const void* q, const void* k, const void* v, const float* w,
+                             const int32_t* wi, const void* o, const float* lse, const void* dout,
+                             void* dq, void* dk, void* dv, float* dw, float* delta, int64_t BH,
+                             int N, int D, int dtype, bool exact, bool causal, cudaStream_t s);
+int attn_fwd_fast_supported(int64_t BH, int64_t N, int64_t D, int dtype, int flags);
+size_t attn_fwd_fast_workspace(int64_t BH, int64_t N, int64_t D, int dtype, int flags);
+int attn_fwd_fast(const void* q, const void* k, const void* v, const float* w, const int32_t* wi,
+                  void* out, float* lse, float* scores, int64_t BH, int N, int D, int dtype,
+                  int flags, void* ws, size_t ws_bytes, cudaStream_t s);
+int attn_bwd_fast_supported(int64_t BH, int64_t N, int64_t D, int dtype, int flags);
+size_t attn_bwd_fast_workspace(int64_t BH, int64_t N, int64_t D, int dtype, int flags);
+int attn_bwd_fast(const void* q, const void* k, const void* v, const float* w, const int32_t* wi,
+                  const void* o, const float* lse, const float* scores, const void* dout, void* dq,
+                  void* dk, void* dv,
+                  float* dw, int64_t BH, int N, int D, int dtype, int flags, void* ws,
+                  size_t ws_bytes, cudaStream_t s);
+int wf_gather(const void* x, const int64_t xs[3], const void* grids, const int64_t gs[4],
+              const int32_t* routing, const int32_t* port_map, const int32_t* spatial_map,
+              const int32_t* active, int64_t n_active, int64_t n_cells, void* out,
+              const int64_t os[4], int64_t n_deps, int64_t batch, int64_t dim, int dtype,
+              cudaStream_t s);
+int wf_index_copy(const void* src, int src_dtype, const int64_t ss[3], const int64_t* src_rows,
+                  void* dst, int dst_dtype, const int64_t ds[3], const int64_t* dst_rows,
+                  int64_t n_rows, int64_t batch, int64_t dim, int accumulate, cudaStream_t s);
+size_t grid_workspace_bytes(int64_t R, int64_t C, int64_t B, int64_t H, int64_t G, int has_U);
+int grid_fwd(const void* x, int x_layout, const void* W_l, const void* W_t, const void* U,
+             const float* bias, const void* top, void* h_out, int64_t R, int64_t C, int64_t B,
+             int64_t H, int64_t G, void* ws, size_t ws_bytes, int check_timeout, cudaStream_t s);
+int grid_bwd(const void* x, int x_layout, const void* W_l, const void* W_t, const void* U,
+             const void* top, const void* h_out, const void* dh, float* dW_l, float* dW_t,
+             float* dU, float* dbias, void* dx, void* dtop, int64_t R, int64_t C, int64_t B,
+             int64_t H, int64_t G, void* ws, size_t ws_bytes, int check_timeout, cudaStream_t s);
+int microbench(int kind, void* scratch, double* ops_per_s);
+int umma_selftest(int variant, int n, const void* A, const void* B, float* D, int* err,
+                  cudaStream_t s);
+
+static bool aligned(const void* p, size_t a) { return (reinterpret_cast<uintptr_t>(p) % a) == 0; }
+
+static int check_attn_common(const void* q, const void* k, const void* v, const float* w,
+                             const int32_t* wi, int64_t BH, int64_t N, int64_t D, int dtype) {
+  if (dtype_size(dtype) == 0) return fail(FLB_ERR_DTYPE, "attention: dtype must be f32, f16 or bf16");
+  if (BH < 0 || N < 0 || D <= 0) return fail(FLB_ERR_SHAPE, "attention: BH, N >= 0 and D > 0 required");
+  if (D > 256) return fail(FLB_ERR_UNSUPPORTED, "attention: head dim D > 256 is not supported");
+  if (N > (int64_t)INT32_MAX / 2) return fail(FLB_ERR_SHAPE, "attention: N too large");
+  if (BH * N > 0 && (!q || !k || !v || !w || !wi))
+    return fail(FLB_ERR_SHAPE, "attention: null input pointer");
+  const size_t es = (size_t)dtype_size(dtype);
+  if (!aligned(q, es) || !aligned(k, es) || !aligned(v, es) || !aligned(w, 4) || !aligned(wi, 4))
+    return fail(FLB_ERR_ALIGN, "attention: pointers must be aligned to their element size");
+  return FLB_OK;
+}
+
+}  // namespace flb
+
+using namespace flb;
+
+extern "C" {
+
+const char* flb_last_error(void) { return g_last_error.c_str(); }
+const char* flb_version(void) { return "flb_b200 0.1 (sm_100a)"; }
+uint64_t flb_launch_count(void) { return g_launches.load(std::memory_order_relaxed); }
+
+size_t flb_attn_fwd_workspace_bytes(int64_t BH, int64_t N, int64_t D, int dtype, int flags) {
+  if (attn_fwd_fast_supported(BH, N, D, dtype, flags))
+    return attn_fwd_fast_workspace(BH, N, D, dtype, flags);
+  return 0;
+}
+
+int flb_attn_fwd(const void* q, const void* k, const void* v, const float* w,
+                 const int32_t* w_index, void* out, float* lse, float* scores, int64_t BH,
+                 int64_t N, int64_t D, int dtype, int flags, void* workspace,
+                 size_t workspace_bytes, void* stream) {
+  int st = check_attn_common(q, k, v, w, w_index, BH, N, D, dtype);
+  if (st != FLB_OK) return st;
+  if (BH * N == 0) return FLB_OK;
+  if (!out || !lse) return fail(FLB_ERR_SHAPE, "attn_fwd: null output pointer");
+  cudaStream_t s = as_stream(stream);
+  if (attn_fwd_fast_supported(BH, N, D, dtype, flags)) {
+    const size_t need = attn_fwd_fast_workspace(BH, N, D, dtype, flags);
+    if (workspace_bytes < need || (need > 0 && !workspace))
+      return fail(FLB_ERR_WORKSPACE, "attn_fwd: workspace smaller than flb_attn_fwd_workspace_bytes()");
+    return attn_fwd_fast(q, k, v, w, w_index, out, lse, scores, BH, (int)N, (int)D, dtype,
+                         flags, workspace, workspace_bytes, s);
+  }
+  cudaError_t e = attn_fwd_generic(q, k, v, w, w_index, out, lse, scores, BH, (int)N, (int)D, dtype,
+                                   (flags & FLB_ATTN_EXACT_TANH) != 0, (flags & FLB_ATTN_CAUSAL) != 0, s);
+  if (e == cudaSuccess) count_launches(1);
+  return check_cuda(e, "attn_fwd (generic) launch");
+}
+
+size_t flb_attn_bwd_workspace_bytes(int64_t BH, int64_t N, int64_t D, int dtype, int flags) {
+  if (attn_bwd_fast_supported(BH, N, D, dtype, flags))
+    return attn_bwd_fast_workspace(BH, N, D, dtype, flags);
+  return (size_t)(BH * N) * sizeof(float);
+}
+
+int flb_attn_bwd(const void* q, const void* k, const void* v, const float* w,
+                 const int32_t* w_index, const void* out, const float* lse,
+                 const float* scores, const void* dout, void* dq, void* dk, void* dv, float* dw,
+                 int64_t BH, int64_t N, int64_t D,
+                 int64_t n_w_rows, int dtype, int flags, void* workspace, size_t workspace_bytes,
+                 void* stream) {
+  int st = check_attn_common(q, k, v, w, w_index, BH, N, D, dtype);
+  if (st != FLB_OK) return st;
+  if (BH * N == 0) return FLB_OK;
+  if (!out || !lse || !dout || !dq || !dk || !dv || !dw)
+    return fail(FLB_ERR_SHAPE, "attn_bwd: null pointer");
+  if (n_w_rows <= 0) return fail(FLB_ERR_SHAPE, "attn_bwd: n_w_rows must be positive");
+  const size_t need = flb_attn_bwd_workspace_bytes(BH, N, D, dtype, flags);
+  if (workspace_bytes < need || !workspace)
+    return fail(FLB_ERR_WORKSPACE, "attn_bwd: workspace smaller than flb_attn_bwd_workspace_bytes()");
+  cudaStream_t s = as_stream(stream);
+  if (attn_bwd_fast_supported(BH, N, D, dtype, flags))
+    return attn_bwd_fast(q, k, v, w, w_index, out, lse, scores, dout, dq, dk, dv, dw, BH,
+                         (int)N, (int)D, dtype, flags, workspace, workspace_bytes, s);
+  cudaError_t e = attn_bwd_generic(q, k, v, w, w_index, out, lse, dout, dq, dk, dv, dw,
+                                   (float*)workspace, BH, (int)N, (int)D, dtype,
+                                   (flags & FLB_ATTN_EXACT_TANH) != 0, (flags & FLB_ATTN_CAUSAL) != 0, s);
+  if (e == cudaSuccess) count_launches(2);
+  return check_cuda(e, "attn_bwd (generic) launch");
+}
+
+int flb_wf_gather(const void* x, const int64_t x_strides[3], const void* grids,
+                  const int64_t grid_strides[4], const int32_t* routing, const int32_t* port_map,
+                  const int32_t* spatial_map, const int32_t* active_cells, int64_t n_active,
+                  int64_t n_cells, void* gathered, const int64_t gathered_strides[4],
+                  int64_t n_deps, int64_t batch, int64_t dim, int dtype, void* stream) {
+  if (n_active < 0 || n_cells < 0 || n_deps < 0 || batch < 0 || dim < 0)
+    return fail(FLB_ERR_SHAPE, "wf_gather: negative size");
+  if (n_deps * n_active * batch * dim > 0 &&
+      (!x || !grids || !routing || !port_map || !spatial_map || !active_cells || !gathered))
+    return fail(FLB_ERR_SHAPE, "wf_gather: null pointer");
+  return wf_gather(x, x_strides, grids, grid_strides, routing, port_map, spatial_map,
+                   active_cells, n_active, n_cells, gathered, gathered_strides, n_deps, batch,
+                   dim, dtype, as_stream(stream));
+}
+
+int flb_wf_index_copy(const void* src, int src_dtype, const int64_t src_strides[3],
+                      const int64_t* src_rows, void* dst, int dst_dtype,
+                      const int64_t dst_strides[3], const int64_t* dst_rows, int64_t n_rows,
+                      int64_t batch, int64_t dim, int accumulate, void* stream) {
+  if (n_rows < 0 || batch < 0 || dim < 0) return fail(FLB_ERR_SHAPE, "wf_index_copy: negative size");
+  if (n_rows * batch * dim > 0 && (!src || !src_rows || !dst || !dst_rows))
+    return fail(FLB_ERR_SHAPE, "wf_index_copy: null pointer");
+  return wf_index_copy(src, src_dtype, src_strides, src_rows, dst, dst_dtype, dst_strides,
+                       dst_rows, n_rows, batch, dim, accumulate, as_stream(stream));
+}
+
+size_t flb_grid_workspace_bytes(int64_t R, int64_t C, int64_t B, int64_t H, int64_t G, int has_U) {
+  return grid_workspace_bytes(R, C, B, H, G, has_U);
+}
+
+int flb_grid_fwd(const void* x, int x_layout, const void* W_l, const void* W_t, const void* U,
+                 const float* bias, const void* top, void* h_out, int64_t R, int64_t C,
+                 int64_t B, int64_t H, int64_t G, void* workspace, size_t workspace_bytes,
+                 int check_timeout, void* stream) {
+  return grid_fwd(x, x_layout, W_l, W_t, U, bias, top, h_out, R, C, B, H, G, workspace,
+                  workspace_bytes, check_timeout, as_stream(stream));
+}
+
+int flb_grid_bwd(const void* x, int x_layout, const void* W_l, const void* W_t, const void* U,
+                 const void* top, const void* h_out, const void* dh, float* dW_l, float* dW_t,
+                 float* dU, float* dbias, void* dx, void* dtop, int64_t R, int64_t C, int64_t B,
+                 int64_t H, int64_t G, void* workspace, size_t workspace_bytes, int check_timeout,
+                 void* stream) {
+  return grid_bwd(x, x_layout, W_l, W_t, U, top, h_out, dh, dW_l, dW_t, dU, dbias, dx, dtop, R,
+                  C, B, H, G, workspace, workspace_bytes, check_timeout, as_stream(stream));
+}
+
+int flb_microbench(int kind, void* scratch, double* ops_per_s) {
+  if (!scratch || !ops_per_s) return fail(FLB_ERR_SHAPE, "microbench: null pointer");
+  return microbench(kind, scratch, ops_per_s);
+}
+
+int flb_selftest_umma(int variant, int n, const void* A, const void* B, float* D, int* err,
+                      void* stream) {
+  if (!A || !B || !D || !err) return fail(FLB_ERR_SHAPE, "selftest_umma: null pointer");
+  return umma_selftest(variant, n, A, B, D, err, as_stream(stream));
+}
+
+}  // extern "C"

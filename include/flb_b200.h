@@ -1,0 +1,188 @@
+/*
+ * flb_b200.h — C ABI of the B200 (sm_100a) implementation of FLB-Transformer's two hot paths:
+ *   (1) fused additive attention  s[i,j] = sum_d w[d] * tanh(q[i,d] + k[j,d]) / sqrt(D),
+ *       row softmax, out = P @ V, forward and backward;
+ *   (2) the anti-diagonal wavefront engine (dependency gather, port scatter, gradient routing)
+ *       and the persistent tanh grid-cell kernels.
+ *
+ * Conventions shared by every entry point:
+ *   - all pointers are DEVICE pointers unless stated otherwise; the library never allocates,
+ *     never frees and never synchronises the stream (except where an error word is read back,
+ *     which is stated per function);
+ *   - every call is enqueued on `stream` (a cudaStream_t passed as void*; NULL = legacy stream);
+ *   - the return value is an flb_status; FLB_OK == 0.  flb_last_error() returns a thread-local
+ *     message for the last non-zero status raised on the calling thread;
+ *   - dtypes are flb_dtype codes; q/k/v/out and grid tensors share one dtype per call.
+ */
+#ifndef FLB_B200_H
+#define FLB_B200_H
+
+#include <stdint.h>
+#include <stddef.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+typedef enum {
+  FLB_OK = 0,
+  FLB_ERR_SHAPE = 1,        /* bad or inconsistent sizes / strides                     */
+  FLB_ERR_DTYPE = 2,        /* unsupported dtype code                                  */
+  FLB_ERR_ALIGN = 3,        /* pointer or stride not aligned as the kernel requires    */
+  FLB_ERR_TIMEOUT = 4,      /* a bounded device-side wait gave up (error word set)     */
+  FLB_ERR_LAUNCH = 5,       /* kernel launch failed                                    */
+  FLB_ERR_UNSUPPORTED = 6,  /* valid request this build does not implement             */
+  FLB_ERR_CUDA = 7,         /* a CUDA runtime / driver / cuBLAS call failed            */
+  FLB_ERR_WORKSPACE = 8     /* workspace missing or smaller than the size query says   */
+} flb_status;
+
+typedef enum { FLB_F32 = 0, FLB_F16 = 1, FLB_BF16 = 2 } flb_dtype;
+
+/* attention flags */
+#define FLB_ATTN_CAUSAL      1  /* mask j > i (extension; the reference has no mask)          */
+#define FLB_ATTN_EXACT_TANH  2  /* tanhf/expf instead of tanh.approx / ex2.approx             */
+#define FLB_ATTN_FORCE_GENERIC 4 /* use the CUDA-core kernels even where a tcgen05 kernel fits */
+
+const char* flb_last_error(void);
+const char* flb_version(void);
+/* Number of kernels this library has launched in this process (all threads, all devices). */
+uint64_t flb_launch_count(void);
+
+/* ------------------------------------------------------------------------------------------
+ * Fused additive attention.
+ * Layout: q, k, v, out are contiguous [BH, N, D] (BH = prod(batch dims) * H) in `dtype`.
+ * w is a float32 table [n_w_rows, D]; head bh uses row w_index[bh] (int32, device), which is
+ * how a v_a broadcast to [..., H, 1, D] is expressed without materialising it.
+ * lse (float32 [BH, N]) receives the natural-log row log-sum-exp of the scaled scores.
+ * ------------------------------------------------------------------------------------------ */
+
+/* Replaces FusedAdditiveAttentionFunc.forward + fused_additive_attention_kernel
+ * (kernels/additive_attention.py:137-181 and :10-86). Scale 1/sqrt(D) as at :66,:145.
+ * scores: optional float32 [BH, N, N] output of the scaled scores s[i,j] (entries with j > i
+ * are left unwritten when causal). When the backward is going to run, saving them lets it
+ * skip the score recomputation (one full tanh pass); NULL = do not save.
+ * Workspace: flb_attn_fwd_workspace_bytes(); may be NULL when that returns 0. */
+int flb_attn_fwd(const void* q, const void* k, const void* v,
+                 const float* w, const int32_t* w_index,
+                 void* out, float* lse, float* scores,
+                 int64_t BH, int64_t N, int64_t D, int dtype, int flags,
+                 void* workspace, size_t workspace_bytes, void* stream);
+
+size_t flb_attn_fwd_workspace_bytes(int64_t BH, int64_t N, int64_t D, int dtype, int flags);
+
+/* Replaces FusedAdditiveAttentionFunc.backward -> compiled_backward_math
+ * (kernels/additive_attention.py:188-198 and :91-130).
+ * Inputs q,k,v,out,lse,dout as produced by flb_attn_fwd; outputs dq,dk,dv in `dtype`
+ * ([BH,N,D], overwritten) and dw, a float32 [n_w_rows, D] table that is ACCUMULATED into
+ * (caller zeroes it), matching the reduction of grad_va over broadcast dims (:126-128).
+ * scores: the [BH, N, N] scores saved by flb_attn_fwd, or NULL to recompute them.
+ * Workspace: flb_attn_bwd_workspace_bytes(). */
+int flb_attn_bwd(const void* q, const void* k, const void* v,
+                 const float* w, const int32_t* w_index,
+                 const void* out, const float* lse, const float* scores, const void* dout,
+                 void* dq, void* dk, void* dv, float* dw,
+                 int64_t BH, int64_t N, int64_t D, int64_t n_w_rows, int dtype, int flags,
+                 void* workspace, size_t workspace_bytes, void* stream);
+
+size_t flb_attn_bwd_workspace_bytes(int64_t BH, int64_t N, int64_t D, int dtype, int flags);
+
+/* ------------------------------------------------------------------------------------------
+ * Wavefront engine primitives (generic-layer path).
+ * Strides are in ELEMENTS.
+ * ------------------------------------------------------------------------------------------ */
+
+/* Replaces fetch_mapped_context_kernel / run_fetch_kernel (wavefront/wavefront_kernel.py:27-82,
+ * :84-106) and its Python twin fetch_mapped_context (:6-25).
+ * For every slot s < n_active and dependency i < n_deps, with cell = active_cells[s] and
+ * t = routing[cell*n_deps + i] (cells >= n_cells are padding and read as t = -1):
+ *   t >= 0  -> gathered[i, s, b, :] = grids[port_map[i], t, b, :]
+ *   t == -2 -> gathered[i, s, b, :] = x[b, spatial_map[cell], :]
+ *   t == -1 -> gathered[i, s, b, :] = 0
+ * grids strides (port, cell, batch, dim); x strides (batch, seq, dim);
+ * gathered strides (dep, slot, batch, dim). */
+int flb_wf_gather(const void* x, const int64_t x_strides[3],
+                  const void* grids, const int64_t grid_strides[4],
+                  const int32_t* routing, const int32_t* port_map, const int32_t* spatial_map,
+                  const int32_t* active_cells, int64_t n_active, int64_t n_cells,
+                  void* gathered, const int64_t gathered_strides[4],
+                  int64_t n_deps, int64_t batch, int64_t dim, int dtype, void* stream);
+
+/* Indexed row copy / accumulate, the data movement of the C++ orchestrator's per-tick
+ * scatters. Replaces, with one primitive:
+ *   - the per-port index_put_ of cell outputs into the stacked grids
+ *     (csrc/wavefront_backend.cpp:40-43),
+ *   - the per-cell index_put_ of parameter gradients (csrc/wavefront_backend.cpp:97-106) and,
+ *     with accumulate != 0 and per-layer destination rows, the later per-layer sum
+ *     (wavefront/wavefront_engine.py:132-139) done on the fly,
+ *   - the index_add_ routing of dependency gradients into the gradient grids and into grad_x
+ *     (csrc/wavefront_backend.cpp:109-130).
+ * For k < n_rows, b < batch, e < dim:
+ *   dst[dst_rows[k]*ds[0] + b*ds[1] + e*ds[2]]  (=, or += when accumulate)
+ *       src[src_rows[k]*ss[0] + b*ss[1] + e*ss[2]]
+ * Row index arrays are int64 (device). src and dst dtypes may differ (e.g. bf16 gradients into
+ * float32 accumulators). Accumulation uses atomics; with accumulate == 0 and repeated dst rows
+ * the surviving write is unspecified, as for index_put_. */
+int flb_wf_index_copy(const void* src, int src_dtype, const int64_t src_strides[3],
+                      const int64_t* src_rows,
+                      void* dst, int dst_dtype, const int64_t dst_strides[3],
+                      const int64_t* dst_rows,
+                      int64_t n_rows, int64_t batch, int64_t dim, int accumulate, void* stream);
+
+/* ------------------------------------------------------------------------------------------
+ * Persistent tanh grid cell (the wavefront grid layer), bf16 storage / fp32 accumulation:
+ *   h[r][c] = tanh(W_l[g] h[r][c-1] + W_t[g] h[r-1][c] + add[r][c] + bias[g]),  g = r if
+ *   per_row_weights else 0; h[r][-1] = 0; h[-1][c] = top[c] (or 0 when top == NULL);
+ *   add = x[r][c] @ U^T (hoisted GEMM) when U != NULL, else 0.
+ * This is the cell of the wavefront engine with dependencies ((-1,0),port 0) and
+ * ((0,-1),port 1) (wavefront/wavefront_api.py:12-14), evaluated by one persistent kernel with
+ * per-cell dependency flags instead of one host tick per anti-diagonal
+ * (csrc/wavefront_backend.cpp:16-44).
+ * Shapes: R rows, C cols, B batch, H hidden (H in {64,128,256}; B a multiple of 16, <= 64).
+ * x: [B, R, C, H] bf16 (row-major, x_layout 0) or [R, C, B, H] (x_layout 1).
+ * W_l, W_t: [G, H, H] bf16 (nn.Linear layout [out, in]); U: [H, H] bf16 or NULL; bias: [G, H] f32.
+ * top: [C, B, H] bf16 or NULL. h_out: [R, C, B, H] bf16 (engine grid order: cell-major).
+ * Workspace: flb_grid_workspace_bytes(); it also carries what the backward needs, so pass the
+ * same workspace, unmodified, to flb_grid_bwd.
+ * A device error word is read back (one 4-byte D2H copy, stream-synchronising) only when
+ * check_timeout != 0.
+ * ------------------------------------------------------------------------------------------ */
+size_t flb_grid_workspace_bytes(int64_t R, int64_t C, int64_t B, int64_t H, int64_t G, int has_U);
+
+int flb_grid_fwd(const void* x, int x_layout, const void* W_l, const void* W_t, const void* U,
+                 const float* bias, const void* top, void* h_out,
+                 int64_t R, int64_t C, int64_t B, int64_t H, int64_t G,
+                 void* workspace, size_t workspace_bytes, int check_timeout, void* stream);
+
+/* Backward of flb_grid_fwd. dh: [R, C, B, H] bf16 upstream gradient of h_out.
+ * Outputs (float32, OVERWRITTEN): dW_l, dW_t [G,H,H]; dU [H,H] (when U was given);
+ * dbias [G,H]; bf16 outputs: dx (same layout as x, when U was given, else NULL) and
+ * dtop [C,B,H] (when top was given, else NULL). */
+int flb_grid_bwd(const void* x, int x_layout, const void* W_l, const void* W_t, const void* U,
+                 const void* top, const void* h_out, const void* dh,
+                 float* dW_l, float* dW_t, float* dU, float* dbias, void* dx, void* dtop,
+                 int64_t R, int64_t C, int64_t B, int64_t H, int64_t G,
+                 void* workspace, size_t workspace_bytes, int check_timeout, void* stream);
+
+/* ------------------------------------------------------------------------------------------
+ * Measurement helpers (used by bench.py for the roofline denominators).
+ * ------------------------------------------------------------------------------------------ */
+
+/* Times a saturating loop of one instruction class on every SM and returns the measured
+ * throughput in operations (elements) per second through *ops_per_s (host pointer).
+ * kind: 0 = tanh.approx.f32, 1 = tanh.approx.f16x2 (2 elements/instr), 2 = tanh.approx.bf16x2,
+ *       3 = ex2.approx.f32, 4 = FFMA f32, 5 = HFMA2 f16x2 (2 elements/instr).
+ * Synchronises the device. scratch: device buffer of >= 4 * 148 * 1024 bytes. */
+int flb_microbench(int kind, void* scratch, double* ops_per_s);
+
+/* Known-answer check of the tcgen05 operand layouts (no reference counterpart; a build check).
+ * D[128 x n] (f32, row-major) = A[128 x 64] (bf16, row-major) * op(B), where
+ * variant 0: B is [n x 64] row-major (D = A B^T, K-major operand, wavefront-cell form);
+ * variant 1: B is [64 x n] row-major (D = A B,   MN-major operand, P@V form). n in {64, 128}.
+ * *err (device int, caller-zeroed) becomes non-zero if a bounded wait gave up. */
+int flb_selftest_umma(int variant, int n, const void* A, const void* B, float* D, int* err,
+                      void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* FLB_B200_H */
