@@ -401,13 +401,426 @@ int attn_fwd_fast(const void* q, const void* k, const void* v, const float* w, c
                  : launch_fwd_tc<128, __half>(q, k, v, w, wi, out, lse, scores, BH, N, causal, err, s);
 }
 
-// Backward: the tcgen05 backward is not wired yet; the CUDA-core backward runs.
-int attn_bwd_fast_supported(int64_t, int64_t, int64_t, int, int) { return 0; }
-size_t attn_bwd_fast_workspace(int64_t, int64_t, int64_t, int, int) { return 0; }
-int attn_bwd_fast(const void*, const void*, const void*, const float*, const int32_t*,
-                  const void*, const float*, const float*, const void*, void*, void*, void*,
-                  float*, int64_t, int, int, int, int, void*, size_t, cudaStream_t) {
-  return fail(FLB_ERR_UNSUPPORTED, "attn_bwd_fast: not available");
+// =============================================================================================
+// Backward (bf16/fp16, D = 64), consuming the scores saved by the forward.
+//
+// One CTA per (128-key block, batch*head), 8 warps, looping over 128-query tiles (causal: only
+// tiles at or below the key block). Per query tile:
+//   1. dP = dO . V^T on the tensor core (A = dO tile, K-major; B = the CTA's V block, K-major;
+//      M = N = 128, K = 64) into TMEM columns [0, 128).
+//   2. Threads (TMEM lane = query row, warps 0-3 / 4-7 take the two 64-key halves) form
+//      P = exp(s - lse) from the saved scores and dS = P * (dP - Delta); P goes to shared memory
+//      as the MN-major A operand of step 3, dS (fp32) to a shared tile.
+//   3. dV += P^T . dO on the tensor core: P is read MN-major (M = keys), and the same swizzled dO
+//      tile serves as an MN-major B operand (N = d); accumulator in TMEM columns [128, 192).
+//   4. The tanh grid (the MUFU-bound part): warp w owns keys 16w..16w+15, lane l owns head dims
+//      2l, 2l+1. For every query row: t = tanh(q + k), u = dS t, g = dS - u t; dK and dw
+//      accumulate in registers over the whole key block, dQ over the warp's 16 keys and then
+//      into a shared fp32 tile with shared-memory atomics, flushed to a global fp32 accumulator
+//      once per tile (one red.add per element per CTA and tile).
+// A prep kernel computes Delta = rowsum(dO * O) and clears the dQ accumulator; a finish kernel
+// scales dQ by w' and casts it. dQ[i,d] = w'[d] sum_j dS (1 - t^2), dK[j,d] = w'[d] sum_i dS
+// (1 - t^2), dw[d] = sum dS t / sqrt(D), w' = w / sqrt(D) (kernels/additive_attention.py:91-130).
+// =============================================================================================
+
+namespace {
+
+struct BwdCfg {
+  static constexpr int D = 64, BM = 128, BN = 128;
+  static constexpr int TILE = BM * D * 2;                  // 16 KB (a q or dO tile, bf16/fp16)
+  static constexpr int OFF_V = 0;                          // V block [128 keys x 64] swizzled
+  static constexpr int OFF_DO = OFF_V + BN * D * 2;        // 2 stages, swizzled
+  static constexpr int OFF_Q = OFF_DO + 2 * TILE;          // 2 stages, plain rows
+  static constexpr int OFF_P = OFF_Q + 2 * TILE;           // 2 x 16 KB MN-major atoms
+  static constexpr int DS_LD = BN + 4;                     // fp32 row pitch of the dS tile
+  static constexpr int OFF_DS = OFF_P + BM * BN * 2;
+  static constexpr int OFF_DQ = OFF_DS + BM * DS_LD * 4;   // fp32 [128 x 64]
+  static constexpr int SMEM = OFF_DQ + BM * D * 4 + 1024;
+  static constexpr int TMEM_COLS = 256;                    // dP: [0,128), dV: [128,192)
+};
+
+template <typename T>
+__global__ void bwd_prep_kernel(const T* __restrict__ o, const T* __restrict__ dout,
+                                float* __restrict__ delta, float* __restrict__ dq_acc,
+                                int64_t rows) {
+  const int lane = threadIdx.x & 31;
+  const int64_t r = (int64_t)blockIdx.x * (blockDim.x / 32) + (threadIdx.x >> 5);
+  if (r >= rows) return;
+  using U = Unpack<T>;
+  const uint32_t* op = reinterpret_cast<const uint32_t*>(o + r * 64);
+  const uint32_t* dp = reinterpret_cast<const uint32_t*>(dout + r * 64);
+  float a0, a1, b0, b1;
+  U::run(op[lane], a0, a1);
+  U::run(dp[lane], b0, b1);
+  float s = warp_sum(a0 * b0 + a1 * b1);
+  if (lane == 0) delta[r] = s;
+  reinterpret_cast<float2*>(dq_acc + r * 64)[lane] = make_float2(0.f, 0.f);
+}
+
+template <typename T>
+__global__ void bwd_finish_kernel(const float* __restrict__ dq_acc, const float* __restrict__ w,
+                                  const int32_t* __restrict__ w_index, T* __restrict__ dq,
+                                  int N, int64_t rows) {
+  const int64_t idx = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;  // one float2 each
+  if (idx >= rows * 32) return;
+  const int64_t r = idx / 32;
+  const int d = (int)(idx % 32) * 2;
+  const int64_t bh = r / N;
+  const float* wr = w + (int64_t)w_index[bh] * 64;
+  const float2 a = reinterpret_cast<const float2*>(dq_acc)[idx];
+  float r0, r1;
+  reinterpret_cast<uint32_t*>(dq)[idx] =
+      Unpack<T>::pack(a.x * wr[d] * 0.125f, a.y * wr[d + 1] * 0.125f, r0, r1);
+}
+
+template <typename T>
+__global__ void __launch_bounds__(256, 1)
+attn_bwd_tc_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmDO,
+                   const __grid_constant__ CUtensorMap tmV, const T* __restrict__ k,
+                   const float* __restrict__ w, const int32_t* __restrict__ w_index,
+                   const float* __restrict__ lse, const float* __restrict__ delta,
+                   const float* __restrict__ scores, float* __restrict__ dq_acc,
+                   T* __restrict__ dk, T* __restrict__ dv, float* __restrict__ dw, int N,
+                   int causal, int* __restrict__ err) {
+  using namespace sm100;
+  using C = BwdCfg;
+  using U = Unpack<T>;
+  constexpr int D = C::D;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* sm = (uint8_t*)(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
+  __shared__ __align__(8) uint64_t full_bar[2];
+  __shared__ __align__(8) uint64_t dp_bar, dv_bar;
+  __shared__ uint32_t tmem_slot;
+
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int kb = blockIdx.x;  // ascending key blocks = most query tiles first
+  const int bh = blockIdx.y;
+  const int kb0 = kb * C::BN;
+  const int nqt = (N + C::BM - 1) / C::BM;
+  const int t_first = causal ? kb : 0;
+  const int ntiles = nqt - t_first;
+  const float inv_sqrt_d = 0.125f;
+  const float* wrow = w + (int64_t)w_index[bh] * D;
+
+  if (tid == 0) {
+    mbar_init(&full_bar[0], 1);
+    mbar_init(&full_bar[1], 1);
+    mbar_init(&dp_bar, 1);
+    mbar_init(&dv_bar, 1);
+    fence_mbar_init();
+  }
+  if (warp == 0) {
+    tmem_alloc(&tmem_slot, C::TMEM_COLS);
+    tmem_relinquish();
+  }
+  float* sDQ = reinterpret_cast<float*>(sm + C::OFF_DQ);
+  for (int i = tid; i < C::BM * D; i += 256) sDQ[i] = 0.f;
+  // this warp's 16 keys, this lane's two head dims, in registers
+  float kr[16][2];
+#pragma unroll
+  for (int j = 0; j < 16; ++j) {
+    const int key = kb0 + warp * 16 + j;
+    if (key < N) {
+      const uint32_t kv = reinterpret_cast<const uint32_t*>(k + ((int64_t)bh * N + key) * D)[lane];
+      U::run(kv, kr[j][0], kr[j][1]);
+    } else {
+      kr[j][0] = kr[j][1] = 0.f;
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = tmem_slot;
+
+  auto issue_tile = [&](int t) {  // t: 0-based tile counter
+    const int st = t & 1;
+    const int q0 = (t_first + t) * C::BM;
+    mbar_arrive_expect_tx(&full_bar[st], 2 * C::TILE);
+    tma_load_3d(sm + C::OFF_DO + st * C::TILE, &tmDO, &full_bar[st], 0, q0, bh);
+    tma_load_3d(sm + C::OFF_Q + st * C::TILE, &tmQ, &full_bar[st], 0, q0, bh);
+  };
+  const uint32_t idesc_dp = make_idesc_f16(128, 128, U::is_bf16, 0, 0);
+  const uint32_t idesc_dv = make_idesc_f16(128, 64, U::is_bf16, 1, 1);
+  auto issue_dp = [&](int t) {  // requires Q/dO tile t resident
+    const uint32_t a = smem_u32(sm + C::OFF_DO + (t & 1) * C::TILE);
+    const uint32_t b = smem_u32(sm + C::OFF_V);
+#pragma unroll
+    for (int kk = 0; kk < D / 16; ++kk)
+      umma_f16(tmem, make_smem_desc(a + kk * 32, 16, 1024, kSwizzle128B),
+               make_smem_desc(b + kk * 32, 16, 1024, kSwizzle128B), idesc_dp, kk > 0 ? 1u : 0u);
+    umma_commit(&dp_bar);
+  };
+
+  if (tid == 0) {
+    tma_prefetch_desc(&tmQ);
+    tma_prefetch_desc(&tmDO);
+    tma_prefetch_desc(&tmV);
+    // V block (K-major B operand of dP) and the first query tile share stage 0's barrier:
+    // exactly one arrive.expect_tx per barrier phase (the barrier's arrival count is 1)
+    mbar_arrive_expect_tx(&full_bar[0], C::BN * D * 2 + 2 * C::TILE);
+    tma_load_3d(sm + C::OFF_V, &tmV, &full_bar[0], 0, kb0, bh);
+    tma_load_3d(sm + C::OFF_DO, &tmDO, &full_bar[0], 0, t_first * C::BM, bh);
+    tma_load_3d(sm + C::OFF_Q, &tmQ, &full_bar[0], 0, t_first * C::BM, bh);
+    if (ntiles > 1) issue_tile(1);
+    if (!mbar_wait(&full_bar[0], 0, kWaitLimit)) atomicExch(err, 11);
+    tc_fence_after();
+    issue_dp(0);
+  }
+  __syncwarp();
+
+  float dka[16][2];
+#pragma unroll
+  for (int j = 0; j < 16; ++j) dka[j][0] = dka[j][1] = 0.f;
+  float dwa0 = 0.f, dwa1 = 0.f;
+  const int arow = 32 * (warp & 3) + lane;  // phase-A query row within the tile (TMEM lane)
+  const int ahalf = warp >> 2;              // phase-A key half
+  float* sDS = reinterpret_cast<float*>(sm + C::OFF_DS);
+
+  for (int t = 0; t < ntiles; ++t) {
+    const int q0 = (t_first + t) * C::BM;
+    const int st = t & 1;
+    // ---- phase A: P and dS from dP (TMEM) and the saved scores ------------------------------
+    // every thread observes the TMA barrier of this tile (phase B reads the Q tile)
+    if (!mbar_wait(&full_bar[st], (uint32_t)(t >> 1) & 1u, kWaitLimit)) atomicExch(err, 10);
+    if (!mbar_wait(&dp_bar, (uint32_t)t & 1u, kWaitLimit)) atomicExch(err, 12);
+    if (t >= 1 && !mbar_wait(&dv_bar, (uint32_t)(t - 1) & 1u, kWaitLimit)) atomicExch(err, 13);
+    tc_fence_after();
+    {
+      const int i = q0 + arow;
+      const bool row_ok = i < N;
+      const float lse2 = row_ok ? lse[(int64_t)bh * N + i] * kLog2e : 0.f;
+      const float dlt = row_ok ? delta[(int64_t)bh * N + i] : 0.f;
+      const float* srow = scores + ((int64_t)bh * N + (row_ok ? i : 0)) * N + kb0 + 64 * ahalf;
+      uint8_t* sP = sm + C::OFF_P + ahalf * (C::BM * 128);
+      float* dsrow = sDS + arow * C::DS_LD + 64 * ahalf;
+#pragma unroll
+      for (int cb = 0; cb < 2; ++cb) {
+        uint32_t r[32];
+        tmem_ld32(tmem + ((uint32_t)(32 * (warp & 3)) << 16) + 64 * ahalf + 32 * cb, r);
+        tmem_wait_ld();
+#pragma unroll
+        for (int g = 0; g < 4; ++g) {
+          float p[8], ds[8];
+#pragma unroll
+          for (int e = 0; e < 8; ++e) {
+            const int jj = 64 * ahalf + 32 * cb + 8 * g + e;
+            const int key = kb0 + jj;
+            const bool ok = row_ok && key < N && (!causal || key <= i);
+            const float sv = ok ? srow[32 * cb + 8 * g + e] : 0.f;
+            p[e] = ok ? ex2_approx(sv * kLog2e - lse2) : 0.f;
+          }
+          uint32_t pk[4];
+#pragma unroll
+          for (int e = 0; e < 4; ++e) {
+            float r0, r1;
+            pk[e] = U::pack(p[2 * e], p[2 * e + 1], r0, r1);
+            ds[2 * e] = r0 * (__uint_as_float(r[8 * g + 2 * e]) - dlt);
+            ds[2 * e + 1] = r1 * (__uint_as_float(r[8 * g + 2 * e + 1]) - dlt);
+          }
+          *reinterpret_cast<uint4*>(sP + sw128_offset(arow, 4 * cb + g)) =
+              make_uint4(pk[0], pk[1], pk[2], pk[3]);
+          reinterpret_cast<float4*>(dsrow + 32 * cb + 8 * g)[0] = make_float4(ds[0], ds[1], ds[2], ds[3]);
+          reinterpret_cast<float4*>(dsrow + 32 * cb + 8 * g)[1] = make_float4(ds[4], ds[5], ds[6], ds[7]);
+        }
+      }
+    }
+    fence_async_shared();
+    tc_fence_before();
+    __syncthreads();
+
+    // ---- one thread: dV += P^T dO, then dP for the next tile ---------------------------------
+    if (tid == 0) {
+      tc_fence_after();
+      const uint32_t pa = smem_u32(sm + C::OFF_P);
+      const uint32_t ob = smem_u32(sm + C::OFF_DO + st * C::TILE);
+#pragma unroll
+      for (int kk = 0; kk < C::BM / 16; ++kk)
+        umma_f16(tmem + 128, make_smem_desc(pa + kk * 2048, C::BM * 128, 1024, kSwizzle128B),
+                 make_smem_desc(ob + kk * 2048, C::BM * 128, 1024, kSwizzle128B), idesc_dv,
+                 (t > 0 || kk > 0) ? 1u : 0u);
+      umma_commit(&dv_bar);
+      if (t + 1 < ntiles) {
+        if (!mbar_wait(&full_bar[(t + 1) & 1], (uint32_t)((t + 1) >> 1) & 1u, kWaitLimit))
+          atomicExch(err, 14);
+        tc_fence_after();
+        issue_dp(t + 1);
+      }
+    }
+    __syncwarp();
+
+    // ---- phase B: the tanh grid ------------------------------------------------------------
+    {
+      const uint32_t* sQ = reinterpret_cast<const uint32_t*>(sm + C::OFF_Q + st * C::TILE);
+      const int key_lo = kb0 + warp * 16;
+      const int rmax = min(C::BM, N - q0);
+#pragma unroll 1
+      for (int r = 0; r < rmax; ++r) {
+        if (causal && key_lo > q0 + r) continue;  // every key of this warp is masked for row r
+        float q0f, q1f;
+        U::run(sQ[r * (D / 2) + lane], q0f, q1f);
+        const float4* dsr = reinterpret_cast<const float4*>(sDS + r * C::DS_LD + warp * 16);
+        float dsv[16];
+#pragma unroll
+        for (int c = 0; c < 4; ++c) {
+          const float4 v4 = dsr[c];
+          dsv[4 * c] = v4.x; dsv[4 * c + 1] = v4.y; dsv[4 * c + 2] = v4.z; dsv[4 * c + 3] = v4.w;
+        }
+        float dq0 = 0.f, dq1 = 0.f;
+#pragma unroll
+        for (int j = 0; j < 16; ++j) {
+          const float t0 = tanh_approx(q0f + kr[j][0]);
+          const float t1 = tanh_approx(q1f + kr[j][1]);
+          const float u0 = dsv[j] * t0, u1 = dsv[j] * t1;
+          const float g0 = fmaf(-u0, t0, dsv[j]), g1 = fmaf(-u1, t1, dsv[j]);
+          dq0 += g0;
+          dq1 += g1;
+          dka[j][0] += g0;
+          dka[j][1] += g1;
+          dwa0 += u0;
+          dwa1 += u1;
+        }
+        atomicAdd(&sDQ[r * D + 2 * lane], dq0);
+        atomicAdd(&sDQ[r * D + 2 * lane + 1], dq1);
+      }
+    }
+    __syncthreads();
+    // ---- flush dQ partials of this tile; refill the stage this tile used ----------------------
+    {
+      const int rows = min(C::BM, N - q0);
+      float* dst = dq_acc + ((int64_t)bh * N + q0) * D;
+      for (int e = tid; e < rows * D; e += 256) {
+        atomicAdd(dst + e, sDQ[e]);
+        sDQ[e] = 0.f;
+      }
+    }
+    if (tid == 0 && t + 2 < ntiles) {
+      // stage st: Q read by phase B (done: barrier above), dO read by dV MMA t
+      if (!mbar_wait(&dv_bar, (uint32_t)t & 1u, kWaitLimit)) atomicExch(err, 15);
+      fence_async_shared();
+      issue_tile(t + 2);
+    }
+    __syncthreads();
+  }
+
+  // ---- epilogue: dV from TMEM, dK and dw from registers ----------------------------------------
+  if (ntiles > 0 && !mbar_wait(&dv_bar, (uint32_t)(ntiles - 1) & 1u, kWaitLimit)) atomicExch(err, 16);
+  tc_fence_after();
+  if (warp < 4) {
+    const int key = kb0 + 32 * warp + lane;
+#pragma unroll
+    for (int cb = 0; cb < 2; ++cb) {
+      uint32_t r[32];
+      tmem_ld32(tmem + ((uint32_t)(32 * warp) << 16) + 128 + 32 * cb, r);
+      tmem_wait_ld();
+      if (key < N) {
+        T* dst = dv + ((int64_t)bh * N + key) * D + 32 * cb;
+#pragma unroll
+        for (int g = 0; g < 4; ++g) {
+          uint32_t pk[4];
+#pragma unroll
+          for (int e = 0; e < 4; ++e) {
+            float r0, r1;
+            const float a = ntiles > 0 ? __uint_as_float(r[8 * g + 2 * e]) : 0.f;
+            const float b2 = ntiles > 0 ? __uint_as_float(r[8 * g + 2 * e + 1]) : 0.f;
+            pk[e] = U::pack(a, b2, r0, r1);
+          }
+          reinterpret_cast<uint4*>(dst)[g] = make_uint4(pk[0], pk[1], pk[2], pk[3]);
+        }
+      }
+    }
+  }
+  {
+    const float w0 = wrow[2 * lane] * inv_sqrt_d, w1 = wrow[2 * lane + 1] * inv_sqrt_d;
+#pragma unroll
+    for (int j = 0; j < 16; ++j) {
+      const int key = kb0 + warp * 16 + j;
+      if (key < N) {
+        float r0, r1;
+        reinterpret_cast<uint32_t*>(dk + ((int64_t)bh * N + key) * D)[lane] =
+            U::pack(dka[j][0] * w0, dka[j][1] * w1, r0, r1);
+      }
+    }
+    float* dwr = dw + (int64_t)w_index[bh] * D;
+    atomicAdd(dwr + 2 * lane, dwa0 * inv_sqrt_d);
+    atomicAdd(dwr + 2 * lane + 1, dwa1 * inv_sqrt_d);
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 0) tmem_dealloc(tmem, C::TMEM_COLS);
+}
+
+template <typename T>
+int launch_bwd_tc(const void* q, const void* k, const void* v, const float* w, const int32_t* wi,
+                  const void* o, const float* lse, const float* scores, const void* dout, void* dq,
+                  void* dk, void* dv, float* dw, int64_t BH, int N, int causal, void* ws,
+                  cudaStream_t s) {
+  using C = BwdCfg;
+  const CUtensorMapDataType dt =
+      Unpack<T>::is_bf16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
+  const uint64_t dims[3] = {64, (uint64_t)N, (uint64_t)BH};
+  const uint64_t strides[2] = {128, (uint64_t)N * 128};
+  const uint32_t box[3] = {64, 128, 1};
+  CUtensorMap tmQ, tmDO, tmV;
+  int st = make_tmap(&tmQ, q, dt, 3, dims, strides, box, CU_TENSOR_MAP_SWIZZLE_NONE);
+  if (st == FLB_OK) st = make_tmap(&tmDO, dout, dt, 3, dims, strides, box, CU_TENSOR_MAP_SWIZZLE_128B);
+  if (st == FLB_OK) st = make_tmap(&tmV, v, dt, 3, dims, strides, box, CU_TENSOR_MAP_SWIZZLE_128B);
+  if (st != FLB_OK) return st;
+  uint8_t* wsb = reinterpret_cast<uint8_t*>(ws);
+  int* err = reinterpret_cast<int*>(wsb);
+  float* delta = reinterpret_cast<float*>(wsb + 256);
+  float* dq_acc = delta + ((BH * N + 63) / 64) * 64;
+  cudaError_t e = cudaMemsetAsync(err, 0, sizeof(int), s);
+  if (e != cudaSuccess) return check_cuda(e, "attn_bwd error-word reset");
+  const int64_t rows = BH * N;
+  bwd_prep_kernel<T><<<(unsigned)((rows + 7) / 8), 256, 0, s>>>((const T*)o, (const T*)dout, delta,
+                                                                dq_acc, rows);
+  static bool attr_set = false;
+  if (!attr_set) {
+    e = cudaFuncSetAttribute(attn_bwd_tc_kernel<T>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             C::SMEM);
+    if (e != cudaSuccess) return check_cuda(e, "attn_bwd_tc smem attribute");
+    attr_set = true;
+  }
+  const dim3 grid((unsigned)((N + C::BN - 1) / C::BN), (unsigned)BH);
+  attn_bwd_tc_kernel<T><<<grid, 256, C::SMEM, s>>>(tmQ, tmDO, tmV, (const T*)k, w, wi, lse, delta,
+                                                   scores, dq_acc, (T*)dk, (T*)dv, dw, N, causal, err);
+  bwd_finish_kernel<T><<<(unsigned)((rows * 32 + 255) / 256), 256, 0, s>>>(dq_acc, w, wi, (T*)dq, N,
+                                                                           rows);
+  count_launches(3);
+  return check_cuda(cudaGetLastError(), "attn_bwd_tc launch");
+}
+
+}  // namespace
+
+int attn_bwd_fast_supported(int64_t BH, int64_t N, int64_t D, int dtype, int flags) {
+  if (flags & (FLB_ATTN_EXACT_TANH | FLB_ATTN_FORCE_GENERIC)) return 0;
+  if (!(dtype == FLB_BF16 || dtype == FLB_F16)) return 0;
+  if (D != 64) return 0;
+  if (N < 1 || BH < 1 || BH > 65535) return 0;
+  return 1;
+}
+
+size_t attn_bwd_fast_workspace(int64_t BH, int64_t N, int64_t D, int, int) {
+  const size_t rows = (size_t)(BH * N);
+  return 256 + ((rows + 63) / 64) * 64 * sizeof(float) + rows * (size_t)D * sizeof(float);
+}
+
+int attn_bwd_fast(const void* q, const void* k, const void* v, const float* w, const int32_t* wi,
+                  const void* o, const float* lse, const float* scores, const void* dout, void* dq,
+                  void* dk, void* dv, float* dw, int64_t BH, int N, int D, int dtype, int flags,
+                  void* ws, size_t ws_bytes, cudaStream_t s) {
+  if (D != 64 || scores == nullptr) return fail(FLB_ERR_UNSUPPORTED, "attn_bwd_fast: needs D=64 and saved scores");
+  if (!aligned16(q) || !aligned16(k) || !aligned16(v) || !aligned16(dout) || !aligned16(o) ||
+      !aligned16(dq) || !aligned16(dk) || !aligned16(dv))
+    return fail(FLB_ERR_ALIGN, "attn_bwd: tensors must be 16-byte aligned for the tcgen05 path");
+  if (ws_bytes < attn_bwd_fast_workspace(BH, N, D, dtype, flags))
+    return fail(FLB_ERR_WORKSPACE, "attn_bwd: workspace too small");
+  const int causal = (flags & FLB_ATTN_CAUSAL) ? 1 : 0;
+  if (dtype == FLB_BF16)
+    return launch_bwd_tc<__nv_bfloat16>(q, k, v, w, wi, o, lse, scores, dout, dq, dk, dv, dw, BH, N,
+                                        causal, ws, s);
+  return launch_bwd_tc<__half>(q, k, v, w, wi, o, lse, scores, dout, dq, dk, dv, dw, BH, N, causal,
+                               ws, s);
 }
 
 }  // namespace flb

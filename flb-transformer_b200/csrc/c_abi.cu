@@ -117,9 +117,12 @@ int flb_attn_fwd(const void* q, const void* k, const void* v, const float* w,
 }
 
 size_t flb_attn_bwd_workspace_bytes(int64_t BH, int64_t N, int64_t D, int dtype, int flags) {
-  if (attn_bwd_fast_supported(BH, N, D, dtype, flags))
-    return attn_bwd_fast_workspace(BH, N, D, dtype, flags);
-  return (size_t)(BH * N) * sizeof(float);
+  const size_t generic = (size_t)(BH * N) * sizeof(float);
+  if (attn_bwd_fast_supported(BH, N, D, dtype, flags)) {
+    const size_t fast = attn_bwd_fast_workspace(BH, N, D, dtype, flags);
+    return fast > generic ? fast : generic;
+  }
+  return generic;
 }
 
 int flb_attn_bwd(const void* q, const void* k, const void* v, const float* w,
@@ -138,7 +141,7 @@ int flb_attn_bwd(const void* q, const void* k, const void* v, const float* w,
   if (workspace_bytes < need || !workspace)
     return fail(FLB_ERR_WORKSPACE, "attn_bwd: workspace smaller than flb_attn_bwd_workspace_bytes()");
   cudaStream_t s = as_stream(stream);
-  if (attn_bwd_fast_supported(BH, N, D, dtype, flags))
+  if (scores != nullptr && attn_bwd_fast_supported(BH, N, D, dtype, flags))
     return attn_bwd_fast(q, k, v, w, w_index, out, lse, scores, dout, dq, dk, dv, dw, BH,
                          (int)N, (int)D, dtype, flags, workspace, workspace_bytes, s);
   cudaError_t e = attn_bwd_generic(q, k, v, w, w_index, out, lse, dout, dq, dk, dv, dw,
