@@ -58,6 +58,10 @@ int grid_bwd(const void* x, int x_layout, const void* W_l, const void* W_t, cons
              const void* top, const void* h_out, const void* dh, float* dW_l, float* dW_t,
              float* dU, float* dbias, void* dx, void* dtop, int64_t R, int64_t C, int64_t B,
              int64_t H, int64_t G, void* ws, size_t ws_bytes, int check_timeout, cudaStream_t s);
+int grid_fwd_impl(const void* x, int x_layout, const void* W_l, const void* W_t, const void* U,
+                  const float* bias, const void* top, void* h_out, int64_t R, int64_t C,
+                  int64_t B, int64_t H, int64_t G, void* ws, size_t ws_bytes, int check_timeout,
+                  cudaStream_t s, int64_t drop_cell, uint32_t spin_limit);
 int microbench(int kind, void* scratch, double* ops_per_s);
 int umma_selftest(int variant, int n, const void* A, const void* B, float* D, int* err,
                   cudaStream_t s);
@@ -196,6 +200,18 @@ int flb_grid_bwd(const void* x, int x_layout, const void* W_l, const void* W_t, 
                  void* stream) {
   return grid_bwd(x, x_layout, W_l, W_t, U, top, h_out, dh, dW_l, dW_t, dU, dbias, dx, dtop, R,
                   C, B, H, G, workspace, workspace_bytes, check_timeout, as_stream(stream));
+}
+
+int flb_grid_fwd_drop_flag_test(const void* x, int x_layout, const void* W_l, const void* W_t,
+                                const void* U, const float* bias, const void* top, void* h_out,
+                                int64_t R, int64_t C, int64_t B, int64_t H, int64_t G,
+                                void* workspace, size_t workspace_bytes, int64_t drop_row,
+                                int64_t drop_col, uint32_t spin_limit, void* stream) {
+  if (drop_row < 0 || drop_row >= R || drop_col < 0 || drop_col >= C)
+    return fail(FLB_ERR_SHAPE, "grid drop-flag test: cell outside the grid");
+  return grid_fwd_impl(x, x_layout, W_l, W_t, U, bias, top, h_out, R, C, B, H, G, workspace,
+                       workspace_bytes, 1, as_stream(stream), drop_row * C + drop_col,
+                       spin_limit);
 }
 
 int flb_microbench(int kind, void* scratch, double* ops_per_s) {

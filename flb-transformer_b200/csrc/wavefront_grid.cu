@@ -1,11 +1,565 @@
-// placeholder: replaced by the persistent grid kernels
+// Persistent tanh grid cell: the wavefront grid layer as one kernel per direction.
+//
+//   h[r][c] = tanh(W_l[g] h[r][c-1] + W_t[g] h[r-1][c] + add[r][c] + bias[g]),   g = r or 0
+//
+// with h[r][-1] = 0, h[-1][c] = top[c] (or 0), add = x[r][c] U^T (one hoisted cuBLAS GEMM).
+// This is the cell of the wavefront engine with dependencies ((-1,0), port 0) and
+// ((0,-1), port 1) (wavefront/wavefront_api.py:12-14). The reference evaluates it with one host
+// tick per anti-diagonal (csrc/wavefront_backend.cpp:16-44: gather launch, vmapped cell, scatter);
+// here a single launch advances the whole grid:
+//   * one CTA per (grid row, 128 output features); rows are co-resident (grid <= the device's
+//     resident-CTA capacity) and a CTA walks its row left to right;
+//   * a cell starts when per-cell dependency flags in global memory say that both 128-feature
+//     halves of its left and top neighbours are stored (ld.acquire.gpu spin with an iteration
+//     bound; on expiry an error word is set and the kernel carries on, so it never hangs);
+//   * the neighbours' h ([batch x hidden] bf16 each) arrive by TMA straight from the output grid;
+//     coordinates outside the grid (c-1 < 0, r-1 < 0) are zero-filled by the TMA unit, which is
+//     exactly the zero boundary;
+//   * the cell GEMM, z^T[128 x B] = [W_l | W_t][128 x 2H] . [h_left ; h_top][2H x B], runs on
+//     tcgen05 with the CTA's weight slice resident in shared memory and the accumulator in TMEM;
+//   * the epilogue adds bias and the hoisted x U^T, applies tanh, stores h (bf16) into the output
+//     grid, fences, and releases the cell's flag.
+// The backward is the mirrored reverse sweep producing dz = dh_total * (1 - h^2) with
+// dh_total = dh_ext + W_l^T dz[r][c+1] + W_t^T dz[r+1][c]; weight gradients are then plain
+// cuBLAS GEMMs over dz and the saved h (and x), and db is reduced inside the sweep.
+#include <cublas_v2.h>
+
 #include "common.cuh"
+#include "sm100.cuh"
+#include "tma_host.cuh"
+
 namespace flb {
-size_t grid_workspace_bytes(int64_t, int64_t, int64_t, int64_t, int64_t, int) { return 0; }
-int grid_fwd(const void*, int, const void*, const void*, const void*, const float*, const void*, void*,
-             int64_t, int64_t, int64_t, int64_t, int64_t, void*, size_t, int, cudaStream_t) {
-  return fail(FLB_ERR_UNSUPPORTED, "grid_fwd: not built yet"); }
-int grid_bwd(const void*, int, const void*, const void*, const void*, const void*, const void*, const void*,
-             float*, float*, float*, float*, void*, void*, int64_t, int64_t, int64_t, int64_t, int64_t,
-             void*, size_t, int, cudaStream_t) { return fail(FLB_ERR_UNSUPPORTED, "grid_bwd: not built yet"); }
+
+namespace {
+
+constexpr uint32_t kWaitLimit = 1u << 22;      // mbarrier polls
+constexpr uint32_t kFlagSpinLimit = 1u << 26;  // flag polls (~ seconds with the backoff)
+
+__device__ __forceinline__ int ld_acquire(const int* p) {
+  int v;
+  asm volatile("ld.acquire.gpu.global.b32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  return v;
 }
+__device__ __forceinline__ void st_release(int* p, int v) {
+  asm volatile("st.release.gpu.global.b32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+// Bounded spin until *p == want. Returns false if it gave up.
+__device__ __forceinline__ bool wait_flag(const int* p, int want, uint32_t limit) {
+  for (uint32_t i = 0; i < limit; ++i) {
+    if (ld_acquire(p) == want) return true;
+    if (i > 64) __nanosleep(64);
+  }
+  return false;
+}
+
+__device__ __forceinline__ void tma_load_4d(void* dst, const void* tmap, uint64_t* bar, int c0,
+                                            int c1, int c2, int c3) {
+  asm volatile(
+      "cp.async.bulk.tensor.4d.shared::cluster.global.mbarrier::complete_tx::bytes"
+      " [%0], [%1, {%3, %4, %5, %6}], [%2];" ::"r"(sm100::smem_u32(dst)),
+      "l"(tmap), "r"(sm100::smem_u32(bar)), "r"(c0), "r"(c1), "r"(c2), "r"(c3)
+      : "memory");
+}
+
+template <int H>
+struct GridCfg {
+  static constexpr int KATOMS = 2 * H / 64;          // 64-element K atoms of [left | top]
+  static constexpr int W_ATOM = 128 * 128;            // bytes: 128 rows x 128 B
+  static constexpr int OFF_W = 0;
+  static constexpr int OFF_IN = KATOMS * W_ATOM;      // B operand atoms follow
+  static int smem(int B) { return OFF_IN + KATOMS * B * 128 + 1024; }
+};
+
+struct GridParams {
+  const float* add;      // hoisted x U^T (fp32) or null
+  int add_layout;        // 0: [B, R, C, H] rows, 1: [R, C, B, H] rows
+  const float* bias;     // [G, H] (forward) ; unused in backward
+  __nv_bfloat16* out;    // forward: h grid [R, C, B, H]; backward: dz grid [R, C, B, H]
+  __nv_bfloat16* out2;   // backward: dz in x layout [B, R, C, H] or null
+  const __nv_bfloat16* h;    // backward: forward output h [R, C, B, H]
+  const __nv_bfloat16* dh;   // backward: upstream gradient [R, C, B, H]
+  float* dbias;          // backward: [G, H] accumulated
+  int* flags;            // [R, C, 2]
+  int R, C, B, G, has_top, reverse;
+  int* err;
+  int64_t drop_cell;     // failure-detection check: this cell's flag is never released (-1: none)
+  uint32_t spin_limit;   // flag polls before a wait gives up
+};
+
+// One kernel body for both directions. Forward (reverse = 0): rows ascend, cells walk right,
+// inputs are h[r][c-1] (left) and h[r-1][c] (top). Backward (reverse = 1): rows descend, cells
+// walk left, inputs are dz[r][c+1] and dz[r+1][c], weights are the transposed W_l^T, W_t^T.
+template <int H>
+__global__ void __launch_bounds__(128, 1)
+grid_sweep_kernel(const __grid_constant__ CUtensorMap tmWa, const __grid_constant__ CUtensorMap tmWb,
+                  const __grid_constant__ CUtensorMap tmIn, const __grid_constant__ CUtensorMap tmTop,
+                  GridParams p) {
+  using namespace sm100;
+  using Cfg = GridCfg<H>;
+  constexpr int NH = H / 128;  // feature halves (CTAs per row)
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* sm = (uint8_t*)(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
+  __shared__ __align__(8) uint64_t bar_w, bar_in, bar_mma;
+  __shared__ uint32_t tmem_slot;
+
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int half = blockIdx.x % NH;
+  const int worker = blockIdx.x / NH;
+  const int nworkers = gridDim.x / NH;
+  const int B = p.B;
+  const int R = p.R, C = p.C;
+
+  if (tid == 0) {
+    mbar_init(&bar_w, 1);
+    mbar_init(&bar_in, 1);
+    mbar_init(&bar_mma, 1);
+    fence_mbar_init();
+    tma_prefetch_desc(&tmWa);
+    tma_prefetch_desc(&tmWb);
+    tma_prefetch_desc(&tmIn);
+    if (p.has_top) tma_prefetch_desc(&tmTop);
+  }
+  if (warp == 0) {
+    tmem_alloc(&tmem_slot, 64);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = tmem_slot;
+  const uint32_t idesc = make_idesc_f16(128, B, 1, 0, 0);
+  const int f = half * 128 + warp * 32 + lane;  // this thread's output feature
+  uint32_t n_wload = 0, n_cell = 0;
+  float db_acc = 0.f;
+  int db_group = -1;
+
+  for (int ri = worker; ri < R; ri += nworkers) {
+    const int r = p.reverse ? (R - 1 - ri) : ri;
+    const int g = (p.G > 1) ? r : 0;
+    // The other-row edge uses the weights of the row that consumes it: forward, cell (r, c)
+    // reads h[r-1][c] through its own W_t[r]; backward, dz[r+1][c] flows back through W_t[r+1].
+    const int g_other = (p.G > 1 && p.reverse) ? min(r + 1, R - 1) : g;
+    if (ri == worker || p.G > 1) {
+      if (tid == 0) {
+        mbar_arrive_expect_tx(&bar_w, Cfg::KATOMS * Cfg::W_ATOM);
+#pragma unroll
+        for (int a = 0; a < H / 64; ++a) {
+          tma_load_2d(sm + Cfg::OFF_W + a * Cfg::W_ATOM, &tmWa, &bar_w, a * 64, g * H + half * 128);
+          tma_load_2d(sm + Cfg::OFF_W + (H / 64 + a) * Cfg::W_ATOM, &tmWb, &bar_w, a * 64,
+                      g_other * H + half * 128);
+        }
+      }
+      if (!mbar_wait(&bar_w, n_wload & 1u, kWaitLimit)) atomicExch(p.err, 1);
+      ++n_wload;
+    }
+    if (p.reverse && db_group != g) {  // flush the bias-gradient partial of the previous group
+      if (db_group >= 0) atomicAdd(p.dbias + (int64_t)db_group * H + f, db_acc);
+      db_acc = 0.f;
+      db_group = g;
+    }
+    for (int ci = 0; ci < C; ++ci) {
+      const int c = p.reverse ? (C - 1 - ci) : ci;
+      const int c_nb = p.reverse ? c + 1 : c - 1;   // same-row neighbour
+      const int r_nb = p.reverse ? r + 1 : r - 1;   // other-row neighbour
+      if (tid == 0) {
+        bool ok = true;
+        if (c_nb >= 0 && c_nb < C)
+          for (int hh = 0; hh < NH; ++hh) ok &= wait_flag(p.flags + ((int64_t)r * C + c_nb) * 2 + hh, 1, p.spin_limit);
+        if (r_nb >= 0 && r_nb < R)
+          for (int hh = 0; hh < NH; ++hh) ok &= wait_flag(p.flags + ((int64_t)r_nb * C + c) * 2 + hh, 1, p.spin_limit);
+        if (!ok) atomicExch(p.err, 2);
+        fence_async_global();  // order the acquired generic stores before the TMA reads
+        uint8_t* sIn = sm + Cfg::OFF_IN;
+        mbar_arrive_expect_tx(&bar_in, Cfg::KATOMS * B * 128);
+#pragma unroll
+        for (int a = 0; a < H / 64; ++a) {
+          // out-of-grid coordinates are zero-filled: the zero boundary
+          tma_load_4d(sIn + a * B * 128, &tmIn, &bar_in, a * 64, 0, c_nb, r);
+          if (!p.reverse && r == 0 && p.has_top)
+            tma_load_3d(sIn + (H / 64 + a) * B * 128, &tmTop, &bar_in, a * 64, 0, c);
+          else
+            tma_load_4d(sIn + (H / 64 + a) * B * 128, &tmIn, &bar_in, a * 64, 0, c, r_nb);
+        }
+        if (!mbar_wait(&bar_in, n_cell & 1u, kWaitLimit)) atomicExch(p.err, 3);
+        tc_fence_after();
+        const uint32_t wa = smem_u32(sm + Cfg::OFF_W), ia = smem_u32(sIn);
+#pragma unroll
+        for (int kk = 0; kk < 2 * H / 16; ++kk) {
+          const uint64_t adesc = make_smem_desc(wa + (kk >> 2) * Cfg::W_ATOM + (kk & 3) * 32, 16, 1024, kSwizzle128B);
+          const uint64_t bdesc = make_smem_desc(ia + (kk >> 2) * B * 128 + (kk & 3) * 32, 16, 1024, kSwizzle128B);
+          umma_f16(tmem, adesc, bdesc, idesc, kk > 0 ? 1u : 0u);
+        }
+        umma_commit(&bar_mma);
+      }
+      __syncwarp();
+      if (!mbar_wait(&bar_mma, n_cell & 1u, kWaitLimit)) atomicExch(p.err, 4);
+      tc_fence_after();
+      ++n_cell;
+
+      // ---- epilogue: this thread owns feature f for every batch element --------------------
+      const int64_t cell = (int64_t)r * C + c;
+      for (int cb = 0; cb < B; cb += 32) {
+        uint32_t acc[32];
+        tmem_ld32(tmem + ((uint32_t)(warp * 32) << 16) + cb, acc);
+        tmem_wait_ld();
+        const int nb = min(32, B - cb);
+#pragma unroll
+        for (int j = 0; j < 32; ++j) {
+          if (j >= nb) break;
+          const int b = cb + j;
+          const int64_t o = (cell * B + b) * H + f;
+          float z = __uint_as_float(acc[j]);
+          if (!p.reverse) {
+            z += p.bias[(int64_t)g * H + f];
+            if (p.add) {
+              const int64_t row = p.add_layout == 0 ? ((int64_t)b * R + r) * C + c : cell * B + b;
+              z += p.add[row * H + f];
+            }
+            p.out[o] = __float2bfloat16_rn(tanh_approx(z));
+          } else {
+            const float hv = __bfloat162float(p.h[o]);
+            const float dz = (z + __bfloat162float(p.dh[o])) * (1.f - hv * hv);
+            const __nv_bfloat16 dzb = __float2bfloat16_rn(dz);
+            p.out[o] = dzb;
+            if (p.out2) p.out2[(((int64_t)b * R + r) * C + c) * H + f] = dzb;
+            db_acc += dz;
+          }
+        }
+      }
+      __threadfence();
+      tc_fence_before();
+      __syncthreads();
+      if (tid == 0 && cell != p.drop_cell) st_release(p.flags + cell * 2 + half, 1);
+    }
+  }
+  if (p.reverse && db_group >= 0) atomicAdd(p.dbias + (int64_t)db_group * H + f, db_acc);
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 0) tmem_dealloc(tmem, 64);
+}
+
+__global__ void transpose_weights_kernel(const __nv_bfloat16* __restrict__ W,
+                                         __nv_bfloat16* __restrict__ WT, int G, int H) {
+  // WT[g][i][o] = W[g][o][i]
+  __shared__ __nv_bfloat16 tile[32][33];
+  const int g = blockIdx.z;
+  const int o0 = blockIdx.y * 32, i0 = blockIdx.x * 32;
+  const __nv_bfloat16* src = W + (int64_t)g * H * H;
+  __nv_bfloat16* dst = WT + (int64_t)g * H * H;
+  for (int y = threadIdx.y; y < 32; y += blockDim.y)
+    tile[y][threadIdx.x] = src[(int64_t)(o0 + y) * H + i0 + threadIdx.x];
+  __syncthreads();
+  for (int y = threadIdx.y; y < 32; y += blockDim.y)
+    dst[(int64_t)(i0 + y) * H + o0 + threadIdx.x] = tile[threadIdx.x][y];
+}
+
+__global__ void sum_rows_kernel(const float* __restrict__ src, float* __restrict__ dst, int R,
+                                int64_t n, int first) {
+  // dst[e] = sum_{r >= first} src[r][e]
+  const int64_t e = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  if (e >= n) return;
+  float s = 0.f;
+  for (int r = first; r < R; ++r) s += src[(int64_t)r * n + e];
+  dst[e] = s;
+}
+
+// ---- cuBLAS (plain GEMMs only: hoisted U x, weight gradients, dx, dtop) ------------------------
+struct Blas {
+  cublasHandle_t h = nullptr;
+  int dev = -1;
+};
+thread_local Blas t_blas;
+
+int blas(cudaStream_t s, void* ws, size_t ws_bytes, cublasHandle_t* out) {
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (t_blas.h == nullptr || t_blas.dev != dev) {
+    if (cublasCreate(&t_blas.h) != CUBLAS_STATUS_SUCCESS) return fail(FLB_ERR_CUDA, "cublasCreate failed");
+    t_blas.dev = dev;
+  }
+  if (cublasSetStream(t_blas.h, s) != CUBLAS_STATUS_SUCCESS) return fail(FLB_ERR_CUDA, "cublasSetStream failed");
+  if (cublasSetWorkspace(t_blas.h, ws, ws_bytes) != CUBLAS_STATUS_SUCCESS)
+    return fail(FLB_ERR_CUDA, "cublasSetWorkspace failed");
+  *out = t_blas.h;
+  return FLB_OK;
+}
+
+// Row-major C[M x N] (+)= op(A)[M x K] . op(B)[K x N], bf16 inputs, fp32 output, batched with
+// element strides sA, sB, sC.
+int gemm_rm(cublasHandle_t h, bool ta, bool tb, int M, int N, int K, const void* A, int lda,
+            long long sA, const void* Bm, int ldb, long long sB, float* Cm, int ldc, long long sC,
+            int batch, float beta, cudaDataType ctype = CUDA_R_32F) {
+  const float alpha = 1.f;
+  cublasStatus_t st = cublasGemmStridedBatchedEx(
+      h, tb ? CUBLAS_OP_T : CUBLAS_OP_N, ta ? CUBLAS_OP_T : CUBLAS_OP_N, N, M, K, &alpha, Bm,
+      CUDA_R_16BF, ldb, sB, A, CUDA_R_16BF, lda, sA, &beta, Cm, ctype, ldc, sC, batch,
+      CUBLAS_COMPUTE_32F, CUBLAS_GEMM_DEFAULT);
+  if (st != CUBLAS_STATUS_SUCCESS) return fail(FLB_ERR_CUDA, "cublasGemmStridedBatchedEx failed (" + std::to_string((int)st) + ")");
+  return FLB_OK;
+}
+
+// ---- workspace layout ------------------------------------------------------------------------------
+constexpr size_t kBlasWs = 32u << 20;
+struct GridWs {
+  int* err;       // 256 B
+  int* flags;     // R*C*2 ints
+  float* add;     // hoisted U x, [R*C*B, H] fp32 (only with U)
+  __nv_bfloat16* dz;    // [R, C, B, H]
+  __nv_bfloat16* dzx;   // [B, R, C, H] (only with U and x_layout 0)
+  __nv_bfloat16* wt;    // transposed W_l, W_t: 2 x [G, H, H]
+  float* wtmp;    // [R, H, H] per-row weight-gradient partials
+  void* blas;     // cuBLAS workspace
+  size_t total;
+};
+
+size_t al(size_t x) { return (x + 255) & ~(size_t)255; }
+
+GridWs carve(void* base, int64_t R, int64_t C, int64_t B, int64_t H, int64_t G, int has_U) {
+  GridWs w{};
+  uint8_t* p = reinterpret_cast<uint8_t*>(base);
+  size_t o = 0;
+  auto take = [&](size_t n) { uint8_t* q = p ? p + o : nullptr; o += al(n); return q; };
+  const size_t cells = (size_t)(R * C);
+  w.err = (int*)take(256);
+  w.flags = (int*)take(cells * 2 * sizeof(int));
+  w.add = has_U ? (float*)take(cells * B * H * sizeof(float)) : nullptr;
+  w.dz = (__nv_bfloat16*)take(cells * B * H * 2);
+  w.dzx = has_U ? (__nv_bfloat16*)take(cells * B * H * 2) : nullptr;
+  w.wt = (__nv_bfloat16*)take((size_t)2 * G * H * H * 2);
+  w.wtmp = (float*)take((size_t)R * H * H * sizeof(float));
+  w.blas = take(kBlasWs);
+  w.total = o;
+  return w;
+}
+
+int make_w_map(CUtensorMap* m, const void* W, int64_t G, int64_t H) {
+  const uint64_t dims[2] = {(uint64_t)H, (uint64_t)(G * H)};
+  const uint64_t strides[1] = {(uint64_t)H * 2};
+  const uint32_t box[2] = {64, 128};
+  return make_tmap(m, W, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, dims, strides, box,
+                   CU_TENSOR_MAP_SWIZZLE_128B);
+}
+int make_grid_map(CUtensorMap* m, const void* X, int64_t R, int64_t C, int64_t B, int64_t H) {
+  const uint64_t dims[4] = {(uint64_t)H, (uint64_t)B, (uint64_t)C, (uint64_t)R};
+  const uint64_t strides[3] = {(uint64_t)H * 2, (uint64_t)(B * H * 2), (uint64_t)(C * B * H * 2)};
+  const uint32_t box[4] = {64, (uint32_t)B, 1, 1};
+  return make_tmap(m, X, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 4, dims, strides, box,
+                   CU_TENSOR_MAP_SWIZZLE_128B);
+}
+int make_top_map(CUtensorMap* m, const void* T, int64_t C, int64_t B, int64_t H) {
+  const uint64_t dims[3] = {(uint64_t)H, (uint64_t)B, (uint64_t)C};
+  const uint64_t strides[2] = {(uint64_t)H * 2, (uint64_t)(B * H * 2)};
+  const uint32_t box[3] = {64, (uint32_t)B, 1};
+  return make_tmap(m, T, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, dims, strides, box,
+                   CU_TENSOR_MAP_SWIZZLE_128B);
+}
+
+template <int H>
+int launch_sweep(const CUtensorMap& wa, const CUtensorMap& wb, const CUtensorMap& in,
+                 const CUtensorMap& top, const GridParams& p, cudaStream_t s, int* grid_ctas) {
+  const int smem = GridCfg<H>::smem(p.B);
+  static bool attr = false;
+  if (!attr) {
+    cudaError_t e = cudaFuncSetAttribute(grid_sweep_kernel<H>,
+                                         cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                         GridCfg<H>::smem(64));
+    if (e != cudaSuccess) return check_cuda(e, "grid_sweep smem attribute");
+    attr = true;
+  }
+  int per_sm = 0;
+  cudaError_t e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, grid_sweep_kernel<H>, 128, smem);
+  if (e != cudaSuccess || per_sm < 1) return fail(FLB_ERR_LAUNCH, "grid_sweep: kernel does not fit on an SM");
+  constexpr int NH = H / 128;
+  // every CTA must be resident at once (they wait on one another): cap the workers
+  const int capacity = per_sm * num_sms();
+  int workers = std::min<int>(p.R, capacity / NH);
+  if (workers < 1) return fail(FLB_ERR_LAUNCH, "grid_sweep: not enough resident CTAs");
+  *grid_ctas = workers * NH;
+  grid_sweep_kernel<H><<<workers * NH, 128, smem, s>>>(wa, wb, in, top, p);
+  count_launches(1);
+  return check_cuda(cudaGetLastError(), "grid_sweep launch");
+}
+
+int check_grid_args(int64_t R, int64_t C, int64_t B, int64_t H, int64_t G) {
+  if (R < 1 || C < 1) return fail(FLB_ERR_SHAPE, "grid: R and C must be >= 1");
+  if (!(H == 128 || H == 256)) return fail(FLB_ERR_UNSUPPORTED, "grid: hidden must be 128 or 256");
+  if (B < 16 || B > 64 || B % 16 != 0) return fail(FLB_ERR_UNSUPPORTED, "grid: batch must be 16, 32, 48 or 64");
+  if (!(G == 1 || G == R)) return fail(FLB_ERR_SHAPE, "grid: G must be 1 (shared) or R (per row)");
+  if (R * C > (int64_t)1 << 26) return fail(FLB_ERR_SHAPE, "grid: too many cells");
+  return FLB_OK;
+}
+
+int read_err(const int* err, cudaStream_t s, const char* what) {
+  int h = 0;
+  cudaError_t e = cudaMemcpyAsync(&h, err, sizeof(int), cudaMemcpyDeviceToHost, s);
+  if (e == cudaSuccess) e = cudaStreamSynchronize(s);
+  if (e != cudaSuccess) return check_cuda(e, what);
+  if (h != 0) return fail(FLB_ERR_TIMEOUT, std::string(what) + ": a bounded device wait gave up (code " + std::to_string(h) + ")");
+  return FLB_OK;
+}
+
+}  // namespace
+
+size_t grid_workspace_bytes(int64_t R, int64_t C, int64_t B, int64_t H, int64_t G, int has_U) {
+  return carve(nullptr, R, C, B, H, G, has_U).total;
+}
+
+int grid_fwd_impl(const void* x, int x_layout, const void* W_l, const void* W_t, const void* U,
+                  const float* bias, const void* top, void* h_out, int64_t R, int64_t C,
+                  int64_t B, int64_t H, int64_t G, void* ws, size_t ws_bytes, int check_timeout,
+                  cudaStream_t s, int64_t drop_cell, uint32_t spin_limit) {
+  int st = check_grid_args(R, C, B, H, G);
+  if (st != FLB_OK) return st;
+  if (!W_l || !W_t || !bias || !h_out || (U && !x)) return fail(FLB_ERR_SHAPE, "grid_fwd: null pointer");
+  GridWs w = carve(ws, R, C, B, H, G, U != nullptr);
+  if (!ws || ws_bytes < w.total) return fail(FLB_ERR_WORKSPACE, "grid_fwd: workspace smaller than flb_grid_workspace_bytes()");
+  cudaError_t e = cudaMemsetAsync(w.err, 0, 256, s);
+  if (e == cudaSuccess) e = cudaMemsetAsync(w.flags, 0, (size_t)R * C * 2 * sizeof(int), s);
+  if (e != cudaSuccess) return check_cuda(e, "grid_fwd memset");
+  if (U) {  // add = x U^T  (rows of x in its own layout)
+    cublasHandle_t h;
+    if ((st = blas(s, w.blas, kBlasWs, &h)) != FLB_OK) return st;
+    st = gemm_rm(h, false, true, (int)(R * C * B), (int)H, (int)H, x, (int)H, 0, U, (int)H, 0,
+                 w.add, (int)H, 0, 1, 0.f);
+    if (st != FLB_OK) return st;
+  }
+  CUtensorMap mWl, mWt, mIn, mTop;
+  if ((st = make_w_map(&mWl, W_l, G, H)) != FLB_OK) return st;
+  if ((st = make_w_map(&mWt, W_t, G, H)) != FLB_OK) return st;
+  if ((st = make_grid_map(&mIn, h_out, R, C, B, H)) != FLB_OK) return st;
+  if (top) {
+    if ((st = make_top_map(&mTop, top, C, B, H)) != FLB_OK) return st;
+  } else {
+    mTop = mIn;
+  }
+  GridParams p{};
+  p.add = U ? w.add : nullptr;
+  p.add_layout = x_layout;
+  p.bias = bias;
+  p.out = (__nv_bfloat16*)h_out;
+  p.flags = w.flags;
+  p.R = (int)R; p.C = (int)C; p.B = (int)B; p.G = (int)G;
+  p.has_top = top != nullptr;
+  p.reverse = 0;
+  p.err = w.err;
+  p.drop_cell = drop_cell;
+  p.spin_limit = spin_limit;
+  int ctas = 0;
+  st = H == 256 ? launch_sweep<256>(mWl, mWt, mIn, mTop, p, s, &ctas)
+                : launch_sweep<128>(mWl, mWt, mIn, mTop, p, s, &ctas);
+  if (st != FLB_OK) return st;
+  return check_timeout ? read_err(w.err, s, "grid_fwd") : FLB_OK;
+}
+
+int grid_fwd(const void* x, int x_layout, const void* W_l, const void* W_t, const void* U,
+             const float* bias, const void* top, void* h_out, int64_t R, int64_t C, int64_t B,
+             int64_t H, int64_t G, void* ws, size_t ws_bytes, int check_timeout, cudaStream_t s) {
+  return grid_fwd_impl(x, x_layout, W_l, W_t, U, bias, top, h_out, R, C, B, H, G, ws, ws_bytes,
+                       check_timeout, s, -1, kFlagSpinLimit);
+}
+
+int grid_bwd(const void* x, int x_layout, const void* W_l, const void* W_t, const void* U,
+             const void* top, const void* h_out, const void* dh, float* dW_l, float* dW_t,
+             float* dU, float* dbias, void* dx, void* dtop, int64_t R, int64_t C, int64_t B,
+             int64_t H, int64_t G, void* ws, size_t ws_bytes, int check_timeout, cudaStream_t s) {
+  int st = check_grid_args(R, C, B, H, G);
+  if (st != FLB_OK) return st;
+  if (!W_l || !W_t || !h_out || !dh || !dW_l || !dW_t || !dbias || (U && (!x || !dU)))
+    return fail(FLB_ERR_SHAPE, "grid_bwd: null pointer");
+  GridWs w = carve(ws, R, C, B, H, G, U != nullptr);
+  if (!ws || ws_bytes < w.total) return fail(FLB_ERR_WORKSPACE, "grid_bwd: workspace smaller than flb_grid_workspace_bytes()");
+  cudaError_t e = cudaMemsetAsync(w.err, 0, 256, s);
+  if (e == cudaSuccess) e = cudaMemsetAsync(w.flags, 0, (size_t)R * C * 2 * sizeof(int), s);
+  if (e == cudaSuccess) e = cudaMemsetAsync(dbias, 0, (size_t)G * H * sizeof(float), s);
+  if (e != cudaSuccess) return check_cuda(e, "grid_bwd memset");
+  // transposed weights: A operand rows are input features
+  __nv_bfloat16* WlT = w.wt;
+  __nv_bfloat16* WtT = w.wt + G * H * H;
+  dim3 tg((unsigned)(H / 32), (unsigned)(H / 32), (unsigned)G), tb(32, 8);
+  transpose_weights_kernel<<<tg, tb, 0, s>>>((const __nv_bfloat16*)W_l, WlT, (int)G, (int)H);
+  transpose_weights_kernel<<<tg, tb, 0, s>>>((const __nv_bfloat16*)W_t, WtT, (int)G, (int)H);
+  count_launches(2);
+  CUtensorMap mWl, mWt, mIn;
+  if ((st = make_w_map(&mWl, WlT, G, H)) != FLB_OK) return st;
+  if ((st = make_w_map(&mWt, WtT, G, H)) != FLB_OK) return st;
+  if ((st = make_grid_map(&mIn, w.dz, R, C, B, H)) != FLB_OK) return st;
+  GridParams p{};
+  p.out = w.dz;
+  p.out2 = (U && x_layout == 0) ? w.dzx : nullptr;
+  p.h = (const __nv_bfloat16*)h_out;
+  p.dh = (const __nv_bfloat16*)dh;
+  p.dbias = dbias;
+  p.flags = w.flags;
+  p.R = (int)R; p.C = (int)C; p.B = (int)B; p.G = (int)G;
+  p.has_top = 0;
+  p.reverse = 1;
+  p.err = w.err;
+  p.drop_cell = -1;
+  p.spin_limit = kFlagSpinLimit;
+  int ctas = 0;
+  st = H == 256 ? launch_sweep<256>(mWl, mWt, mIn, mIn, p, s, &ctas)
+                : launch_sweep<128>(mWl, mWt, mIn, mIn, p, s, &ctas);
+  if (st != FLB_OK) return st;
+
+  cublasHandle_t hb;
+  if ((st = blas(s, w.blas, kBlasWs, &hb)) != FLB_OK) return st;
+  const int Hi = (int)H;
+  const long long cellHB = (long long)B * H;         // elements per cell
+  const long long rowHB = (long long)C * cellHB;     // elements per grid row
+  const __nv_bfloat16* hh = (const __nv_bfloat16*)h_out;
+  float* tmp = w.wtmp;
+  // dW_l[r] = sum_{c>=1, b} dz[r][c][b][:]^T h[r][c-1][b][:]  (per row, K = (C-1) B)
+  if (C > 1) {
+    float* dst = (G > 1) ? dW_l : tmp;
+    st = gemm_rm(hb, true, false, Hi, Hi, (int)((C - 1) * B), w.dz + cellHB, Hi, rowHB, hh, Hi,
+                 rowHB, dst, Hi, (long long)H * H, (int)R, 0.f);
+    if (st != FLB_OK) return st;
+    if (G == 1) {
+      sum_rows_kernel<<<(unsigned)((H * H + 255) / 256), 256, 0, s>>>(tmp, dW_l, (int)R, H * H, 0);
+      count_launches(1);
+    }
+  } else {
+    e = cudaMemsetAsync(dW_l, 0, (size_t)G * H * H * sizeof(float), s);
+    if (e != cudaSuccess) return check_cuda(e, "grid_bwd memset dW_l");
+  }
+  // dW_t[r] = sum_{c, b} dz[r][c]^T h[r-1][c]  (r >= 1), and dz[0]^T top for r = 0
+  {
+    float* dst = (G > 1) ? dW_t : tmp;
+    if (R > 1) {
+      st = gemm_rm(hb, true, false, Hi, Hi, (int)(C * B), w.dz + rowHB, Hi, rowHB, hh, Hi, rowHB,
+                   dst + (long long)H * H, Hi, (long long)H * H, (int)(R - 1), 0.f);
+      if (st != FLB_OK) return st;
+    }
+    if (top) {
+      st = gemm_rm(hb, true, false, Hi, Hi, (int)(C * B), w.dz, Hi, 0, top, Hi, 0, dst, Hi, 0, 1, 0.f);
+    } else {
+      e = cudaMemsetAsync(dst, 0, (size_t)H * H * sizeof(float), s);
+      st = check_cuda(e, "grid_bwd memset dW_t row 0");
+    }
+    if (st != FLB_OK) return st;
+    if (G == 1) {
+      sum_rows_kernel<<<(unsigned)((H * H + 255) / 256), 256, 0, s>>>(tmp, dW_t, (int)R, H * H, 0);
+      count_launches(1);
+    }
+  }
+  if (U) {
+    const __nv_bfloat16* dzx = (x_layout == 0) ? w.dzx : w.dz;
+    const int M = (int)(R * C * B);
+    // dU = dz^T x ; dx = dz U
+    st = gemm_rm(hb, true, false, Hi, Hi, M, dzx, Hi, 0, x, Hi, 0, dU, Hi, 0, 1, 0.f);
+    if (st != FLB_OK) return st;
+    if (dx) {
+      st = gemm_rm(hb, false, false, M, Hi, Hi, dzx, Hi, 0, U, Hi, 0, (float*)dx, Hi, 0, 1, 0.f,
+                   CUDA_R_16BF);
+      if (st != FLB_OK) return st;
+    }
+  }
+  if (top && dtop) {  // dtop[c] = dz[0][c] W_t[0]
+    st = gemm_rm(hb, false, false, (int)(C * B), Hi, Hi, w.dz, Hi, 0, W_t, Hi, 0, (float*)dtop, Hi,
+                 0, 1, 0.f, CUDA_R_16BF);
+    if (st != FLB_OK) return st;
+  }
+  return check_timeout ? read_err(w.err, s, "grid_bwd") : FLB_OK;
+}
+
+}  // namespace flb

@@ -137,8 +137,9 @@ class FusedAdditiveAttentionFunc(torch.autograd.Function):
 
     @staticmethod
     def forward(q, k, v, v_a, causal=False, exact=False):
-        need_grad = torch.is_grad_enabled() and any(
-            t.requires_grad for t in (q, k, v, v_a))
+        # grad mode is off inside Function.forward; the inputs' flags say whether a backward
+        # can follow
+        need_grad = any(t.requires_grad for t in (q, k, v, v_a))
         out, lse, table, idx, scores = attention_forward(
             q, k, v, v_a, causal, exact, save_scores=need_grad and _save_scores_ok(q))
         out._flb_aux = (lse, table, idx, scores)

@@ -141,8 +141,7 @@ int flb_wf_index_copy(const void* src, int src_dtype, const int64_t src_strides[
  * x: [B, R, C, H] bf16 (row-major, x_layout 0) or [R, C, B, H] (x_layout 1).
  * W_l, W_t: [G, H, H] bf16 (nn.Linear layout [out, in]); U: [H, H] bf16 or NULL; bias: [G, H] f32.
  * top: [C, B, H] bf16 or NULL. h_out: [R, C, B, H] bf16 (engine grid order: cell-major).
- * Workspace: flb_grid_workspace_bytes(); it also carries what the backward needs, so pass the
- * same workspace, unmodified, to flb_grid_bwd.
+ * Workspace: flb_grid_workspace_bytes() (the backward takes its own, of the same size).
  * A device error word is read back (one 4-byte D2H copy, stream-synchronising) only when
  * check_timeout != 0.
  * ------------------------------------------------------------------------------------------ */
@@ -162,6 +161,17 @@ int flb_grid_bwd(const void* x, int x_layout, const void* W_l, const void* W_t, 
                  float* dW_l, float* dW_t, float* dU, float* dbias, void* dx, void* dtop,
                  int64_t R, int64_t C, int64_t B, int64_t H, int64_t G,
                  void* workspace, size_t workspace_bytes, int check_timeout, void* stream);
+
+/* Failure-detection check of the grid kernels' bounded dependency waits (no reference
+ * counterpart). Runs flb_grid_fwd with the flag of cell (drop_row, drop_col) never released and
+ * the flag-wait bound lowered to spin_limit polls: the cells waiting on it give up, record the
+ * error word and finish their row, so the call returns FLB_ERR_TIMEOUT (read back
+ * synchronously) and the context stays usable. No GPU fault or trap is involved. */
+int flb_grid_fwd_drop_flag_test(const void* x, int x_layout, const void* W_l, const void* W_t,
+                                const void* U, const float* bias, const void* top, void* h_out,
+                                int64_t R, int64_t C, int64_t B, int64_t H, int64_t G,
+                                void* workspace, size_t workspace_bytes, int64_t drop_row,
+                                int64_t drop_col, uint32_t spin_limit, void* stream);
 
 /* ------------------------------------------------------------------------------------------
  * Measurement helpers (used by bench.py for the roofline denominators).
