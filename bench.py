@@ -248,9 +248,47 @@ def extra_grid(device, steps=3, warmup=1):
         step()
     ms = time_steps(step, steps, 1) / steps
     cells = 64 * 64
-    return {"workload": "wavefront grid 64x64 batch32 hidden256 bf16 fwd+bwd", "ms": round(ms, 3),
-            "cells_per_s": cells / (ms * 1e-3),
+    return {"workload": "wavefront grid 64x64 batch32 hidden256 bf16 fwd+bwd (U x at every cell)",
+            "ms": round(ms, 3), "cells_per_s": cells / (ms * 1e-3),
             "tensor_tflops": 3 * 51.5e9 / (ms * 1e-3) / 1e12}
+
+
+def extra_engine(device, steps=2, warmup=1):
+    """The engine API on a 64x64 grid of per-row tanh cells (batch 32, hidden 256, bf16, x at
+    row 0 as in the reference engine), forward + backward: the persistent kernels (fast path)
+    against the per-diagonal tick loop (the reference's schedule: one host tick per
+    anti-diagonal with gather, vmapped cell and scatter), same inputs and weights."""
+    import torch.nn as nn
+    from wavefront import WavefrontConfig, WavefrontEngine
+    from wavefront.grid_layer import TanhGridCell
+
+    class TickCell(TanhGridCell):  # not the exact type: the engine takes its per-tick path
+        pass
+
+    torch.manual_seed(0)
+    R = C = 64
+    B, H = 32, 256
+    cfg = WavefrontConfig(grid_shape=(R, C), batch_size=B, dim=H)
+    fast = nn.ModuleList([TanhGridCell(H) for _ in range(R)]).to(device)
+    tick = nn.ModuleList([TickCell(H) for _ in range(R)]).to(device)
+    tick.load_state_dict(fast.state_dict())
+    x = torch.randn(B, C, H, device=device).bfloat16()
+    res = {}
+    for name, layers, n in (("persistent", fast, steps), ("per_diagonal", tick, 1)):
+        eng = WavefrontEngine(cfg, layers).to(device)
+
+        def step():
+            xx = x.detach().requires_grad_(True)
+            g = eng(xx)
+            (g[0].float().sum() + g[1][-1].float().sum()).backward()
+        for _ in range(warmup):
+            step()
+        res[name] = time_steps(step, n, 1) / n
+    return {"workload": "WavefrontEngine 64x64 per-row tanh cells, batch32 hidden256 bf16 fwd+bwd",
+            "persistent_ms": round(res["persistent"], 3),
+            "per_diagonal_ms": round(res["per_diagonal"], 3),
+            "speedup": res["per_diagonal"] / res["persistent"],
+            "cells_per_s": R * C / (res["persistent"] * 1e-3)}
 
 
 # ------------------------------------------------------------------ arms
@@ -327,6 +365,7 @@ def run_flb(args):
         g = extra_grid(device)
         if g is not None:
             out["extras"]["grid"] = g
+        out["extras"]["engine"] = extra_engine(device)
     if rank == 0:
         print(json.dumps(out), flush=True)
     if world > 1:
@@ -363,6 +402,27 @@ def run_reference(args):
     print(json.dumps(out), flush=True)
 
 
+def run_profile_case(case: str):
+    """A short, fixed workload for ncu: one warm-up step and one profiled step, no timing.
+    attn: A2 attention forward (saving scores) + backward. grid: W4 grid layer forward +
+    backward (64x64, batch 32, hidden 256)."""
+    device = torch.device("cuda", 0)
+    if case == "attn":
+        from kernels.additive_attention import attention_forward, attention_backward
+        q, k, v, w, do = make_attn_inputs(A2, 1000, device)
+        for _ in range(2):
+            out, lse, table, idx, sc = attention_forward(q, k, v, w, True, save_scores=True)
+            attention_backward(q, k, v, w, out, lse, do, table, idx, True, scores=sc)
+    else:
+        from wavefront.grid_layer import wavefront_grid_layer, grid_inputs
+        x, Wl, Wt, U, b, dh = grid_inputs(32, 64, 64, 256, device, seed=3)
+        for _ in range(2):
+            ts = [t.detach().requires_grad_(True) for t in (x, Wl, Wt, U, b)]
+            wavefront_grid_layer(*ts).backward(dh)
+    torch.cuda.synchronize()
+    print("profile case done:", case)
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -371,8 +431,12 @@ def main():
     ap.add_argument("--impl", choices=["flb", "reference"], default="flb")
     ap.add_argument("--no-extras", action="store_true")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--profile", choices=["attn", "grid"], default=None,
+                    help="run one fixed warm-up + profiled step for ncu and exit")
     args = ap.parse_args()
-    if args.impl == "reference":
+    if args.profile:
+        run_profile_case(args.profile)
+    elif args.impl == "reference":
         run_reference(args)
     else:
         run_flb(args)

@@ -67,7 +67,9 @@ struct GridCfg {
   static constexpr int W_ATOM = 128 * 128;            // bytes: 128 rows x 128 B
   static constexpr int OFF_W = 0;
   static constexpr int OFF_IN = KATOMS * W_ATOM;      // B operand atoms follow
-  static int smem(int B) { return OFF_IN + KATOMS * B * 128 + 1024; }
+  // epilogue operands of a cell, staged by TMA: [B][128] fp32 (add) or 2 x [B][128] bf16 (h, dh)
+  __host__ __device__ static int off_ep(int B) { return OFF_IN + KATOMS * B * 128; }
+  __host__ __device__ static int smem(int B) { return off_ep(B) + B * 128 * 4 + 1024; }
 };
 
 struct GridParams {
@@ -93,13 +95,14 @@ template <int H>
 __global__ void __launch_bounds__(128, 1)
 grid_sweep_kernel(const __grid_constant__ CUtensorMap tmWa, const __grid_constant__ CUtensorMap tmWb,
                   const __grid_constant__ CUtensorMap tmIn, const __grid_constant__ CUtensorMap tmTop,
+                  const __grid_constant__ CUtensorMap tmE1, const __grid_constant__ CUtensorMap tmE2,
                   GridParams p) {
   using namespace sm100;
   using Cfg = GridCfg<H>;
   constexpr int NH = H / 128;  // feature halves (CTAs per row)
   extern __shared__ uint8_t smem_raw[];
   uint8_t* sm = (uint8_t*)(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
-  __shared__ __align__(8) uint64_t bar_w, bar_in, bar_mma;
+  __shared__ __align__(8) uint64_t bar_w, bar_in, bar_mma, bar_ep;
   __shared__ uint32_t tmem_slot;
 
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
@@ -113,6 +116,7 @@ grid_sweep_kernel(const __grid_constant__ CUtensorMap tmWa, const __grid_constan
     mbar_init(&bar_w, 1);
     mbar_init(&bar_in, 1);
     mbar_init(&bar_mma, 1);
+    mbar_init(&bar_ep, 1);
     fence_mbar_init();
     tma_prefetch_desc(&tmWa);
     tma_prefetch_desc(&tmWb);
@@ -129,7 +133,7 @@ grid_sweep_kernel(const __grid_constant__ CUtensorMap tmWa, const __grid_constan
   const uint32_t tmem = tmem_slot;
   const uint32_t idesc = make_idesc_f16(128, B, 1, 0, 0);
   const int f = half * 128 + warp * 32 + lane;  // this thread's output feature
-  uint32_t n_wload = 0, n_cell = 0;
+  uint32_t n_wload = 0, n_cell = 0, n_ep = 0;
   float db_acc = 0.f;
   int db_group = -1;
 
@@ -161,6 +165,22 @@ grid_sweep_kernel(const __grid_constant__ CUtensorMap tmWa, const __grid_constan
       const int c = p.reverse ? (C - 1 - ci) : ci;
       const int c_nb = p.reverse ? c + 1 : c - 1;   // same-row neighbour
       const int r_nb = p.reverse ? r + 1 : r - 1;   // other-row neighbour
+      const bool stage_add = !p.reverse && p.add != nullptr;
+      if (tid == 0 && (p.reverse || stage_add)) {
+        // epilogue operands do not depend on the recurrence: fetch them before waiting on it
+        uint8_t* sE = sm + Cfg::off_ep(B);
+        if (p.reverse) {
+          mbar_arrive_expect_tx(&bar_ep, 2 * B * 128 * 2);
+          tma_load_4d(sE, &tmE1, &bar_ep, half * 128, 0, c, r);                 // h
+          tma_load_4d(sE + B * 128 * 2, &tmE2, &bar_ep, half * 128, 0, c, r);   // dh
+        } else {
+          mbar_arrive_expect_tx(&bar_ep, B * 128 * 4);
+          if (p.add_layout == 0)
+            tma_load_4d(sE, &tmE1, &bar_ep, half * 128, c, r, 0);  // add rows (b, r, c)
+          else
+            tma_load_4d(sE, &tmE1, &bar_ep, half * 128, 0, c, r);  // add rows (r, c, b)
+        }
+      }
       if (tid == 0) {
         bool ok = true;
         if (c_nb >= 0 && c_nb < C)
@@ -198,6 +218,13 @@ grid_sweep_kernel(const __grid_constant__ CUtensorMap tmWa, const __grid_constan
 
       // ---- epilogue: this thread owns feature f for every batch element --------------------
       const int64_t cell = (int64_t)r * C + c;
+      const uint8_t* sE = sm + Cfg::off_ep(B);
+      const int fl = warp * 32 + lane;  // feature within this CTA's half
+      if (p.reverse || stage_add) {
+        if (!mbar_wait(&bar_ep, n_ep & 1u, kWaitLimit)) atomicExch(p.err, 5);
+        ++n_ep;
+      }
+      const float bias_f = p.reverse ? 0.f : p.bias[(int64_t)g * H + f];
       for (int cb = 0; cb < B; cb += 32) {
         uint32_t acc[32];
         tmem_ld32(tmem + ((uint32_t)(warp * 32) << 16) + cb, acc);
@@ -210,15 +237,14 @@ grid_sweep_kernel(const __grid_constant__ CUtensorMap tmWa, const __grid_constan
           const int64_t o = (cell * B + b) * H + f;
           float z = __uint_as_float(acc[j]);
           if (!p.reverse) {
-            z += p.bias[(int64_t)g * H + f];
-            if (p.add) {
-              const int64_t row = p.add_layout == 0 ? ((int64_t)b * R + r) * C + c : cell * B + b;
-              z += p.add[row * H + f];
-            }
+            z += bias_f;
+            if (stage_add) z += reinterpret_cast<const float*>(sE)[b * 128 + fl];
             p.out[o] = __float2bfloat16_rn(tanh_approx(z));
           } else {
-            const float hv = __bfloat162float(p.h[o]);
-            const float dz = (z + __bfloat162float(p.dh[o])) * (1.f - hv * hv);
+            const float hv = __bfloat162float(reinterpret_cast<const __nv_bfloat16*>(sE)[b * 128 + fl]);
+            const float dhv = __bfloat162float(
+                reinterpret_cast<const __nv_bfloat16*>(sE + B * 128 * 2)[b * 128 + fl]);
+            const float dz = (z + dhv) * (1.f - hv * hv);
             const __nv_bfloat16 dzb = __float2bfloat16_rn(dz);
             p.out[o] = dzb;
             if (p.out2) p.out2[(((int64_t)b * R + r) * C + c) * H + f] = dzb;
@@ -354,9 +380,26 @@ int make_top_map(CUtensorMap* m, const void* T, int64_t C, int64_t B, int64_t H)
                    CU_TENSOR_MAP_SWIZZLE_128B);
 }
 
+// Epilogue staging maps: a cell's [B x 128] slice of a [R, C, B, H] grid (bf16 or fp32), or of a
+// [B, R, C, H] array (x layout 0, fp32).
+int make_ep_map(CUtensorMap* m, const void* X, CUtensorMapDataType dt, int esz, int layout,
+                int64_t R, int64_t C, int64_t B, int64_t H) {
+  if (layout == 1) {
+    const uint64_t dims[4] = {(uint64_t)H, (uint64_t)B, (uint64_t)C, (uint64_t)R};
+    const uint64_t strides[3] = {(uint64_t)H * esz, (uint64_t)(B * H * esz), (uint64_t)(C * B * H * esz)};
+    const uint32_t box[4] = {128, (uint32_t)B, 1, 1};
+    return make_tmap(m, X, dt, 4, dims, strides, box, CU_TENSOR_MAP_SWIZZLE_NONE);
+  }
+  const uint64_t dims[4] = {(uint64_t)H, (uint64_t)C, (uint64_t)R, (uint64_t)B};
+  const uint64_t strides[3] = {(uint64_t)H * esz, (uint64_t)(C * H * esz), (uint64_t)(R * C * H * esz)};
+  const uint32_t box[4] = {128, 1, 1, (uint32_t)B};
+  return make_tmap(m, X, dt, 4, dims, strides, box, CU_TENSOR_MAP_SWIZZLE_NONE);
+}
+
 template <int H>
 int launch_sweep(const CUtensorMap& wa, const CUtensorMap& wb, const CUtensorMap& in,
-                 const CUtensorMap& top, const GridParams& p, cudaStream_t s, int* grid_ctas) {
+                 const CUtensorMap& top, const CUtensorMap& e1, const CUtensorMap& e2,
+                 const GridParams& p, cudaStream_t s, int* grid_ctas) {
   const int smem = GridCfg<H>::smem(p.B);
   static bool attr = false;
   if (!attr) {
@@ -375,7 +418,7 @@ int launch_sweep(const CUtensorMap& wa, const CUtensorMap& wb, const CUtensorMap
   int workers = std::min<int>(p.R, capacity / NH);
   if (workers < 1) return fail(FLB_ERR_LAUNCH, "grid_sweep: not enough resident CTAs");
   *grid_ctas = workers * NH;
-  grid_sweep_kernel<H><<<workers * NH, 128, smem, s>>>(wa, wb, in, top, p);
+  grid_sweep_kernel<H><<<workers * NH, 128, smem, s>>>(wa, wb, in, top, e1, e2, p);
   count_launches(1);
   return check_cuda(cudaGetLastError(), "grid_sweep launch");
 }
@@ -432,6 +475,9 @@ int grid_fwd_impl(const void* x, int x_layout, const void* W_l, const void* W_t,
   } else {
     mTop = mIn;
   }
+  CUtensorMap mAdd = mIn;
+  if (U && (st = make_ep_map(&mAdd, w.add, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4, x_layout, R, C, B, H)) != FLB_OK)
+    return st;
   GridParams p{};
   p.add = U ? w.add : nullptr;
   p.add_layout = x_layout;
@@ -445,8 +491,8 @@ int grid_fwd_impl(const void* x, int x_layout, const void* W_l, const void* W_t,
   p.drop_cell = drop_cell;
   p.spin_limit = spin_limit;
   int ctas = 0;
-  st = H == 256 ? launch_sweep<256>(mWl, mWt, mIn, mTop, p, s, &ctas)
-                : launch_sweep<128>(mWl, mWt, mIn, mTop, p, s, &ctas);
+  st = H == 256 ? launch_sweep<256>(mWl, mWt, mIn, mTop, mAdd, mAdd, p, s, &ctas)
+                : launch_sweep<128>(mWl, mWt, mIn, mTop, mAdd, mAdd, p, s, &ctas);
   if (st != FLB_OK) return st;
   return check_timeout ? read_err(w.err, s, "grid_fwd") : FLB_OK;
 }
@@ -497,8 +543,11 @@ int grid_bwd(const void* x, int x_layout, const void* W_l, const void* W_t, cons
   p.drop_cell = -1;
   p.spin_limit = kFlagSpinLimit;
   int ctas = 0;
-  st = H == 256 ? launch_sweep<256>(mWl, mWt, mIn, mIn, p, s, &ctas)
-                : launch_sweep<128>(mWl, mWt, mIn, mIn, p, s, &ctas);
+  CUtensorMap mH, mDH;
+  if ((st = make_ep_map(&mH, h_out, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, 1, R, C, B, H)) != FLB_OK) return st;
+  if ((st = make_ep_map(&mDH, dh, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, 1, R, C, B, H)) != FLB_OK) return st;
+  st = H == 256 ? launch_sweep<256>(mWl, mWt, mIn, mIn, mH, mDH, p, s, &ctas)
+                : launch_sweep<128>(mWl, mWt, mIn, mIn, mH, mDH, p, s, &ctas);
   if (st != FLB_OK) return st;
 
   cublasHandle_t hb;
