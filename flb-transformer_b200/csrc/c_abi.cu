@@ -62,6 +62,9 @@ int grid_fwd_impl(const void* x, int x_layout, const void* W_l, const void* W_t,
                   const float* bias, const void* top, void* h_out, int64_t R, int64_t C,
                   int64_t B, int64_t H, int64_t G, void* ws, size_t ws_bytes, int check_timeout,
                   cudaStream_t s, int64_t drop_cell, uint32_t spin_limit);
+int grid_fwd_static(const void* W_l, const void* W_t, const float* bias, const void* top,
+                    void* h_out, int64_t R, int64_t C, int64_t B, int64_t H, int64_t G,
+                    int check_timeout, cudaStream_t s);
 int microbench(int kind, void* scratch, double* ops_per_s);
 int umma_selftest(int variant, int n, const void* A, const void* B, float* D, int* err,
                   cudaStream_t s);
@@ -212,6 +215,13 @@ int flb_grid_fwd_drop_flag_test(const void* x, int x_layout, const void* W_l, co
   return grid_fwd_impl(x, x_layout, W_l, W_t, U, bias, top, h_out, R, C, B, H, G, workspace,
                        workspace_bytes, 1, as_stream(stream), drop_row * C + drop_col,
                        spin_limit);
+}
+
+int flb_grid_fwd_static(const void* W_l, const void* W_t, const float* bias, const void* top,
+                        void* h_out, int64_t R, int64_t C, int64_t B, int64_t H, int64_t G,
+                        int check_timeout, void* stream) {
+  return grid_fwd_static(W_l, W_t, bias, top, h_out, R, C, B, H, G, check_timeout,
+                         as_stream(stream));
 }
 
 int flb_microbench(int kind, void* scratch, double* ops_per_s) {

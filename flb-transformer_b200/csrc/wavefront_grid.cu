@@ -24,6 +24,9 @@
 // cuBLAS GEMMs over dz and the saved h (and x), and db is reduced inside the sweep.
 #include <cublas_v2.h>
 
+#include <mutex>
+#include <string>
+
 #include "common.cuh"
 #include "sm100.cuh"
 #include "tma_host.cuh"
@@ -609,6 +612,88 @@ int grid_bwd(const void* x, int x_layout, const void* W_l, const void* W_t, cons
     if (st != FLB_OK) return st;
   }
   return check_timeout ? read_err(w.err, s, "grid_bwd") : FLB_OK;
+}
+
+// =============================================================================================
+// Allocation-free grid forward.
+//
+// Some callers cannot allocate device memory at the moment they run this layer: a serving process
+// that carved all of its device memory into a fixed pool up front, code running inside another
+// runtime's allocator, or a call site that must not touch the CUDA allocator at all. For them
+// flb_grid_fwd_static takes no workspace: its scratch (the error word and the per-cell dependency
+// flags) lives in the file-scope array below, sized for at most kStaticMaxCells grid cells. The
+// array belongs to the library's module on every device that loads it (512 KB + 256 B) and stays
+// there until the process exits. Calls share it: each call clears the part it uses before its
+// kernel runs, and two calls whose kernels overlap on the GPU (different streams, no ordering
+// between them) would race on the flags, so such calls must be ordered. On the first call on a
+// device the host looks the array's device address up (cudaGetSymbolAddress, with that device
+// current) and caches it; make that first call before any stream capture.
+// =============================================================================================
+constexpr int64_t kStaticMaxCells = 65536;
+constexpr int kStaticErrInts = 64;  // 256 bytes, the error word and padding
+static __device__ __align__(256) int g_grid_static_scratch[kStaticErrInts + kStaticMaxCells * 2];
+
+int grid_fwd_static(const void* W_l, const void* W_t, const float* bias, const void* top,
+                    void* h_out, int64_t R, int64_t C, int64_t B, int64_t H, int64_t G,
+                    int check_timeout, cudaStream_t s) {
+  int st = check_grid_args(R, C, B, H, G);
+  if (st != FLB_OK) return st;
+  if (!W_l || !W_t || !bias || !h_out) return fail(FLB_ERR_SHAPE, "grid_fwd_static: null pointer");
+  if (R * C > kStaticMaxCells)
+    return fail(FLB_ERR_SHAPE, "grid_fwd_static: " + std::to_string(R * C) +
+                                   " cells exceed the static scratch limit of " +
+                                   std::to_string(kStaticMaxCells) +
+                                   " cells; use flb_grid_fwd with a workspace");
+  constexpr int kMaxDevices = 64;
+  static std::mutex mu;
+  static int* dev_ptr[kMaxDevices] = {};
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return check_cuda(e, "grid_fwd_static: cudaGetDevice");
+  if (dev < 0 || dev >= kMaxDevices) return fail(FLB_ERR_UNSUPPORTED, "grid_fwd_static: device index too large");
+  int* base = nullptr;
+  {
+    std::lock_guard<std::mutex> lock(mu);
+    if (dev_ptr[dev] == nullptr) {
+      void* p = nullptr;
+      e = cudaGetSymbolAddress(&p, g_grid_static_scratch);
+      if (e != cudaSuccess) return check_cuda(e, "grid_fwd_static: cudaGetSymbolAddress");
+      dev_ptr[dev] = static_cast<int*>(p);
+    }
+    base = dev_ptr[dev];
+  }
+  int* err = base;
+  int* flags = base + kStaticErrInts;
+  // the previous call left its flags and error word behind: clear what this call reads
+  e = cudaMemsetAsync(err, 0, kStaticErrInts * sizeof(int), s);
+  if (e == cudaSuccess) e = cudaMemsetAsync(flags, 0, (size_t)R * C * 2 * sizeof(int), s);
+  if (e != cudaSuccess) return check_cuda(e, "grid_fwd_static: clear scratch");
+  CUtensorMap mWl, mWt, mIn, mTop;
+  if ((st = make_w_map(&mWl, W_l, G, H)) != FLB_OK) return st;
+  if ((st = make_w_map(&mWt, W_t, G, H)) != FLB_OK) return st;
+  if ((st = make_grid_map(&mIn, h_out, R, C, B, H)) != FLB_OK) return st;
+  if (top) {
+    if ((st = make_top_map(&mTop, top, C, B, H)) != FLB_OK) return st;
+  } else {
+    mTop = mIn;
+  }
+  GridParams p{};
+  p.add = nullptr;
+  p.add_layout = 1;
+  p.bias = bias;
+  p.out = (__nv_bfloat16*)h_out;
+  p.flags = flags;
+  p.R = (int)R; p.C = (int)C; p.B = (int)B; p.G = (int)G;
+  p.has_top = top != nullptr;
+  p.reverse = 0;
+  p.err = err;
+  p.drop_cell = -1;
+  p.spin_limit = kFlagSpinLimit;
+  int ctas = 0;
+  st = H == 256 ? launch_sweep<256>(mWl, mWt, mIn, mTop, mIn, mIn, p, s, &ctas)
+                : launch_sweep<128>(mWl, mWt, mIn, mTop, mIn, mIn, p, s, &ctas);
+  if (st != FLB_OK) return st;
+  return check_timeout ? read_err(err, s, "grid_fwd_static") : FLB_OK;
 }
 
 }  // namespace flb

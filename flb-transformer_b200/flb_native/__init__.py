@@ -55,6 +55,8 @@ PROTOTYPES = {
     "flb_grid_fwd_drop_flag_test": (_i32, [_vp, _i32, _vp, _vp, _vp, _vp, _vp, _vp, _i64, _i64,
                                            _i64, _i64, _i64, _vp, _sz, _i64, _i64, ctypes.c_uint32,
                                            _vp]),
+    "flb_grid_fwd_static": (_i32, [_vp, _vp, _vp, _vp, _vp, _i64, _i64, _i64, _i64, _i64, _i32,
+                                   _vp]),
     "flb_microbench": (_i32, [_i32, _vp, _dblp]),
     "flb_selftest_umma": (_i32, [_i32, _i32, _vp, _vp, _vp, _vp, _vp]),
 }

@@ -162,6 +162,20 @@ int flb_grid_bwd(const void* x, int x_layout, const void* W_l, const void* W_t, 
                  int64_t R, int64_t C, int64_t B, int64_t H, int64_t G,
                  void* workspace, size_t workspace_bytes, int check_timeout, void* stream);
 
+/* Allocation-free form of flb_grid_fwd for callers that cannot allocate device memory when they
+ * run the layer (a serving process with its memory carved into a fixed pool up front, code running
+ * inside another runtime's allocator). No counterpart in the reference. It takes no workspace:
+ * its scratch (error word and per-cell dependency flags) is a static device array of the library,
+ * 512 KB + 256 B on every device that loads it, held until process exit, which limits it to
+ * R * C <= 65536 cells (larger grids are rejected with FLB_ERR_SHAPE). It evaluates the engine
+ * form of the cell (no x U^T term: x enters through `top`, or not at all). The first call on a
+ * device looks the array's address up and caches it, so make that call before any stream
+ * capture. All calls share the array and each clears what it uses; calls whose kernels could
+ * overlap on the GPU race on it and must be ordered. Arguments as for flb_grid_fwd. */
+int flb_grid_fwd_static(const void* W_l, const void* W_t, const float* bias, const void* top,
+                        void* h_out, int64_t R, int64_t C, int64_t B, int64_t H, int64_t G,
+                        int check_timeout, void* stream);
+
 /* Failure-detection check of the grid kernels' bounded dependency waits (no reference
  * counterpart). Runs flb_grid_fwd with the flag of cell (drop_row, drop_col) never released and
  * the flag-wait bound lowered to spin_limit polls: the cells waiting on it give up, record the
