@@ -178,8 +178,8 @@ class AttnStep:
             e[2].record()
             self.ev.append(e)
         if self.world > 1:
-            import torch.distributed as dist
-            dist.all_reduce(w.grad)
+            from kernels.sharding import all_reduce_v_a_grad
+            all_reduce_v_a_grad(w)  # the backward's exchange step: v_a is replicated
         return out, q.grad, k.grad, v.grad, w.grad
 
     def kernel_ms(self):
