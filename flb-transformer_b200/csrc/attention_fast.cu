@@ -87,6 +87,25 @@ __device__ __forceinline__ float ex2_approx(float x) {
   return y;
 }
 
+// Packed half-precision helpers of the backward's tanh grid. On B200 tanh.approx.f16x2 and the
+// f16x2 add/mul/fma deliver as many elements per second as their f32 forms with half the
+// instructions, and that stage is issue-bound.
+__device__ __forceinline__ __half2 tanh_h2(__half2 x) {
+  uint32_t r, v = *reinterpret_cast<uint32_t*>(&x);
+  asm("tanh.approx.f16x2 %0, %1;" : "=r"(r) : "r"(v));
+  return *reinterpret_cast<__half2*>(&r);
+}
+__device__ __forceinline__ void red_shared_f32(float* p, float v) {
+  asm volatile("red.shared.add.f32 [%0], %1;" ::"r"(sm100::smem_u32(p)), "f"(v) : "memory");
+}
+template <typename T> __device__ __forceinline__ __half2 to_h2(uint32_t packed);
+template <> __device__ __forceinline__ __half2 to_h2<__half>(uint32_t packed) {
+  return *reinterpret_cast<__half2*>(&packed);
+}
+template <> __device__ __forceinline__ __half2 to_h2<__nv_bfloat16>(uint32_t packed) {
+  return __floats2half2_rn(__uint_as_float(packed << 16), __uint_as_float(packed & 0xFFFF0000u));
+}
+
 template <int D, typename T>
 __global__ void __launch_bounds__(128, 2)
 attn_fwd_tc_kernel(const __grid_constant__ CUtensorMap tmK, const __grid_constant__ CUtensorMap tmV,
@@ -432,7 +451,7 @@ struct BwdCfg {
   static constexpr int OFF_DO = OFF_V + BN * D * 2;        // 2 stages, swizzled
   static constexpr int OFF_Q = OFF_DO + 2 * TILE;          // 2 stages, plain rows
   static constexpr int OFF_P = OFF_Q + 2 * TILE;           // 2 x 16 KB MN-major atoms
-  static constexpr int DS_LD = BN + 4;                     // fp32 row pitch of the dS tile
+  static constexpr int DS_LD = BN + 4;                     // row pitch (4-byte entries) of the dS tile
   static constexpr int OFF_DS = OFF_P + BM * BN * 2;
   static constexpr int OFF_DQ = OFF_DS + BM * DS_LD * 4;   // fp32 [128 x 64]
   static constexpr int SMEM = OFF_DQ + BM * D * 4 + 1024;
@@ -474,7 +493,7 @@ __global__ void bwd_finish_kernel(const float* __restrict__ dq_acc, const float*
 }
 
 template <typename T>
-__global__ void __launch_bounds__(256, 1)
+__global__ void __launch_bounds__(512, 1)
 attn_bwd_tc_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmDO,
                    const __grid_constant__ CUtensorMap tmV, const T* __restrict__ k,
                    const float* __restrict__ w, const int32_t* __restrict__ w_index,
@@ -486,6 +505,7 @@ attn_bwd_tc_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constan
   using C = BwdCfg;
   using U = Unpack<T>;
   constexpr int D = C::D;
+  constexpr int NT = 512;  // 16 warps
   extern __shared__ uint8_t smem_raw[];
   uint8_t* sm = (uint8_t*)(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
   __shared__ __align__(8) uint64_t full_bar[2];
@@ -501,6 +521,7 @@ attn_bwd_tc_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constan
   const int ntiles = nqt - t_first;
   const float inv_sqrt_d = 0.125f;
   const float* wrow = w + (int64_t)w_index[bh] * D;
+  const T* kbh = k + (int64_t)bh * N * D;
 
   if (tid == 0) {
     mbar_init(&full_bar[0], 1);
@@ -514,19 +535,17 @@ attn_bwd_tc_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constan
     tmem_relinquish();
   }
   float* sDQ = reinterpret_cast<float*>(sm + C::OFF_DQ);
-  for (int i = tid; i < C::BM * D; i += 256) sDQ[i] = 0.f;
-  // this warp's 16 keys, this lane's two head dims, in registers
-  float kr[16][2];
+  for (int i = tid; i < C::BM * D; i += NT) sDQ[i] = 0.f;
+  // phase B ownership: warp w holds keys 8w..8w+7 of the block, lane l holds head dims 2l, 2l+1
+  __half2 kr[8];
 #pragma unroll
-  for (int j = 0; j < 16; ++j) {
-    const int key = kb0 + warp * 16 + j;
-    if (key < N) {
-      const uint32_t kv = reinterpret_cast<const uint32_t*>(k + ((int64_t)bh * N + key) * D)[lane];
-      U::run(kv, kr[j][0], kr[j][1]);
-    } else {
-      kr[j][0] = kr[j][1] = 0.f;
-    }
+  for (int j = 0; j < 8; ++j) {
+    const int key = kb0 + warp * 8 + j;
+    kr[j] = key < N ? to_h2<T>(reinterpret_cast<const uint32_t*>(kbh + (int64_t)key * D)[lane])
+                    : __floats2half2_rn(0.f, 0.f);
   }
+  __shared__ unsigned s_amax;  // max |dS| of the current tile (float bits; non-negative floats order as ints)
+  if (tid == 0) s_amax = 0u;
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
@@ -555,8 +574,7 @@ attn_bwd_tc_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constan
     tma_prefetch_desc(&tmQ);
     tma_prefetch_desc(&tmDO);
     tma_prefetch_desc(&tmV);
-    // V block (K-major B operand of dP) and the first query tile share stage 0's barrier:
-    // exactly one arrive.expect_tx per barrier phase (the barrier's arrival count is 1)
+    // V block and the first query tile share stage 0's barrier: one arrive.expect_tx per phase
     mbar_arrive_expect_tx(&full_bar[0], C::BN * D * 2 + 2 * C::TILE);
     tma_load_3d(sm + C::OFF_V, &tmV, &full_bar[0], 0, kb0, bh);
     tma_load_3d(sm + C::OFF_DO, &tmDO, &full_bar[0], 0, t_first * C::BM, bh);
@@ -568,60 +586,98 @@ attn_bwd_tc_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constan
   }
   __syncwarp();
 
-  float dka[16][2];
-#pragma unroll
-  for (int j = 0; j < 16; ++j) dka[j][0] = dka[j][1] = 0.f;
-  float dwa0 = 0.f, dwa1 = 0.f;
-  const int arow = 32 * (warp & 3) + lane;  // phase-A query row within the tile (TMEM lane)
-  const int ahalf = warp >> 2;              // phase-A key half
+  // phase A ownership: TMEM lane quarter (warp & 3) = query rows, key group (warp >> 2) of 32
+  const int arow = 32 * (warp & 3) + lane;
+  const int agrp = warp >> 2;
   float* sDS = reinterpret_cast<float*>(sm + C::OFF_DS);
+
+  // phase A inputs of a tile (saved scores, lse, Delta), loaded one tile ahead
+  float sc[32], lse2 = 0.f, dlt = 0.f;
+  auto load_scores = [&](int t) {
+    const int i = (t_first + t) * C::BM + arow;
+    const bool row_ok = i < N;
+    lse2 = row_ok ? lse[(int64_t)bh * N + i] * kLog2e : 0.f;
+    dlt = row_ok ? delta[(int64_t)bh * N + i] : 0.f;
+    const int key0 = kb0 + 32 * agrp;
+    const float* srow = scores + ((int64_t)bh * N + (row_ok ? i : 0)) * N + key0;
+    const bool any = row_ok && key0 < N && (!causal || key0 <= i);
+    if (any && key0 + 32 <= N && (reinterpret_cast<uintptr_t>(srow) & 15u) == 0) {
+      // 8 vector loads; unwritten (masked) entries are read but discarded below
+#pragma unroll
+      for (int c = 0; c < 8; ++c) {
+        const float4 v4 = reinterpret_cast<const float4*>(srow)[c];
+        sc[4 * c] = v4.x; sc[4 * c + 1] = v4.y; sc[4 * c + 2] = v4.z; sc[4 * c + 3] = v4.w;
+      }
+    } else {
+#pragma unroll
+      for (int e = 0; e < 32; ++e) sc[e] = (any && key0 + e < N) ? srow[e] : 0.f;
+    }
+#pragma unroll
+    for (int e = 0; e < 32; ++e) {
+      const int key = key0 + e;
+      if (!(row_ok && key < N && (!causal || key <= i))) sc[e] = -INFINITY;
+    }
+  };
+  load_scores(0);
+
+  float dka[8][2];  // fp32 dK partials of this warp's keys over all tiles
+#pragma unroll
+  for (int j = 0; j < 8; ++j) dka[j][0] = dka[j][1] = 0.f;
+  float dwa0 = 0.f, dwa1 = 0.f;
+  uint32_t* sDSh = reinterpret_cast<uint32_t*>(sm + C::OFF_DS);  // dS tile as scaled {ds, ds} half2
 
   for (int t = 0; t < ntiles; ++t) {
     const int q0 = (t_first + t) * C::BM;
     const int st = t & 1;
-    // ---- phase A: P and dS from dP (TMEM) and the saved scores ------------------------------
     // every thread observes the TMA barrier of this tile (phase B reads the Q tile)
     if (!mbar_wait(&full_bar[st], (uint32_t)(t >> 1) & 1u, kWaitLimit)) atomicExch(err, 10);
     if (!mbar_wait(&dp_bar, (uint32_t)t & 1u, kWaitLimit)) atomicExch(err, 12);
     if (t >= 1 && !mbar_wait(&dv_bar, (uint32_t)(t - 1) & 1u, kWaitLimit)) atomicExch(err, 13);
     tc_fence_after();
+    // ---- phase A: P and dS for (row arow, keys 32*agrp .. +31) ------------------------------
+    float ds[32];
     {
-      const int i = q0 + arow;
-      const bool row_ok = i < N;
-      const float lse2 = row_ok ? lse[(int64_t)bh * N + i] * kLog2e : 0.f;
-      const float dlt = row_ok ? delta[(int64_t)bh * N + i] : 0.f;
-      const float* srow = scores + ((int64_t)bh * N + (row_ok ? i : 0)) * N + kb0 + 64 * ahalf;
-      uint8_t* sP = sm + C::OFF_P + ahalf * (C::BM * 128);
-      float* dsrow = sDS + arow * C::DS_LD + 64 * ahalf;
+      uint32_t r[32];
+      tmem_ld32(tmem + ((uint32_t)(32 * (warp & 3)) << 16) + 32 * agrp, r);
+      tmem_wait_ld();
+      uint8_t* sP = sm + C::OFF_P + (agrp >> 1) * (C::BM * 128);
+      float amax = 0.f;
 #pragma unroll
-      for (int cb = 0; cb < 2; ++cb) {
-        uint32_t r[32];
-        tmem_ld32(tmem + ((uint32_t)(32 * (warp & 3)) << 16) + 64 * ahalf + 32 * cb, r);
-        tmem_wait_ld();
+      for (int g = 0; g < 4; ++g) {
+        uint32_t pk[4];
 #pragma unroll
-        for (int g = 0; g < 4; ++g) {
-          float p[8], ds[8];
-#pragma unroll
-          for (int e = 0; e < 8; ++e) {
-            const int jj = 64 * ahalf + 32 * cb + 8 * g + e;
-            const int key = kb0 + jj;
-            const bool ok = row_ok && key < N && (!causal || key <= i);
-            const float sv = ok ? srow[32 * cb + 8 * g + e] : 0.f;
-            p[e] = ok ? ex2_approx(sv * kLog2e - lse2) : 0.f;
-          }
-          uint32_t pk[4];
-#pragma unroll
-          for (int e = 0; e < 4; ++e) {
-            float r0, r1;
-            pk[e] = U::pack(p[2 * e], p[2 * e + 1], r0, r1);
-            ds[2 * e] = r0 * (__uint_as_float(r[8 * g + 2 * e]) - dlt);
-            ds[2 * e + 1] = r1 * (__uint_as_float(r[8 * g + 2 * e + 1]) - dlt);
-          }
-          *reinterpret_cast<uint4*>(sP + sw128_offset(arow, 4 * cb + g)) =
-              make_uint4(pk[0], pk[1], pk[2], pk[3]);
-          reinterpret_cast<float4*>(dsrow + 32 * cb + 8 * g)[0] = make_float4(ds[0], ds[1], ds[2], ds[3]);
-          reinterpret_cast<float4*>(dsrow + 32 * cb + 8 * g)[1] = make_float4(ds[4], ds[5], ds[6], ds[7]);
+        for (int e = 0; e < 4; ++e) {
+          const float p0 = ex2_approx(sc[8 * g + 2 * e] * kLog2e - lse2);
+          const float p1 = ex2_approx(sc[8 * g + 2 * e + 1] * kLog2e - lse2);
+          float r0, r1;
+          pk[e] = U::pack(p0, p1, r0, r1);
+          ds[8 * g + 2 * e] = r0 * (__uint_as_float(r[8 * g + 2 * e]) - dlt);
+          ds[8 * g + 2 * e + 1] = r1 * (__uint_as_float(r[8 * g + 2 * e + 1]) - dlt);
+          amax = fmaxf(amax, fmaxf(fabsf(ds[8 * g + 2 * e]), fabsf(ds[8 * g + 2 * e + 1])));
         }
+        *reinterpret_cast<uint4*>(sP + sw128_offset(arow, 4 * (agrp & 1) + g)) =
+            make_uint4(pk[0], pk[1], pk[2], pk[3]);
+      }
+      amax = warp_max(amax);
+      if (lane == 0) atomicMax(&s_amax, __float_as_uint(amax));
+    }
+    __syncthreads();
+    // a power-of-two scale per tile keeps the half-precision sums of phase B inside fp16's
+    // normal range: max |dS| * scale lies in [256, 512)
+    const float amax_tile = __uint_as_float(s_amax);
+    const int ex = amax_tile > 0.f ? ilogbf(amax_tile) : 0;
+    const float ds_scale = ldexpf(1.f, 8 - ex), ds_unscale = ldexpf(1.f, ex - 8);
+    {
+      uint32_t* dsrow = sDSh + arow * C::DS_LD + 32 * agrp;
+#pragma unroll
+      for (int c = 0; c < 8; ++c) {
+        uint32_t v[4];
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+          __half2 h = __float2half2_rn(ds[4 * c + e] * ds_scale);
+          v[e] = *reinterpret_cast<uint32_t*>(&h);
+        }
+        reinterpret_cast<uint4*>(dsrow)[c] = make_uint4(v[0], v[1], v[2], v[3]);
       }
     }
     fence_async_shared();
@@ -647,40 +703,59 @@ attn_bwd_tc_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constan
       }
     }
     __syncwarp();
+    // next tile's phase-A inputs: global loads in flight during the tanh grid below
+    if (t + 1 < ntiles) load_scores(t + 1);
 
-    // ---- phase B: the tanh grid ------------------------------------------------------------
+    // ---- phase B: the tanh grid, packed f16x2 (lane = head dims 2l, 2l+1) ----------------------
     {
       const uint32_t* sQ = reinterpret_cast<const uint32_t*>(sm + C::OFF_Q + st * C::TILE);
-      const int key_lo = kb0 + warp * 16;
+      const int key_lo = kb0 + warp * 8;
       const int rmax = min(C::BM, N - q0);
+      const __half2 hz = __floats2half2_rn(0.f, 0.f);
+      __half2 dk2[8];
+#pragma unroll
+      for (int j = 0; j < 8; ++j) dk2[j] = hz;
+      int pending = 0;  // rows accumulated in dk2 since the last flush
 #pragma unroll 1
       for (int r = 0; r < rmax; ++r) {
         if (causal && key_lo > q0 + r) continue;  // every key of this warp is masked for row r
-        float q0f, q1f;
-        U::run(sQ[r * (D / 2) + lane], q0f, q1f);
-        const float4* dsr = reinterpret_cast<const float4*>(sDS + r * C::DS_LD + warp * 16);
-        float dsv[16];
+        const __half2 q2 = to_h2<T>(sQ[r * (D / 2) + lane]);
+        const uint4* dsr = reinterpret_cast<const uint4*>(sDSh + r * C::DS_LD + warp * 8);
+        const uint4 a4 = dsr[0], b4 = dsr[1];
+        const uint32_t dsu[8] = {a4.x, a4.y, a4.z, a4.w, b4.x, b4.y, b4.z, b4.w};
+        __half2 dq2 = hz, dw2 = hz;
 #pragma unroll
-        for (int c = 0; c < 4; ++c) {
-          const float4 v4 = dsr[c];
-          dsv[4 * c] = v4.x; dsv[4 * c + 1] = v4.y; dsv[4 * c + 2] = v4.z; dsv[4 * c + 3] = v4.w;
+        for (int j = 0; j < 8; ++j) {
+          const __half2 d2 = *reinterpret_cast<const __half2*>(&dsu[j]);
+          const __half2 t2 = tanh_h2(__hadd2(q2, kr[j]));
+          const __half2 u2 = __hmul2(d2, t2);
+          const __half2 g2 = __hfma2(__hneg2(u2), t2, d2);
+          dq2 = __hadd2(dq2, g2);
+          dk2[j] = __hadd2(dk2[j], g2);
+          dw2 = __hadd2(dw2, u2);
         }
-        float dq0 = 0.f, dq1 = 0.f;
+        const float2 dqf = __half22float2(dq2), dwf = __half22float2(dw2);
+        // dQ partials: layout [row][c * 32 + lane] for head dim 2 * lane + c (conflict-free)
+        red_shared_f32(&sDQ[r * D + lane], dqf.x * ds_unscale);
+        red_shared_f32(&sDQ[r * D + 32 + lane], dqf.y * ds_unscale);
+        dwa0 = fmaf(dwf.x, ds_unscale, dwa0);
+        dwa1 = fmaf(dwf.y, ds_unscale, dwa1);
+        if (++pending == 32) {
 #pragma unroll
-        for (int j = 0; j < 16; ++j) {
-          const float t0 = tanh_approx(q0f + kr[j][0]);
-          const float t1 = tanh_approx(q1f + kr[j][1]);
-          const float u0 = dsv[j] * t0, u1 = dsv[j] * t1;
-          const float g0 = fmaf(-u0, t0, dsv[j]), g1 = fmaf(-u1, t1, dsv[j]);
-          dq0 += g0;
-          dq1 += g1;
-          dka[j][0] += g0;
-          dka[j][1] += g1;
-          dwa0 += u0;
-          dwa1 += u1;
+          for (int j = 0; j < 8; ++j) {
+            const float2 f = __half22float2(dk2[j]);
+            dka[j][0] = fmaf(f.x, ds_unscale, dka[j][0]);
+            dka[j][1] = fmaf(f.y, ds_unscale, dka[j][1]);
+            dk2[j] = hz;
+          }
+          pending = 0;
         }
-        atomicAdd(&sDQ[r * D + 2 * lane], dq0);
-        atomicAdd(&sDQ[r * D + 2 * lane + 1], dq1);
+      }
+#pragma unroll
+      for (int j = 0; j < 8; ++j) {
+        const float2 f = __half22float2(dk2[j]);
+        dka[j][0] = fmaf(f.x, ds_unscale, dka[j][0]);
+        dka[j][1] = fmaf(f.y, ds_unscale, dka[j][1]);
       }
     }
     __syncthreads();
@@ -688,10 +763,13 @@ attn_bwd_tc_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constan
     {
       const int rows = min(C::BM, N - q0);
       float* dst = dq_acc + ((int64_t)bh * N + q0) * D;
-      for (int e = tid; e < rows * D; e += 256) {
-        atomicAdd(dst + e, sDQ[e]);
-        sDQ[e] = 0.f;
+      for (int e = tid; e < rows * D; e += NT) {
+        const int rr = e / D, d = e % D;
+        float* src = &sDQ[rr * D + (d & 1) * 32 + (d >> 1)];
+        atomicAdd(dst + e, *src);
+        *src = 0.f;
       }
+      if (tid == 0) s_amax = 0u;
     }
     if (tid == 0 && t + 2 < ntiles) {
       // stage st: Q read by phase B (done: barrier above), dO read by dV MMA t
@@ -702,38 +780,35 @@ attn_bwd_tc_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constan
     __syncthreads();
   }
 
-  // ---- epilogue: dV from TMEM, dK and dw from registers ----------------------------------------
-  if (ntiles > 0 && !mbar_wait(&dv_bar, (uint32_t)(ntiles - 1) & 1u, kWaitLimit)) atomicExch(err, 16);
+  // ---- epilogue: dV from TMEM (warps 0-7: lane quarter x column half), dK and dw from registers
+  if (!mbar_wait(&dv_bar, (uint32_t)(ntiles - 1) & 1u, kWaitLimit)) atomicExch(err, 16);
   tc_fence_after();
-  if (warp < 4) {
-    const int key = kb0 + 32 * warp + lane;
+  if (warp < 8) {
+    const int key = kb0 + 32 * (warp & 3) + lane;
+    const int cb = warp >> 2;  // columns 32*cb .. +31 of dV
+    uint32_t r[32];
+    tmem_ld32(tmem + ((uint32_t)(32 * (warp & 3)) << 16) + 128 + 32 * cb, r);
+    tmem_wait_ld();
+    if (key < N) {
+      T* dst = dv + ((int64_t)bh * N + key) * D + 32 * cb;
 #pragma unroll
-    for (int cb = 0; cb < 2; ++cb) {
-      uint32_t r[32];
-      tmem_ld32(tmem + ((uint32_t)(32 * warp) << 16) + 128 + 32 * cb, r);
-      tmem_wait_ld();
-      if (key < N) {
-        T* dst = dv + ((int64_t)bh * N + key) * D + 32 * cb;
+      for (int g = 0; g < 4; ++g) {
+        uint32_t pk[4];
 #pragma unroll
-        for (int g = 0; g < 4; ++g) {
-          uint32_t pk[4];
-#pragma unroll
-          for (int e = 0; e < 4; ++e) {
-            float r0, r1;
-            const float a = ntiles > 0 ? __uint_as_float(r[8 * g + 2 * e]) : 0.f;
-            const float b2 = ntiles > 0 ? __uint_as_float(r[8 * g + 2 * e + 1]) : 0.f;
-            pk[e] = U::pack(a, b2, r0, r1);
-          }
-          reinterpret_cast<uint4*>(dst)[g] = make_uint4(pk[0], pk[1], pk[2], pk[3]);
+        for (int e = 0; e < 4; ++e) {
+          float r0, r1;
+          pk[e] = U::pack(__uint_as_float(r[8 * g + 2 * e]), __uint_as_float(r[8 * g + 2 * e + 1]),
+                          r0, r1);
         }
+        reinterpret_cast<uint4*>(dst)[g] = make_uint4(pk[0], pk[1], pk[2], pk[3]);
       }
     }
   }
   {
     const float w0 = wrow[2 * lane] * inv_sqrt_d, w1 = wrow[2 * lane + 1] * inv_sqrt_d;
 #pragma unroll
-    for (int j = 0; j < 16; ++j) {
-      const int key = kb0 + warp * 16 + j;
+    for (int j = 0; j < 8; ++j) {
+      const int key = kb0 + warp * 8 + j;
       if (key < N) {
         float r0, r1;
         reinterpret_cast<uint32_t*>(dk + ((int64_t)bh * N + key) * D)[lane] =
@@ -782,7 +857,7 @@ int launch_bwd_tc(const void* q, const void* k, const void* v, const float* w, c
     attr_set = true;
   }
   const dim3 grid((unsigned)((N + C::BN - 1) / C::BN), (unsigned)BH);
-  attn_bwd_tc_kernel<T><<<grid, 256, C::SMEM, s>>>(tmQ, tmDO, tmV, (const T*)k, w, wi, lse, delta,
+  attn_bwd_tc_kernel<T><<<grid, 512, C::SMEM, s>>>(tmQ, tmDO, tmV, (const T*)k, w, wi, lse, delta,
                                                    scores, dq_acc, (T*)dk, (T*)dv, dw, N, causal, err);
   bwd_finish_kernel<T><<<(unsigned)((rows * 32 + 255) / 256), 256, 0, s>>>(dq_acc, w, wi, (T*)dq, N,
                                                                            rows);
