@@ -111,7 +111,8 @@ __global__ void __launch_bounds__(128, 2)
 attn_fwd_tc_kernel(const __grid_constant__ CUtensorMap tmK, const __grid_constant__ CUtensorMap tmV,
                    const T* __restrict__ q, T* __restrict__ out, float* __restrict__ lse,
                    float* __restrict__ scores, const float* __restrict__ w,
-                   const int32_t* __restrict__ w_index, int N, int causal, int* __restrict__ err) {
+                   const int32_t* __restrict__ w_index, int N, int causal, int nbh,
+                   int* __restrict__ err) {
   using namespace sm100;
   using C = FwdCfg<D>;
   using U = Unpack<T>;
@@ -122,9 +123,12 @@ attn_fwd_tc_kernel(const __grid_constant__ CUtensorMap tmK, const __grid_constan
   __shared__ uint32_t tmem_slot;
 
   const int tid = threadIdx.x, warp = tid >> 5;
-  const int nqb = gridDim.x;
-  const int qb = causal ? (nqb - 1 - (int)blockIdx.x) : (int)blockIdx.x;  // heavy blocks first
-  const int bh = blockIdx.y;
+  // 1-D grid over (query block, head), heaviest query blocks of every head first (causal work
+  // grows with the block index): the longest CTAs start in the first wave, not in the tail
+  const int nqb = gridDim.x / nbh;
+  const int lin = blockIdx.x;
+  const int qb = causal ? (nqb - 1 - lin / nbh) : (lin / nbh);
+  const int bh = lin % nbh;
   const int m0 = qb * C::BM;
   const int row = m0 + tid;
   const bool row_ok = row < N;
@@ -382,9 +386,9 @@ int launch_fwd_tc(const void* q, const void* k, const void* v, const float* w, c
     if (e != cudaSuccess) return check_cuda(e, "attn_fwd_tc smem attribute");
     attr_set = true;
   }
-  const dim3 grid((unsigned)((N + C::BM - 1) / C::BM), (unsigned)BH);
+  const unsigned grid = (unsigned)(((N + C::BM - 1) / C::BM) * BH);
   attn_fwd_tc_kernel<D, T><<<grid, 128, C::SMEM, s>>>(tmK, tmV, (const T*)q, (T*)out, lse, scores,
-                                                      w, wi, N, causal, err);
+                                                      w, wi, N, causal, (int)BH, err);
   count_launches(1);
   return check_cuda(cudaGetLastError(), "attn_fwd_tc launch");
 }
@@ -500,7 +504,7 @@ attn_bwd_tc_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constan
                    const float* __restrict__ lse, const float* __restrict__ delta,
                    const float* __restrict__ scores, float* __restrict__ dq_acc,
                    T* __restrict__ dk, T* __restrict__ dv, float* __restrict__ dw, int N,
-                   int causal, int* __restrict__ err) {
+                   int causal, int nbh, int* __restrict__ err) {
   using namespace sm100;
   using C = BwdCfg;
   using U = Unpack<T>;
@@ -513,8 +517,10 @@ attn_bwd_tc_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constan
   __shared__ uint32_t tmem_slot;
 
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-  const int kb = blockIdx.x;  // ascending key blocks = most query tiles first
-  const int bh = blockIdx.y;
+  // 1-D grid over (key block, head); key blocks ascend = most query tiles first, so every head's
+  // heaviest CTAs start in the first wave
+  const int kb = blockIdx.x / nbh;
+  const int bh = blockIdx.x % nbh;
   const int kb0 = kb * C::BN;
   const int nqt = (N + C::BM - 1) / C::BM;
   const int t_first = causal ? kb : 0;
@@ -856,9 +862,10 @@ int launch_bwd_tc(const void* q, const void* k, const void* v, const float* w, c
     if (e != cudaSuccess) return check_cuda(e, "attn_bwd_tc smem attribute");
     attr_set = true;
   }
-  const dim3 grid((unsigned)((N + C::BN - 1) / C::BN), (unsigned)BH);
+  const unsigned grid = (unsigned)(((N + C::BN - 1) / C::BN) * BH);
   attn_bwd_tc_kernel<T><<<grid, 512, C::SMEM, s>>>(tmQ, tmDO, tmV, (const T*)k, w, wi, lse, delta,
-                                                   scores, dq_acc, (T*)dk, (T*)dv, dw, N, causal, err);
+                                                   scores, dq_acc, (T*)dk, (T*)dv, dw, N, causal,
+                                                   (int)BH, err);
   bwd_finish_kernel<T><<<(unsigned)((rows * 32 + 255) / 256), 256, 0, s>>>(dq_acc, w, wi, (T*)dq, N,
                                                                            rows);
   count_launches(3);

@@ -194,7 +194,9 @@ int flb_grid_fwd_drop_flag_test(const void* x, int x_layout, const void* W_l, co
 /* Times a saturating loop of one instruction class on every SM and returns the measured
  * throughput in operations (elements) per second through *ops_per_s (host pointer).
  * kind: 0 = tanh.approx.f32, 1 = tanh.approx.f16x2 (2 elements/instr), 2 = tanh.approx.bf16x2,
- *       3 = ex2.approx.f32, 4 = FFMA f32, 5 = HFMA2 f16x2 (2 elements/instr).
+ *       3 = ex2.approx.f32, 4 = FFMA f32, 5 = HFMA2 f16x2 (2 elements/instr),
+ *       6 = the attention backward's per-element tanh-grid step in f16x2 (tanh elements),
+ *       7 = the same step in f32, 8 = the forward's score step (FADD, tanh, FFMA) in f32.
  * Synchronises the device. scratch: device buffer of >= 4 * 148 * 1024 bytes. */
 int flb_microbench(int kind, void* scratch, double* ops_per_s);
 
