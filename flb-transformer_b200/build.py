@@ -39,6 +39,7 @@ NVCC_FLAGS = [
     "-gencode", "arch=compute_100a,code=sm_100a",
     "-O3", "-lineinfo", "-std=c++17",
     "-Xcompiler", "-fPIC",
+    "-Xcompiler", "-fvisibility=hidden",  # export only the C API declared in include/flb_b200.h
     "--expt-relaxed-constexpr",
     "-Xptxas", "-warn-spills",
     "-I", INCLUDE,

@@ -20,6 +20,11 @@
 #include <stdint.h>
 #include <stddef.h>
 
+/* Only the C API is exported from libflb_b200.so (built with -fvisibility=hidden). */
+#if defined(__GNUC__)
+#pragma GCC visibility push(default)
+#endif
+
 #ifdef __cplusplus
 extern "C" {
 #endif
@@ -210,5 +215,9 @@ int flb_selftest_umma(int variant, int n, const void* A, const void* B, float* D
 
 #ifdef __cplusplus
 }
+#endif
+
+#if defined(__GNUC__)
+#pragma GCC visibility pop
 #endif
 #endif /* FLB_B200_H */
