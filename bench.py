@@ -335,7 +335,7 @@ def run_flb(args):
     tanh_peak = nat.microbench(0, device)
     # DRAM bytes per launch (dram__bytes_read.sum + dram__bytes_write.sum) from an ncu capture of
     # `bench.py --profile attn` on B200; the launches of this workload move the same bytes.
-    traffic = {"forward": 113.1e6 + 1063.6e6, "backward": 1296.5e6 + 128.3e6}
+    traffic = {"forward": 356.1e6 + 1061.7e6, "backward": 2073.4e6 + 503.7e6}
     tanh_work = pairs_of(cfg) * cfg["D"]
     dom = "backward" if bwd_ms >= fwd_ms else "forward"
     dom_ms = max(bwd_ms, fwd_ms)
