@@ -1,25 +1,28 @@
 // Blackwell (sm_100a) additive-attention forward for bf16/fp16 inputs, head dim 64 or 128.
 //
-// Per CTA: 128 query rows of one (batch, head), one thread per row, 4 warps; two CTAs per SM.
+// Per CTA: 128 query rows of one (batch, head). D / 32 threads share a row, each holding 32 of
+// its head dims: 8 warps (D = 64, two CTAs per SM) or 16 warps (D = 128, one CTA per SM), so
+// 16 warps per SM hide the MUFU and shared-memory latencies at 128 registers per thread.
 //   * K and V tiles of 64 keys stream into shared memory with TMA (3-D tensor maps over
-//     [BH, N, D], no multicast), 2-3 stages, completion on mbarriers.
-//   * Scores are an FMA/MUFU elementwise reduction, not a GEMM: each thread keeps its q row in
-//     fp32 registers and, for every key, accumulates w'[d] * tanh.approx(q[d] + k[d]) with
-//     fp32 FADD / MUFU / FFMA (w' = w * log2(e) / sqrt(D), so scores are in log2 units). K is
-//     read from shared memory with warp-broadcast 16-byte loads. On B200 the packed
-//     tanh.approx.{f16x2,bf16x2} forms deliver the same elements per second as the f32 form,
-//     so fp32 costs nothing and keeps full accumulation precision.
-//   * Softmax: each thread owns a whole row, so no cross-thread reduction. The row keeps a
-//     reference max m fixed from its first key tile; P = exp2(s - m). Only if a later tile's
-//     max exceeds m by more than 8 (P would exceed 256) is the row rescaled, which needs the
-//     accumulator in TMEM to be read, scaled and written back (rare: the scores of this
-//     operator are bounded by sum|w|/sqrt(D)).
+//     [BH, N, D], no multicast), 3 stages, completion on mbarriers.
+//   * Scores are an FMA/MUFU elementwise reduction, not a GEMM: each thread keeps its part of
+//     the q row in fp32 registers and, for every key, accumulates w'[d] * tanh.approx(q[d] +
+//     k[d]) with fp32 FADD / MUFU / FFMA (w' = w * log2(e) / sqrt(D), so scores are in log2
+//     units); a shuffle butterfly over the row's lanes completes the sum. K is read from shared
+//     memory with broadcast 16-byte loads. On B200 the packed tanh.approx.{f16x2,bf16x2} forms
+//     deliver the same elements per second as the f32 form, so fp32 costs nothing and keeps
+//     full accumulation precision.
+//   * Softmax: every lane of a row holds the row's full scores, so no further reduction. The
+//     row keeps a reference max m fixed from its first keys; P = exp2(s - m). Only if a later
+//     group's max exceeds m by more than 8 (P would exceed 256) is the row rescaled: its P
+//     pieces of the tile at once, the accumulator rows in TMEM at the end of the tile (rare: the
+//     scores of this operator are bounded by sum|w|/sqrt(D)).
 //   * P (bf16/fp16, the dtype of V) is written by the threads into a K-major 128-byte-swizzled
 //     shared tile; one elected thread issues tcgen05.mma (M=128, N=D, K=16 steps) with V as an
 //     MN-major operand, accumulating O in TMEM. MMA completion (tcgen05.commit -> mbarrier)
 //     gates the reuse of the P and V buffers, so the tensor core runs one tile behind the
 //     score computation.
-//   * Epilogue: tcgen05.ld of the row, scale by 1/l, store; lse = (m + log2 l) * ln 2.
+//   * Epilogue: tcgen05.ld of the rows, scale by 1/l, store; lse = (m + log2 l) * ln 2.
 // Every mbarrier wait is bounded; a wait that gives up records an error code in the error
 // word (workspace) and the kernel still releases its TMEM and exits.
 #include "common.cuh"
@@ -38,7 +41,10 @@ constexpr float kRescaleThreshold = 8.f;  // log2 units
 template <int D>
 struct FwdCfg {
   static constexpr int BM = 128, BN = 64;
-  static constexpr int STAGES = (D == 64) ? 3 : 2;
+  static constexpr int TPR = D / 32;               // threads per query row, 32 dims each
+  static constexpr int THREADS = BM * TPR;         // 256 (D = 64) or 512 (D = 128)
+  static constexpr int MIN_BLOCKS = (D == 64) ? 2 : 1;
+  static constexpr int STAGES = 3;
   static constexpr int KTILE = BN * D * 2;   // bytes, bf16/fp16
   static constexpr int VTILE = BN * D * 2;
   static constexpr int PTILE = BM * BN * 2;  // 16 KB
@@ -107,22 +113,34 @@ template <> __device__ __forceinline__ __half2 to_h2<__nv_bfloat16>(uint32_t pac
 }
 
 template <int D, typename T>
-__global__ void __launch_bounds__(128, 2)
+__global__ void __launch_bounds__(FwdCfg<D>::THREADS, FwdCfg<D>::MIN_BLOCKS)
 attn_fwd_tc_kernel(const __grid_constant__ CUtensorMap tmK, const __grid_constant__ CUtensorMap tmV,
                    const T* __restrict__ q, T* __restrict__ out, float* __restrict__ lse,
                    float* __restrict__ scores, const float* __restrict__ w,
                    const int32_t* __restrict__ w_index, int N, int causal, int nbh,
-                   int* __restrict__ err) {
+                   int scores_vec, int* __restrict__ err) {
   using namespace sm100;
   using C = FwdCfg<D>;
   using U = Unpack<T>;
+  constexpr int TPR = C::TPR;     // threads per query row
+  constexpr int DH = D / TPR;     // head dims per thread (32)
+  constexpr int KPT = 8 / TPR;    // keys of each 8-key group this thread scores into P
+  constexpr int RPW = 32 / TPR;   // rows per warp
   extern __shared__ uint8_t smem_raw[];
   uint8_t* sm = (uint8_t*)(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
   __shared__ __align__(8) uint64_t full_bar[C::STAGES];
   __shared__ __align__(8) uint64_t mma_bar[2];
   __shared__ uint32_t tmem_slot;
+  __shared__ float sAlpha[C::BM];  // per-row accumulator rescale of the current tile
+  __shared__ float sL[C::BM];      // per-row softmax denominators for the epilogue
 
-  const int tid = threadIdx.x, warp = tid >> 5;
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  // TPR consecutive lanes of a warp share a query row, each owning DH of its head dims. Warp w
+  // serves TMEM lane quarter w % 4 (the only lanes its tcgen05.ld/st may touch): rows
+  // 32 (w % 4) + RPW (w / 4) + lane / TPR of the 128-row tile.
+  const int quarter = warp & 3, wsub = warp >> 2;
+  const int dh = lane % TPR;
+  const int mrow = 32 * quarter + RPW * wsub + lane / TPR;
   // 1-D grid over (query block, head), heaviest query blocks of every head first (causal work
   // grows with the block index): the longest CTAs start in the first wave, not in the tail
   const int nqb = gridDim.x / nbh;
@@ -130,11 +148,11 @@ attn_fwd_tc_kernel(const __grid_constant__ CUtensorMap tmK, const __grid_constan
   const int qb = causal ? (nqb - 1 - lin / nbh) : (lin / nbh);
   const int bh = lin % nbh;
   const int m0 = qb * C::BM;
-  const int row = m0 + tid;
+  const int row = m0 + mrow;
   const bool row_ok = row < N;
   const int kend = causal ? min(N, m0 + C::BM) : N;
   const int ntiles = (kend + C::BN - 1) / C::BN;
-  const int warp_last_row = m0 + warp * 32 + 31;
+  const int warp_last_row = m0 + 32 * quarter + RPW * wsub + RPW - 1;
 
   float* sW = reinterpret_cast<float*>(sm + C::OFF_W);
   if (tid < D) sW[tid] = w[(int64_t)w_index[bh] * D + tid] * (kLog2e * rsqrtf((float)D));
@@ -148,12 +166,13 @@ attn_fwd_tc_kernel(const __grid_constant__ CUtensorMap tmK, const __grid_constan
     tmem_alloc(&tmem_slot, C::TMEM_COLS);
     tmem_relinquish();
   }
-  // q row -> fp32 registers
-  float qr[D];
+  // this thread's half of the q row -> fp32 registers
+  float qr[DH];
   {
-    const uint4* src = reinterpret_cast<const uint4*>(q + ((int64_t)bh * N + (row_ok ? row : 0)) * D);
+    const uint4* src = reinterpret_cast<const uint4*>(
+        q + ((int64_t)bh * N + (row_ok ? row : 0)) * D + dh * DH);
 #pragma unroll
-    for (int c = 0; c < D / 8; ++c) {
+    for (int c = 0; c < DH / 8; ++c) {
       uint4 v = row_ok ? src[c] : make_uint4(0, 0, 0, 0);
       U::run(v.x, qr[8 * c + 0], qr[8 * c + 1]);
       U::run(v.y, qr[8 * c + 2], qr[8 * c + 3]);
@@ -165,7 +184,7 @@ attn_fwd_tc_kernel(const __grid_constant__ CUtensorMap tmK, const __grid_constan
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = tmem_slot;
-  const uint32_t tmem_row = tmem + ((uint32_t)(warp * 32) << 16);
+  const uint32_t tmem_quarter = tmem + ((uint32_t)(quarter * 32) << 16);
 
   auto issue_tile = [&](int t) {
     const int s = t % C::STAGES;
@@ -182,7 +201,10 @@ attn_fwd_tc_kernel(const __grid_constant__ CUtensorMap tmK, const __grid_constan
     for (int t = 0; t < min(ntiles, C::STAGES - 1); ++t) issue_tile(t);
   }
 
-  float m_ref = 0.f, l = 0.f;
+  // m_ref, l and the P values are per row; both threads of a row compute the same full scores
+  // (a + b == b + a exactly), so they take identical softmax decisions. Each thread adds only
+  // its own four keys of every group to l and writes only their 8 bytes of the P chunk.
+  float m_ref = 0.f, l = 0.f, alpha_tile = 1.f;
   const uint32_t idesc = make_idesc_f16(128, D, U::is_bf16, 0, 1);
 
   for (int t = 0; t < ntiles; ++t) {
@@ -208,11 +230,12 @@ attn_fwd_tc_kernel(const __grid_constant__ CUtensorMap tmK, const __grid_constan
         float acc[8][2];
 #pragma unroll
         for (int e = 0; e < 8; ++e) acc[e][0] = acc[e][1] = 0.f;
-        const uint8_t* kg = sK + (g * 8) * D * 2;
+        const uint8_t* kg = sK + (g * 8) * D * 2 + dh * DH * 2;
+        const float4* wh = reinterpret_cast<const float4*>(sW + dh * DH);
 #pragma unroll
-        for (int c = 0; c < D / 8; ++c) {
-          const float4 w0 = reinterpret_cast<const float4*>(sW)[2 * c];
-          const float4 w1 = reinterpret_cast<const float4*>(sW)[2 * c + 1];
+        for (int c = 0; c < DH / 8; ++c) {
+          const float4 w0 = wh[2 * c];
+          const float4 w1 = wh[2 * c + 1];
 #pragma unroll
           for (int e = 0; e < 8; ++e) {
             const uint4 kk = reinterpret_cast<const uint4*>(kg + e * D * 2)[c];
@@ -233,77 +256,105 @@ attn_fwd_tc_kernel(const __grid_constant__ CUtensorMap tmK, const __grid_constan
         }
 #pragma unroll
         for (int e = 0; e < 8; ++e) {
+          // butterfly over the TPR lanes of the row: every lane ends with the same sum
+          float full = acc[e][0] + acc[e][1];
+#pragma unroll
+          for (int o = 1; o < TPR; o <<= 1) full += __shfl_xor_sync(0xffffffffu, full, o);
           const int key = jg + e;
           const bool ok = key < N && (!causal || key <= row);
-          s8[e] = ok ? (acc[e][0] + acc[e][1]) : -INFINITY;
+          s8[e] = ok ? full : -INFINITY;
         }
       }
-      if (scores != nullptr && row_ok) {
-        float* dst = scores + ((int64_t)bh * N + row) * N + jg;
+      // this thread's keys of the group: KPT dh .. KPT dh + KPT - 1
+      float sk[KPT];
 #pragma unroll
-        for (int e = 0; e < 8; ++e)
-          if (jg + e < N && (!causal || jg + e <= row)) dst[e] = s8[e] * kLn2;
+      for (int e = 0; e < KPT; ++e) {
+        sk[e] = s8[e];
+#pragma unroll
+        for (int o = 1; o < TPR; ++o)
+          if (dh == o) sk[e] = s8[KPT * o + e];
+      }
+      if (scores != nullptr && row_ok) {
+        const int k0 = jg + KPT * dh;
+        float* dst = scores + ((int64_t)bh * N + row) * N + k0;
+        if (scores_vec && k0 + KPT - 1 < N && (!causal || k0 + KPT - 1 <= row)) {
+          if constexpr (KPT == 4)
+            *reinterpret_cast<float4*>(dst) =
+                make_float4(sk[0] * kLn2, sk[1] * kLn2, sk[2] * kLn2, sk[3] * kLn2);
+          else
+            *reinterpret_cast<float2*>(dst) = make_float2(sk[0] * kLn2, sk[1] * kLn2);
+        } else {
+#pragma unroll
+          for (int e = 0; e < KPT; ++e)
+            if (k0 + e < N && (!causal || k0 + e <= row)) dst[e] = sk[e] * kLn2;
+        }
       }
       float gm = s8[0];
 #pragma unroll
       for (int e = 1; e < 8; ++e) gm = fmaxf(gm, s8[e]);
 
       // reference max: fixed by the first group of the row; raised (rarely) when a group's max
-      // exceeds it by more than the threshold
+      // exceeds it by more than the threshold. The accumulator rows in TMEM are rescaled once,
+      // at the end of the tile (alpha_tile), before the tile's MMA.
       if (t == 0 && g == 0) {
         m_ref = row_ok ? gm : 0.f;
-      } else {
-        const bool need = row_ok && gm > m_ref + kRescaleThreshold;
-        if (__any_sync(0xffffffffu, need)) {
-          const float alpha = need ? ex2_approx(m_ref - gm) : 1.f;
-          if (need) {
-            l *= alpha;
-            m_ref = gm;
-            // chunks 0..g-1 of this tile's P row were written with the old reference
-            for (int c = 0; c < g; ++c) {
-              uint4* pc = reinterpret_cast<uint4*>(sP + sw128_offset(tid, c));
-              uint4 v = *pc;
-              uint32_t* vv = reinterpret_cast<uint32_t*>(&v);
-              float lo, hi, r0, r1;
-              for (int e = 0; e < 4; ++e) {
-                U::run(vv[e], lo, hi);
-                vv[e] = U::pack(lo * alpha, hi * alpha, r0, r1);
-              }
-              *pc = v;
-            }
-          }
-          if (t > 0) {
-            // the accumulator holds tiles < t: wait for the last issued MMA (tile t-1)
-            if (!mbar_wait(&mma_bar[(t - 1) & 1], (uint32_t)((t - 1) >> 1) & 1u, kWaitLimit))
-              atomicExch(err, 2);
-            tc_fence_after();
+      } else if (row_ok && gm > m_ref + kRescaleThreshold) {
+        const float alpha = ex2_approx(m_ref - gm);
+        l *= alpha;
+        alpha_tile *= alpha;
+        m_ref = gm;
+        // this thread's pieces of chunks 0..g-1 of the tile's P row used the old reference
+        for (int c = 0; c < g; ++c) {
+          uint32_t* pc = reinterpret_cast<uint32_t*>(sP + sw128_offset(mrow, c) + 2 * KPT * dh);
 #pragma unroll
-            for (int cb = 0; cb < D / 32; ++cb) {
-              uint32_t r[32];
-              tmem_ld32(tmem_row + cb * 32, r);
-              tmem_wait_ld();
-#pragma unroll
-              for (int i = 0; i < 32; ++i) r[i] = __float_as_uint(__uint_as_float(r[i]) * alpha);
-              tmem_st32(tmem_row + cb * 32, r);
-            }
-            tmem_wait_st();
+          for (int e = 0; e < KPT / 2; ++e) {
+            float lo, hi, r0, r1;
+            U::run(pc[e], lo, hi);
+            pc[e] = U::pack(lo * alpha, hi * alpha, r0, r1);
           }
         }
       }
-      uint32_t pk[4];
+      uint32_t pk[KPT / 2];
 #pragma unroll
-      for (int e = 0; e < 4; ++e) {
-        const float p0 = row_ok ? ex2_approx(s8[2 * e] - m_ref) : 0.f;
-        const float p1 = row_ok ? ex2_approx(s8[2 * e + 1] - m_ref) : 0.f;
+      for (int e = 0; e < KPT / 2; ++e) {
+        const float p0 = row_ok ? ex2_approx(sk[2 * e] - m_ref) : 0.f;
+        const float p1 = row_ok ? ex2_approx(sk[2 * e + 1] - m_ref) : 0.f;
         float r0, r1;
         pk[e] = U::pack(p0, p1, r0, r1);
         l += r0 + r1;
       }
-      *reinterpret_cast<uint4*>(sP + sw128_offset(tid, g)) = make_uint4(pk[0], pk[1], pk[2], pk[3]);
+      uint8_t* pdst = sP + sw128_offset(mrow, g) + 2 * KPT * dh;
+      if constexpr (KPT == 4)
+        *reinterpret_cast<uint2*>(pdst) = make_uint2(pk[0], pk[1]);
+      else
+        *reinterpret_cast<uint32_t*>(pdst) = pk[0];
     }
+    if (dh == 0) sAlpha[mrow] = alpha_tile;
     fence_async_shared();
     tc_fence_before();
-    __syncthreads();
+    if (__syncthreads_or(alpha_tile != 1.f) && t > 0) {
+      // rare: some row raised its reference max in this tile. The accumulator holds tiles < t:
+      // wait for the last issued MMA (tile t-1), then warps 0-3 scale their lane quarters.
+      if (warp < 4) {
+        if (!mbar_wait(&mma_bar[(t - 1) & 1], (uint32_t)((t - 1) >> 1) & 1u, kWaitLimit))
+          atomicExch(err, 2);
+        tc_fence_after();
+        const float a = sAlpha[32 * warp + lane];
+#pragma unroll
+        for (int cb = 0; cb < D / 32; ++cb) {
+          uint32_t r[32];
+          tmem_ld32(tmem_quarter + cb * 32, r);
+          tmem_wait_ld();
+#pragma unroll
+          for (int i = 0; i < 32; ++i) r[i] = __float_as_uint(__uint_as_float(r[i]) * a);
+          tmem_st32(tmem_quarter + cb * 32, r);
+        }
+        tmem_wait_st();
+      }
+      tc_fence_before();
+      __syncthreads();
+    }
+    alpha_tile = 1.f;
 
     // ---- one thread: O += P @ V on the tensor core, then refill the freed stage ----------
     if (tid == 0) {
@@ -335,15 +386,27 @@ attn_fwd_tc_kernel(const __grid_constant__ CUtensorMap tmK, const __grid_constan
     const int tl = ntiles - 1;
     if (!mbar_wait(&mma_bar[tl & 1], (uint32_t)(tl >> 1) & 1u, kWaitLimit)) atomicExch(err, 5);
   }
-  tc_fence_after();
-  const float inv_l = (row_ok && l > 0.f) ? 1.f / l : 0.f;
-  T* orow = out + ((int64_t)bh * N + (row_ok ? row : 0)) * D;
+  float l_row = l;
 #pragma unroll
-  for (int cb = 0; cb < D / 32; ++cb) {
+  for (int o = 1; o < TPR; o <<= 1) l_row += __shfl_xor_sync(0xffffffffu, l_row, o);
+  if (dh == 0) {
+    sL[mrow] = l_row;
+    if (row_ok) lse[(int64_t)bh * N + row] = (m_ref + __log2f(l_row)) * kLn2;
+  }
+  __syncthreads();
+  tc_fence_after();
+  // warp w stores columns [DH (w / 4), DH (w / 4 + 1)) of the 32 rows of its lane quarter
+  const int orow_m = 32 * quarter + lane;
+  const bool orow_ok = m0 + orow_m < N;
+  const float lsum = sL[orow_m];
+  const float inv_l = (orow_ok && lsum > 0.f) ? 1.f / lsum : 0.f;
+  T* orow = out + ((int64_t)bh * N + (orow_ok ? m0 + orow_m : 0)) * D + wsub * DH;
+#pragma unroll
+  for (int cb = 0; cb < DH / 32; ++cb) {
     uint32_t r[32];
-    tmem_ld32(tmem_row + cb * 32, r);
+    tmem_ld32(tmem_quarter + wsub * DH + cb * 32, r);
     tmem_wait_ld();
-    if (row_ok) {
+    if (orow_ok) {
 #pragma unroll
       for (int g = 0; g < 4; ++g) {
         uint32_t pk[4];
@@ -357,7 +420,6 @@ attn_fwd_tc_kernel(const __grid_constant__ CUtensorMap tmK, const __grid_constan
       }
     }
   }
-  if (row_ok) lse[(int64_t)bh * N + row] = (m_ref + __log2f(l)) * kLn2;
   tc_fence_before();
   __syncthreads();
   if (warp == 0) tmem_dealloc(tmem, C::TMEM_COLS);
@@ -387,8 +449,12 @@ int launch_fwd_tc(const void* q, const void* k, const void* v, const float* w, c
     attr_set = true;
   }
   const unsigned grid = (unsigned)(((N + C::BM - 1) / C::BM) * BH);
-  attn_fwd_tc_kernel<D, T><<<grid, 128, C::SMEM, s>>>(tmK, tmV, (const T*)q, (T*)out, lse, scores,
-                                                      w, wi, N, causal, (int)BH, err);
+  // vector score stores (8 / TPR floats) need rows aligned to their size
+  const int kpt = 8 / C::TPR;
+  const int scores_vec = (N % kpt == 0) &&
+                         ((reinterpret_cast<uintptr_t>(scores) & (uintptr_t)(4 * kpt - 1)) == 0);
+  attn_fwd_tc_kernel<D, T><<<grid, C::THREADS, C::SMEM, s>>>(
+      tmK, tmV, (const T*)q, (T*)out, lse, scores, w, wi, N, causal, (int)BH, scores_vec, err);
   count_launches(1);
   return check_cuda(cudaGetLastError(), "attn_fwd_tc launch");
 }
