@@ -276,7 +276,7 @@ attn_fwd_tc_kernel(const __grid_constant__ CUtensorMap tmK, const __grid_constan
       }
       if (scores != nullptr && row_ok) {
         const int k0 = jg + KPT * dh;
-        float* dst = scores + ((int64_t)bh * N + row) * N + k0;
+        float* dst = scores + ((int64_t)bh * N + row) * attn_scores_ld(N) + k0;
         if (scores_vec && k0 + KPT - 1 < N && (!causal || k0 + KPT - 1 <= row)) {
           if constexpr (KPT == 4)
             *reinterpret_cast<float4*>(dst) =
@@ -449,10 +449,9 @@ int launch_fwd_tc(const void* q, const void* k, const void* v, const float* w, c
     attr_set = true;
   }
   const unsigned grid = (unsigned)(((N + C::BM - 1) / C::BM) * BH);
-  // vector score stores (8 / TPR floats) need rows aligned to their size
+  // vector score stores (8 / TPR floats) need an aligned base (rows are padded to 16 bytes)
   const int kpt = 8 / C::TPR;
-  const int scores_vec = (N % kpt == 0) &&
-                         ((reinterpret_cast<uintptr_t>(scores) & (uintptr_t)(4 * kpt - 1)) == 0);
+  const int scores_vec = (reinterpret_cast<uintptr_t>(scores) & (uintptr_t)(4 * kpt - 1)) == 0;
   attn_fwd_tc_kernel<D, T><<<grid, C::THREADS, C::SMEM, s>>>(
       tmK, tmV, (const T*)q, (T*)out, lse, scores, w, wi, N, causal, (int)BH, scores_vec, err);
   count_launches(1);
@@ -517,15 +516,20 @@ namespace {
 struct BwdCfg {
   static constexpr int D = 64, BM = 128, BN = 128;
   static constexpr int TILE = BM * D * 2;                  // 16 KB (a q or dO tile, bf16/fp16)
+  static constexpr int SC_BOX = BM * 32 * 4;               // 16 KB: scores of 128 rows x 32 keys
   static constexpr int OFF_V = 0;                          // V block [128 keys x 64] swizzled
   static constexpr int OFF_DO = OFF_V + BN * D * 2;        // 2 stages, swizzled
   static constexpr int OFF_Q = OFF_DO + 2 * TILE;          // 2 stages, plain rows
-  static constexpr int OFF_P = OFF_Q + 2 * TILE;           // 2 x 16 KB MN-major atoms
-  static constexpr int DS_LD = BN + 4;                     // row pitch (4-byte entries) of the dS tile
-  static constexpr int OFF_DS = OFF_P + BM * BN * 2;
-  static constexpr int OFF_DQ = OFF_DS + BM * DS_LD * 4;   // fp32 [128 x 64]
+  // P tile (2 x 16 KB MN-major atoms). Between the dV MMA of a tile and the P writes of the
+  // next one it holds score boxes 0-1 (keys 0-63) of the next tile; OFF_SC holds boxes 2-3.
+  static constexpr int OFF_P = OFF_Q + 2 * TILE;
+  static constexpr int OFF_SC = OFF_P + BM * BN * 2;
+  static constexpr int DS_LD = BN + 8;                     // row pitch (halves) of the dS tile
+  static constexpr int OFF_DS = OFF_SC + 2 * SC_BOX;       // fp16 [128 x DS_LD]
+  static constexpr int OFF_DQ = OFF_DS + BM * DS_LD * 2;   // fp32 [128 x 64]
   static constexpr int SMEM = OFF_DQ + BM * D * 4 + 1024;
   static constexpr int TMEM_COLS = 256;                    // dP: [0,128), dV: [128,192)
+  static_assert(OFF_P % 1024 == 0 && OFF_SC % 1024 == 0, "swizzled boxes need 1 KB alignment");
 };
 
 template <typename T>
@@ -565,10 +569,10 @@ __global__ void bwd_finish_kernel(const float* __restrict__ dq_acc, const float*
 template <typename T>
 __global__ void __launch_bounds__(512, 1)
 attn_bwd_tc_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmDO,
-                   const __grid_constant__ CUtensorMap tmV, const T* __restrict__ k,
-                   const float* __restrict__ w, const int32_t* __restrict__ w_index,
-                   const float* __restrict__ lse, const float* __restrict__ delta,
-                   const float* __restrict__ scores, float* __restrict__ dq_acc,
+                   const __grid_constant__ CUtensorMap tmV, const __grid_constant__ CUtensorMap tmSC,
+                   const T* __restrict__ k, const float* __restrict__ w,
+                   const int32_t* __restrict__ w_index, const float* __restrict__ lse,
+                   const float* __restrict__ delta, float* __restrict__ dq_acc,
                    T* __restrict__ dk, T* __restrict__ dv, float* __restrict__ dw, int N,
                    int causal, int nbh, int* __restrict__ err) {
   using namespace sm100;
@@ -579,7 +583,7 @@ attn_bwd_tc_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constan
   extern __shared__ uint8_t smem_raw[];
   uint8_t* sm = (uint8_t*)(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
   __shared__ __align__(8) uint64_t full_bar[2];
-  __shared__ __align__(8) uint64_t dp_bar, dv_bar;
+  __shared__ __align__(8) uint64_t dp_bar, dv_bar, sc_bar;
   __shared__ uint32_t tmem_slot;
 
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
@@ -600,6 +604,7 @@ attn_bwd_tc_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constan
     mbar_init(&full_bar[1], 1);
     mbar_init(&dp_bar, 1);
     mbar_init(&dv_bar, 1);
+    mbar_init(&sc_bar, 1);
     fence_mbar_init();
   }
   if (warp == 0) {
@@ -641,16 +646,28 @@ attn_bwd_tc_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constan
                make_smem_desc(b + kk * 32, 16, 1024, kSwizzle128B), idesc_dp, kk > 0 ? 1u : 0u);
     umma_commit(&dp_bar);
   };
+  // saved scores of query tile t: four swizzled boxes of 32 keys x 128 rows (OOB rows and keys
+  // read as zero and are masked in phase A); boxes 0-1 land in the P buffer, 2-3 in OFF_SC
+  auto issue_scores = [&](int t) {
+    const int q0 = (t_first + t) * C::BM;
+    mbar_arrive_expect_tx(&sc_bar, 4 * C::SC_BOX);
+#pragma unroll
+    for (int g = 0; g < 4; ++g)
+      tma_load_3d(sm + (g < 2 ? C::OFF_P : C::OFF_SC - 2 * C::SC_BOX) + g * C::SC_BOX, &tmSC,
+                  &sc_bar, kb0 + 32 * g, q0, bh);
+  };
 
   if (tid == 0) {
     tma_prefetch_desc(&tmQ);
     tma_prefetch_desc(&tmDO);
     tma_prefetch_desc(&tmV);
+    tma_prefetch_desc(&tmSC);
     // V block and the first query tile share stage 0's barrier: one arrive.expect_tx per phase
     mbar_arrive_expect_tx(&full_bar[0], C::BN * D * 2 + 2 * C::TILE);
     tma_load_3d(sm + C::OFF_V, &tmV, &full_bar[0], 0, kb0, bh);
     tma_load_3d(sm + C::OFF_DO, &tmDO, &full_bar[0], 0, t_first * C::BM, bh);
     tma_load_3d(sm + C::OFF_Q, &tmQ, &full_bar[0], 0, t_first * C::BM, bh);
+    issue_scores(0);
     if (ntiles > 1) issue_tile(1);
     if (!mbar_wait(&full_bar[0], 0, kWaitLimit)) atomicExch(err, 11);
     tc_fence_after();
@@ -661,42 +678,23 @@ attn_bwd_tc_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constan
   // phase A ownership: TMEM lane quarter (warp & 3) = query rows, key group (warp >> 2) of 32
   const int arow = 32 * (warp & 3) + lane;
   const int agrp = warp >> 2;
-  float* sDS = reinterpret_cast<float*>(sm + C::OFF_DS);
+  const uint8_t* sc_row = sm + (agrp < 2 ? C::OFF_P : C::OFF_SC - 2 * C::SC_BOX) +
+                          agrp * C::SC_BOX + arow * 128;
 
-  // phase A inputs of a tile (saved scores, lse, Delta), loaded one tile ahead
-  float sc[32], lse2 = 0.f, dlt = 0.f;
-  auto load_scores = [&](int t) {
+  // per-row phase A inputs (lse, Delta), loaded one tile ahead
+  float lse2 = 0.f, dlt = 0.f;
+  auto load_row_stats = [&](int t) {
     const int i = (t_first + t) * C::BM + arow;
-    const bool row_ok = i < N;
-    lse2 = row_ok ? lse[(int64_t)bh * N + i] * kLog2e : 0.f;
-    dlt = row_ok ? delta[(int64_t)bh * N + i] : 0.f;
-    const int key0 = kb0 + 32 * agrp;
-    const float* srow = scores + ((int64_t)bh * N + (row_ok ? i : 0)) * N + key0;
-    const bool any = row_ok && key0 < N && (!causal || key0 <= i);
-    if (any && key0 + 32 <= N && (reinterpret_cast<uintptr_t>(srow) & 15u) == 0) {
-      // 8 vector loads; unwritten (masked) entries are read but discarded below
-#pragma unroll
-      for (int c = 0; c < 8; ++c) {
-        const float4 v4 = reinterpret_cast<const float4*>(srow)[c];
-        sc[4 * c] = v4.x; sc[4 * c + 1] = v4.y; sc[4 * c + 2] = v4.z; sc[4 * c + 3] = v4.w;
-      }
-    } else {
-#pragma unroll
-      for (int e = 0; e < 32; ++e) sc[e] = (any && key0 + e < N) ? srow[e] : 0.f;
-    }
-#pragma unroll
-    for (int e = 0; e < 32; ++e) {
-      const int key = key0 + e;
-      if (!(row_ok && key < N && (!causal || key <= i))) sc[e] = -INFINITY;
-    }
+    lse2 = i < N ? lse[(int64_t)bh * N + i] * kLog2e : 0.f;
+    dlt = i < N ? delta[(int64_t)bh * N + i] : 0.f;
   };
-  load_scores(0);
+  load_row_stats(0);
 
   float dka[8][2];  // fp32 dK partials of this warp's keys over all tiles
 #pragma unroll
   for (int j = 0; j < 8; ++j) dka[j][0] = dka[j][1] = 0.f;
   float dwa0 = 0.f, dwa1 = 0.f;
-  uint32_t* sDSh = reinterpret_cast<uint32_t*>(sm + C::OFF_DS);  // dS tile as scaled {ds, ds} half2
+  __half* sDS = reinterpret_cast<__half*>(sm + C::OFF_DS);  // dS tile, scaled, fp16
 
   for (int t = 0; t < ntiles; ++t) {
     const int q0 = (t_first + t) * C::BM;
@@ -705,8 +703,25 @@ attn_bwd_tc_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constan
     if (!mbar_wait(&full_bar[st], (uint32_t)(t >> 1) & 1u, kWaitLimit)) atomicExch(err, 10);
     if (!mbar_wait(&dp_bar, (uint32_t)t & 1u, kWaitLimit)) atomicExch(err, 12);
     if (t >= 1 && !mbar_wait(&dv_bar, (uint32_t)(t - 1) & 1u, kWaitLimit)) atomicExch(err, 13);
+    if (!mbar_wait(&sc_bar, (uint32_t)t & 1u, kWaitLimit)) atomicExch(err, 17);
     tc_fence_after();
     // ---- phase A: P and dS for (row arow, keys 32*agrp .. +31) ------------------------------
+    float sc[32];
+    {
+      const int i = q0 + arow;
+#pragma unroll
+      for (int c = 0; c < 8; ++c) {
+        const float4 v4 = *reinterpret_cast<const float4*>(sc_row + ((c ^ (arow & 7)) << 4));
+        sc[4 * c] = v4.x; sc[4 * c + 1] = v4.y; sc[4 * c + 2] = v4.z; sc[4 * c + 3] = v4.w;
+      }
+#pragma unroll
+      for (int e = 0; e < 32; ++e) {
+        const int key = kb0 + 32 * agrp + e;
+        if (!(i < N && key < N && (!causal || key <= i))) sc[e] = -INFINITY;
+      }
+    }
+    // boxes 0-1 share the P buffer: every thread's scores are in registers before P is written
+    __syncthreads();
     float ds[32];
     {
       uint32_t r[32];
@@ -740,13 +755,14 @@ attn_bwd_tc_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constan
     const int ex = amax_tile > 0.f ? ilogbf(amax_tile) : 0;
     const float ds_scale = ldexpf(1.f, 8 - ex), ds_unscale = ldexpf(1.f, ex - 8);
     {
-      uint32_t* dsrow = sDSh + arow * C::DS_LD + 32 * agrp;
+      __half* dsrow = sDS + arow * C::DS_LD + 32 * agrp;
 #pragma unroll
-      for (int c = 0; c < 8; ++c) {
+      for (int c = 0; c < 4; ++c) {
         uint32_t v[4];
 #pragma unroll
         for (int e = 0; e < 4; ++e) {
-          __half2 h = __float2half2_rn(ds[4 * c + e] * ds_scale);
+          __half2 h = __floats2half2_rn(ds[8 * c + 2 * e] * ds_scale,
+                                        ds[8 * c + 2 * e + 1] * ds_scale);
           v[e] = *reinterpret_cast<uint32_t*>(&h);
         }
         reinterpret_cast<uint4*>(dsrow)[c] = make_uint4(v[0], v[1], v[2], v[3]);
@@ -756,7 +772,7 @@ attn_bwd_tc_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constan
     tc_fence_before();
     __syncthreads();
 
-    // ---- one thread: dV += P^T dO, then dP for the next tile ---------------------------------
+    // ---- one thread: dV += P^T dO, dP for the next tile, the next tile's scores -------------
     if (tid == 0) {
       tc_fence_after();
       const uint32_t pa = smem_u32(sm + C::OFF_P);
@@ -772,34 +788,56 @@ attn_bwd_tc_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constan
           atomicExch(err, 14);
         tc_fence_after();
         issue_dp(t + 1);
+        // the P buffer is free once the dV MMA of this tile has read it
+        if (!mbar_wait(&dv_bar, (uint32_t)t & 1u, kWaitLimit)) atomicExch(err, 18);
+        fence_async_shared();
+        issue_scores(t + 1);
       }
     }
     __syncwarp();
-    // next tile's phase-A inputs: global loads in flight during the tanh grid below
-    if (t + 1 < ntiles) load_scores(t + 1);
+    // next tile's lse and Delta: global loads in flight during the tanh grid below
+    if (t + 1 < ntiles) load_row_stats(t + 1);
 
     // ---- phase B: the tanh grid, packed f16x2 (lane = head dims 2l, 2l+1) ----------------------
+    // Rows are software-pipelined: the tanh of row r + 1 is issued before the sums of row r, so
+    // the MUFU queue stays fed across the per-row reductions.
     {
       const uint32_t* sQ = reinterpret_cast<const uint32_t*>(sm + C::OFF_Q + st * C::TILE);
       const int key_lo = kb0 + warp * 8;
       const int rmax = min(C::BM, N - q0);
+      // causal: rows r < key_lo - q0 mask every key of this warp
+      const int r_lo = causal ? max(0, key_lo - q0) : 0;
       const __half2 hz = __floats2half2_rn(0.f, 0.f);
       __half2 dk2[8];
 #pragma unroll
       for (int j = 0; j < 8; ++j) dk2[j] = hz;
       int pending = 0;  // rows accumulated in dk2 since the last flush
+      __half2 tn[8];
+      if (r_lo < rmax) {
+        const __half2 q2 = to_h2<T>(sQ[r_lo * (D / 2) + lane]);
+#pragma unroll
+        for (int j = 0; j < 8; ++j) tn[j] = tanh_h2(__hadd2(q2, kr[j]));
+      }
 #pragma unroll 1
-      for (int r = 0; r < rmax; ++r) {
-        if (causal && key_lo > q0 + r) continue;  // every key of this warp is masked for row r
-        const __half2 q2 = to_h2<T>(sQ[r * (D / 2) + lane]);
-        const uint4* dsr = reinterpret_cast<const uint4*>(sDSh + r * C::DS_LD + warp * 8);
-        const uint4 a4 = dsr[0], b4 = dsr[1];
-        const uint32_t dsu[8] = {a4.x, a4.y, a4.z, a4.w, b4.x, b4.y, b4.z, b4.w};
+      for (int r = r_lo; r < rmax; ++r) {
+        __half2 tc[8];
+#pragma unroll
+        for (int j = 0; j < 8; ++j) tc[j] = tn[j];
+        const uint4 dsv = *reinterpret_cast<const uint4*>(sDS + r * C::DS_LD + warp * 8);
+        {
+          // the last row recomputes itself rather than branch
+          const int rn = min(r + 1, rmax - 1);
+          const __half2 qn = to_h2<T>(sQ[rn * (D / 2) + lane]);
+#pragma unroll
+          for (int j = 0; j < 8; ++j) tn[j] = tanh_h2(__hadd2(qn, kr[j]));
+        }
+        const uint32_t dsu[4] = {dsv.x, dsv.y, dsv.z, dsv.w};
         __half2 dq2 = hz, dw2 = hz;
 #pragma unroll
         for (int j = 0; j < 8; ++j) {
-          const __half2 d2 = *reinterpret_cast<const __half2*>(&dsu[j]);
-          const __half2 t2 = tanh_h2(__hadd2(q2, kr[j]));
+          const __half2 dpair = *reinterpret_cast<const __half2*>(&dsu[j >> 1]);
+          const __half2 d2 = (j & 1) ? __high2half2(dpair) : __low2half2(dpair);
+          const __half2 t2 = tc[j];
           const __half2 u2 = __hmul2(d2, t2);
           const __half2 g2 = __hfma2(__hneg2(u2), t2, d2);
           dq2 = __hadd2(dq2, g2);
@@ -907,11 +945,21 @@ int launch_bwd_tc(const void* q, const void* k, const void* v, const float* w, c
   const uint64_t dims[3] = {64, (uint64_t)N, (uint64_t)BH};
   const uint64_t strides[2] = {128, (uint64_t)N * 128};
   const uint32_t box[3] = {64, 128, 1};
-  CUtensorMap tmQ, tmDO, tmV;
+  CUtensorMap tmQ, tmDO, tmV, tmSC;
   int st = make_tmap(&tmQ, q, dt, 3, dims, strides, box, CU_TENSOR_MAP_SWIZZLE_NONE);
   if (st == FLB_OK) st = make_tmap(&tmDO, dout, dt, 3, dims, strides, box, CU_TENSOR_MAP_SWIZZLE_128B);
   if (st == FLB_OK) st = make_tmap(&tmV, v, dt, 3, dims, strides, box, CU_TENSOR_MAP_SWIZZLE_128B);
   if (st != FLB_OK) return st;
+  {
+    // saved scores [BH, N, ld] fp32, boxes of 32 keys (128 bytes, swizzled) x 128 rows
+    const uint64_t ld = (uint64_t)attn_scores_ld(N);
+    const uint64_t sdims[3] = {(uint64_t)N, (uint64_t)N, (uint64_t)BH};
+    const uint64_t sstrides[2] = {ld * 4, (uint64_t)N * ld * 4};
+    const uint32_t sbox[3] = {32, 128, 1};
+    st = make_tmap(&tmSC, scores, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 3, sdims, sstrides, sbox,
+                   CU_TENSOR_MAP_SWIZZLE_128B);
+    if (st != FLB_OK) return st;
+  }
   uint8_t* wsb = reinterpret_cast<uint8_t*>(ws);
   int* err = reinterpret_cast<int*>(wsb);
   float* delta = reinterpret_cast<float*>(wsb + 256);
@@ -929,8 +977,8 @@ int launch_bwd_tc(const void* q, const void* k, const void* v, const float* w, c
     attr_set = true;
   }
   const unsigned grid = (unsigned)(((N + C::BN - 1) / C::BN) * BH);
-  attn_bwd_tc_kernel<T><<<grid, 512, C::SMEM, s>>>(tmQ, tmDO, tmV, (const T*)k, w, wi, lse, delta,
-                                                   scores, dq_acc, (T*)dk, (T*)dv, dw, N, causal,
+  attn_bwd_tc_kernel<T><<<grid, 512, C::SMEM, s>>>(tmQ, tmDO, tmV, tmSC, (const T*)k, w, wi, lse,
+                                                   delta, dq_acc, (T*)dk, (T*)dv, dw, N, causal,
                                                    (int)BH, err);
   bwd_finish_kernel<T><<<(unsigned)((rows * 32 + 255) / 256), 256, 0, s>>>(dq_acc, w, wi, (T*)dq, N,
                                                                            rows);

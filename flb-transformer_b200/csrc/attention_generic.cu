@@ -67,7 +67,7 @@ attn_fwd_generic_kernel(const T* __restrict__ q, const T* __restrict__ k, const 
     }
     float s = transpose_reduce32(part);
     const bool valid = (j0 + lane) < jmax;
-    if (scores != nullptr && valid) scores[row * (int64_t)N + j0 + lane] = s;
+    if (scores != nullptr && valid) scores[row * attn_scores_ld(N) + j0 + lane] = s;
     s = valid ? s : -INFINITY;
     const float m_new = fmaxf(m, warp_max(s));
     const float alpha = exp_f<EXACT>(m - m_new);

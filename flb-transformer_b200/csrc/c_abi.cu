@@ -95,6 +95,8 @@ const char* flb_last_error(void) { return g_last_error.c_str(); }
 const char* flb_version(void) { return "flb_b200 0.1 (sm_100a)"; }
 uint64_t flb_launch_count(void) { return g_launches.load(std::memory_order_relaxed); }
 
+int64_t flb_attn_scores_ld(int64_t N) { return N < 0 ? 0 : attn_scores_ld(N); }
+
 size_t flb_attn_fwd_workspace_bytes(int64_t BH, int64_t N, int64_t D, int dtype, int flags) {
   if (attn_fwd_fast_supported(BH, N, D, dtype, flags))
     return attn_fwd_fast_workspace(BH, N, D, dtype, flags);

@@ -26,6 +26,10 @@ inline int dtype_size(int dtype) {
   }
 }
 
+// Row pitch (floats) of the saved attention scores [BH, N, ld]: rows padded to 16 bytes, the
+// stride alignment TMA needs.
+__host__ __device__ inline int64_t attn_scores_ld(int64_t N) { return (N + 3) & ~(int64_t)3; }
+
 inline int num_sms() {
   static int n = 0;
   if (n == 0) {

@@ -40,7 +40,8 @@ PROTOTYPES = {
     "flb_attn_fwd": (_i32, [_vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _i64, _i64, _i64, _i32,
                             _i32, _vp, _sz, _vp]),
     "flb_attn_fwd_workspace_bytes": (_sz, [_i64, _i64, _i64, _i32, _i32]),
-    "flb_attn_bwd": (_i32, [_vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp,
+    "flb_attn_scores_ld": (_i64, [_i64]),
+    "flb_attn_bwd":(_i32, [_vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp,
                             _i64, _i64, _i64, _i64, _i32, _i32, _vp, _sz, _vp]),
     "flb_attn_bwd_workspace_bytes": (_sz, [_i64, _i64, _i64, _i32, _i32]),
     "flb_wf_gather": (_i32, [_vp, _i64p, _vp, _i64p, _vp, _vp, _vp, _vp, _i64, _i64, _vp, _i64p,

@@ -55,7 +55,7 @@ def _flags(causal: bool, exact: bool, force_generic: bool = False) -> int:
 def attention_forward(q, k, v, v_a, causal=False, exact=False, force_generic=False,
                       save_scores=False):
     """Run flb_attn_fwd. Returns (out [..,H,N,D], lse float32 [BH, N], w_table, w_index,
-    scores float32 [BH, N, N] or None)."""
+    scores float32 [BH, N, flb_attn_scores_ld(N)] or None; columns >= N are padding)."""
     nat.require_cuda(q, k, v, v_a)
     if not (q.shape == k.shape == v.shape):
         raise ValueError(f"q, k, v shapes differ: {tuple(q.shape)} {tuple(k.shape)} {tuple(v.shape)}")
@@ -70,7 +70,8 @@ def attention_forward(q, k, v, v_a, causal=False, exact=False, force_generic=Fal
     table, idx = _w_table(v_a, q)
     out = torch.empty_like(qf)
     lse = torch.empty((BH, N), dtype=torch.float32, device=q.device)
-    scores = (torch.empty((BH, N, N), dtype=torch.float32, device=q.device)
+    scores = (torch.empty((BH, N, int(nat.lib.flb_attn_scores_ld(N))), dtype=torch.float32,
+                          device=q.device)
               if save_scores else None)
     dt = nat.dtype_code(q.dtype)
     flags = _flags(causal, exact, force_generic)

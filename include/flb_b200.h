@@ -63,9 +63,10 @@ uint64_t flb_launch_count(void);
 
 /* Replaces FusedAdditiveAttentionFunc.forward + fused_additive_attention_kernel
  * (kernels/additive_attention.py:137-181 and :10-86). Scale 1/sqrt(D) as at :66,:145.
- * scores: optional float32 [BH, N, N] output of the scaled scores s[i,j] (entries with j > i
- * are left unwritten when causal). When the backward is going to run, saving them lets it
- * skip the score recomputation (one full tanh pass); NULL = do not save.
+ * scores: optional float32 [BH, N, flb_attn_scores_ld(N)] output of the scaled scores s[i,j]
+ * (row pitch padded to 16 bytes; padding and, when causal, entries with j > i are left
+ * unwritten). When the backward is going to run, saving them lets it skip the score
+ * recomputation (one full tanh pass); NULL = do not save.
  * Workspace: flb_attn_fwd_workspace_bytes(); may be NULL when that returns 0. */
 int flb_attn_fwd(const void* q, const void* k, const void* v,
                  const float* w, const int32_t* w_index,
@@ -75,12 +76,17 @@ int flb_attn_fwd(const void* q, const void* k, const void* v,
 
 size_t flb_attn_fwd_workspace_bytes(int64_t BH, int64_t N, int64_t D, int dtype, int flags);
 
+/* Row pitch, in floats, of the saved scores: N rounded up to a multiple of 4 (16-byte rows, as
+ * the backward's TMA loads need). No reference counterpart (the reference saves no scores). */
+int64_t flb_attn_scores_ld(int64_t N);
+
 /* Replaces FusedAdditiveAttentionFunc.backward -> compiled_backward_math
  * (kernels/additive_attention.py:188-198 and :91-130).
  * Inputs q,k,v,out,lse,dout as produced by flb_attn_fwd; outputs dq,dk,dv in `dtype`
  * ([BH,N,D], overwritten) and dw, a float32 [n_w_rows, D] table that is ACCUMULATED into
  * (caller zeroes it), matching the reduction of grad_va over broadcast dims (:126-128).
- * scores: the [BH, N, N] scores saved by flb_attn_fwd, or NULL to recompute them.
+ * scores: the [BH, N, flb_attn_scores_ld(N)] scores saved by flb_attn_fwd, or NULL to
+ * recompute them.
  * Workspace: flb_attn_bwd_workspace_bytes(). */
 int flb_attn_bwd(const void* q, const void* k, const void* v,
                  const float* w, const int32_t* w_index,
