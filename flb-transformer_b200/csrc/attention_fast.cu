@@ -720,6 +720,16 @@ attn_bwd_tc_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constan
         if (!(i < N && key < N && (!causal || key <= i))) sc[e] = -INFINITY;
       }
     }
+    if constexpr (U::is_bf16) {
+      // phase B adds q + k in f16x2: convert this tile's Q rows in place, once
+      uint32_t* q32 = reinterpret_cast<uint32_t*>(sm + C::OFF_Q + st * C::TILE);
+#pragma unroll
+      for (int i = tid; i < C::BM * D / 2; i += NT) {
+        const __half2 h = to_h2<T>(q32[i]);
+        q32[i] = *reinterpret_cast<const uint32_t*>(&h);
+      }
+      fence_async_shared();  // the stage is refilled by TMA later
+    }
     // boxes 0-1 share the P buffer: every thread's scores are in registers before P is written
     __syncthreads();
     float ds[32];
@@ -799,10 +809,11 @@ attn_bwd_tc_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constan
     if (t + 1 < ntiles) load_row_stats(t + 1);
 
     // ---- phase B: the tanh grid, packed f16x2 (lane = head dims 2l, 2l+1) ----------------------
-    // Rows are software-pipelined: the tanh of row r + 1 is issued before the sums of row r, so
-    // the MUFU queue stays fed across the per-row reductions.
+    // Rows are software-pipelined over two register buffers: the tanh of the next row is issued
+    // before the sums of the current one, so the MUFU queue stays fed across the per-row
+    // reductions. The Q tile holds f16x2 pairs here (converted in place in phase A).
     {
-      const uint32_t* sQ = reinterpret_cast<const uint32_t*>(sm + C::OFF_Q + st * C::TILE);
+      const __half2* sQh = reinterpret_cast<const __half2*>(sm + C::OFF_Q + st * C::TILE);
       const int key_lo = kb0 + warp * 8;
       const int rmax = min(C::BM, N - q0);
       // causal: rows r < key_lo - q0 mask every key of this warp
@@ -812,44 +823,29 @@ attn_bwd_tc_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constan
 #pragma unroll
       for (int j = 0; j < 8; ++j) dk2[j] = hz;
       int pending = 0;  // rows accumulated in dk2 since the last flush
-      __half2 tn[8];
-      if (r_lo < rmax) {
-        const __half2 q2 = to_h2<T>(sQ[r_lo * (D / 2) + lane]);
+      auto tanh_row = [&](int rr, __half2 (&tt)[8]) {
+        const __half2 q2 = sQh[rr * (D / 2) + lane];
 #pragma unroll
-        for (int j = 0; j < 8; ++j) tn[j] = tanh_h2(__hadd2(q2, kr[j]));
-      }
-#pragma unroll 1
-      for (int r = r_lo; r < rmax; ++r) {
-        __half2 tc[8];
-#pragma unroll
-        for (int j = 0; j < 8; ++j) tc[j] = tn[j];
-        const uint4 dsv = *reinterpret_cast<const uint4*>(sDS + r * C::DS_LD + warp * 8);
-        {
-          // the last row recomputes itself rather than branch
-          const int rn = min(r + 1, rmax - 1);
-          const __half2 qn = to_h2<T>(sQ[rn * (D / 2) + lane]);
-#pragma unroll
-          for (int j = 0; j < 8; ++j) tn[j] = tanh_h2(__hadd2(qn, kr[j]));
-        }
+        for (int j = 0; j < 8; ++j) tt[j] = tanh_h2(__hadd2(q2, kr[j]));
+      };
+      auto sums_row = [&](int rr, const __half2 (&tt)[8], __half2& dw2) {
+        const uint4 dsv = *reinterpret_cast<const uint4*>(sDS + rr * C::DS_LD + warp * 8);
         const uint32_t dsu[4] = {dsv.x, dsv.y, dsv.z, dsv.w};
-        __half2 dq2 = hz, dw2 = hz;
+        __half2 dq2 = hz;
 #pragma unroll
         for (int j = 0; j < 8; ++j) {
           const __half2 dpair = *reinterpret_cast<const __half2*>(&dsu[j >> 1]);
           const __half2 d2 = (j & 1) ? __high2half2(dpair) : __low2half2(dpair);
-          const __half2 t2 = tc[j];
-          const __half2 u2 = __hmul2(d2, t2);
-          const __half2 g2 = __hfma2(__hneg2(u2), t2, d2);
+          const __half2 u2 = __hmul2(d2, tt[j]);
+          const __half2 g2 = __hfma2(__hneg2(u2), tt[j], d2);
           dq2 = __hadd2(dq2, g2);
           dk2[j] = __hadd2(dk2[j], g2);
           dw2 = __hadd2(dw2, u2);
         }
-        const float2 dqf = __half22float2(dq2), dwf = __half22float2(dw2);
+        const float2 dqf = __half22float2(dq2);
         // dQ partials: layout [row][c * 32 + lane] for head dim 2 * lane + c (conflict-free)
-        red_shared_f32(&sDQ[r * D + lane], dqf.x * ds_unscale);
-        red_shared_f32(&sDQ[r * D + 32 + lane], dqf.y * ds_unscale);
-        dwa0 = fmaf(dwf.x, ds_unscale, dwa0);
-        dwa1 = fmaf(dwf.y, ds_unscale, dwa1);
+        red_shared_f32(&sDQ[rr * D + lane], dqf.x * ds_unscale);
+        red_shared_f32(&sDQ[rr * D + 32 + lane], dqf.y * ds_unscale);
         if (++pending == 32) {
 #pragma unroll
           for (int j = 0; j < 8; ++j) {
@@ -860,6 +856,23 @@ attn_bwd_tc_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constan
           }
           pending = 0;
         }
+      };
+      __half2 ta[8], tb[8];
+      if (r_lo < rmax) tanh_row(r_lo, ta);
+      // two rows per iteration; near the end the clamped row index recomputes the last row
+      // rather than branch
+#pragma unroll 1
+      for (int r = r_lo; r < rmax; r += 2) {
+        __half2 dw2 = hz;  // dw over both rows: |sum| <= 16 * 512, inside fp16's range
+        tanh_row(min(r + 1, rmax - 1), tb);
+        sums_row(r, ta, dw2);
+        if (r + 1 < rmax) {
+          tanh_row(min(r + 2, rmax - 1), ta);
+          sums_row(r + 1, tb, dw2);
+        }
+        const float2 dwf = __half22float2(dw2);
+        dwa0 = fmaf(dwf.x, ds_unscale, dwa0);
+        dwa1 = fmaf(dwf.y, ds_unscale, dwa1);
       }
 #pragma unroll
       for (int j = 0; j < 8; ++j) {
