@@ -828,25 +828,48 @@ attn_bwd_tc_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constan
 #pragma unroll
         for (int j = 0; j < 8; ++j) tt[j] = tanh_h2(__hadd2(q2, kr[j]));
       };
-      auto sums_row = [&](int rr, const __half2 (&tt)[8], __half2& dw2) {
+      // per row: g = dS (1 - t^2) into dQ (summed over the warp's keys) and dK (per key, over
+      // rows); u = dS t into dw. Row sums are pairwise trees (short dependency chains).
+      auto sums_row = [&](int rr, const __half2 (&tt)[8]) -> __half2 {
         const uint4 dsv = *reinterpret_cast<const uint4*>(sDS + rr * C::DS_LD + warp * 8);
         const uint32_t dsu[4] = {dsv.x, dsv.y, dsv.z, dsv.w};
-        __half2 dq2 = hz;
+        __half2 g2[8], u2[8];
 #pragma unroll
         for (int j = 0; j < 8; ++j) {
           const __half2 dpair = *reinterpret_cast<const __half2*>(&dsu[j >> 1]);
           const __half2 d2 = (j & 1) ? __high2half2(dpair) : __low2half2(dpair);
-          const __half2 u2 = __hmul2(d2, tt[j]);
-          const __half2 g2 = __hfma2(__hneg2(u2), tt[j], d2);
-          dq2 = __hadd2(dq2, g2);
-          dk2[j] = __hadd2(dk2[j], g2);
-          dw2 = __hadd2(dw2, u2);
+          u2[j] = __hmul2(d2, tt[j]);
+          g2[j] = __hfma2(__hneg2(u2[j]), tt[j], d2);
+          dk2[j] = __hadd2(dk2[j], g2[j]);
         }
+        const __half2 dq2 = __hadd2(__hadd2(__hadd2(g2[0], g2[1]), __hadd2(g2[2], g2[3])),
+                                    __hadd2(__hadd2(g2[4], g2[5]), __hadd2(g2[6], g2[7])));
         const float2 dqf = __half22float2(dq2);
-        // dQ partials: layout [row][c * 32 + lane] for head dim 2 * lane + c (conflict-free)
-        red_shared_f32(&sDQ[rr * D + lane], dqf.x * ds_unscale);
-        red_shared_f32(&sDQ[rr * D + 32 + lane], dqf.y * ds_unscale);
-        if (++pending == 32) {
+        // dQ partials (scaled; the flush unscales): layout [row][c * 32 + lane] for head dim
+        // 2 * lane + c (conflict-free)
+        red_shared_f32(&sDQ[rr * D + lane], dqf.x);
+        red_shared_f32(&sDQ[rr * D + 32 + lane], dqf.y);
+        return __hadd2(__hadd2(__hadd2(u2[0], u2[1]), __hadd2(u2[2], u2[3])),
+                       __hadd2(__hadd2(u2[4], u2[5]), __hadd2(u2[6], u2[7])));
+      };
+      __half2 ta[8], tb[8];
+      if (r_lo < rmax) tanh_row(r_lo, ta);
+      // two rows per iteration; near the end the clamped row index recomputes the last row
+      // rather than branch
+#pragma unroll 1
+      for (int r = r_lo; r < rmax; r += 2) {
+        tanh_row(min(r + 1, rmax - 1), tb);
+        __half2 dw2 = sums_row(r, ta);  // dw over both rows: |sum| <= 16 * 512, fp16's range
+        if (r + 1 < rmax) {
+          tanh_row(min(r + 2, rmax - 1), ta);
+          dw2 = __hadd2(dw2, sums_row(r + 1, tb));
+        }
+        const float2 dwf = __half22float2(dw2);
+        dwa0 = fmaf(dwf.x, ds_unscale, dwa0);
+        dwa1 = fmaf(dwf.y, ds_unscale, dwa1);
+        // dk2 holds at most 32 rows: |sum| <= 32 * 512
+        pending += 2;
+        if (pending >= 32) {
 #pragma unroll
           for (int j = 0; j < 8; ++j) {
             const float2 f = __half22float2(dk2[j]);
@@ -856,23 +879,6 @@ attn_bwd_tc_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constan
           }
           pending = 0;
         }
-      };
-      __half2 ta[8], tb[8];
-      if (r_lo < rmax) tanh_row(r_lo, ta);
-      // two rows per iteration; near the end the clamped row index recomputes the last row
-      // rather than branch
-#pragma unroll 1
-      for (int r = r_lo; r < rmax; r += 2) {
-        __half2 dw2 = hz;  // dw over both rows: |sum| <= 16 * 512, inside fp16's range
-        tanh_row(min(r + 1, rmax - 1), tb);
-        sums_row(r, ta, dw2);
-        if (r + 1 < rmax) {
-          tanh_row(min(r + 2, rmax - 1), ta);
-          sums_row(r + 1, tb, dw2);
-        }
-        const float2 dwf = __half22float2(dw2);
-        dwa0 = fmaf(dwf.x, ds_unscale, dwa0);
-        dwa1 = fmaf(dwf.y, ds_unscale, dwa1);
       }
 #pragma unroll
       for (int j = 0; j < 8; ++j) {
@@ -889,7 +895,7 @@ attn_bwd_tc_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constan
       for (int e = tid; e < rows * D; e += NT) {
         const int rr = e / D, d = e % D;
         float* src = &sDQ[rr * D + (d & 1) * 32 + (d >> 1)];
-        atomicAdd(dst + e, *src);
+        atomicAdd(dst + e, *src * ds_unscale);
         *src = 0.f;
       }
       if (tid == 0) s_amax = 0u;
