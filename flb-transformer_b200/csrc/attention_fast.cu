@@ -823,15 +823,18 @@ attn_bwd_tc_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constan
 #pragma unroll
       for (int j = 0; j < 8; ++j) dk2[j] = hz;
       int pending = 0;  // rows accumulated in dk2 since the last flush
-      auto tanh_row = [&](int rr, __half2 (&tt)[8]) {
-        const __half2 q2 = sQh[rr * (D / 2) + lane];
+      // rows are addressed through running pointers (row strides: Q 32 half2, dS DS_LD halves,
+      // dQ partials D floats)
+      constexpr int DS_ROW = C::DS_LD / 8;  // uint4 per dS row
+      auto tanh_row = [&](const __half2* qp, __half2 (&tt)[8]) {
+        const __half2 q2 = *qp;
 #pragma unroll
         for (int j = 0; j < 8; ++j) tt[j] = tanh_h2(__hadd2(q2, kr[j]));
       };
       // per row: g = dS (1 - t^2) into dQ (summed over the warp's keys) and dK (per key, over
       // rows); u = dS t into dw. Row sums are pairwise trees (short dependency chains).
-      auto sums_row = [&](int rr, const __half2 (&tt)[8]) -> __half2 {
-        const uint4 dsv = *reinterpret_cast<const uint4*>(sDS + rr * C::DS_LD + warp * 8);
+      auto sums_row = [&](const uint4* dsp, float* dqp, const __half2 (&tt)[8]) -> __half2 {
+        const uint4 dsv = *dsp;
         const uint32_t dsu[4] = {dsv.x, dsv.y, dsv.z, dsv.w};
         __half2 g2[8], u2[8];
 #pragma unroll
@@ -847,23 +850,30 @@ attn_bwd_tc_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constan
         const float2 dqf = __half22float2(dq2);
         // dQ partials (scaled; the flush unscales): layout [row][c * 32 + lane] for head dim
         // 2 * lane + c (conflict-free)
-        red_shared_f32(&sDQ[rr * D + lane], dqf.x);
-        red_shared_f32(&sDQ[rr * D + 32 + lane], dqf.y);
+        red_shared_f32(dqp, dqf.x);
+        red_shared_f32(dqp + 32, dqf.y);
         return __hadd2(__hadd2(__hadd2(u2[0], u2[1]), __hadd2(u2[2], u2[3])),
                        __hadd2(__hadd2(u2[4], u2[5]), __hadd2(u2[6], u2[7])));
       };
+      const __half2* qp = sQh + r_lo * (D / 2) + lane;
+      const uint4* dsp = reinterpret_cast<const uint4*>(sDS + warp * 8) + r_lo * DS_ROW;
+      float* dqp = sDQ + r_lo * D + lane;
       __half2 ta[8], tb[8];
-      if (r_lo < rmax) tanh_row(r_lo, ta);
-      // two rows per iteration; near the end the clamped row index recomputes the last row
+      if (r_lo < rmax) tanh_row(qp, ta);
+      // two rows per iteration; near the end the clamped row offset recomputes the last row
       // rather than branch
 #pragma unroll 1
       for (int r = r_lo; r < rmax; r += 2) {
-        tanh_row(min(r + 1, rmax - 1), tb);
-        __half2 dw2 = sums_row(r, ta);  // dw over both rows: |sum| <= 16 * 512, fp16's range
-        if (r + 1 < rmax) {
-          tanh_row(min(r + 2, rmax - 1), ta);
-          dw2 = __hadd2(dw2, sums_row(r + 1, tb));
+        const bool two = r + 1 < rmax, three = r + 2 < rmax;
+        tanh_row(qp + (two ? D / 2 : 0), tb);
+        __half2 dw2 = sums_row(dsp, dqp, ta);  // dw over both rows: |sum| <= 16 * 512
+        if (two) {
+          tanh_row(qp + (three ? D : D / 2), ta);
+          dw2 = __hadd2(dw2, sums_row(dsp + DS_ROW, dqp + D, tb));
         }
+        qp += D;
+        dsp += 2 * DS_ROW;
+        dqp += 2 * D;
         const float2 dwf = __half22float2(dw2);
         dwa0 = fmaf(dwf.x, ds_unscale, dwa0);
         dwa1 = fmaf(dwf.y, ds_unscale, dwa1);
