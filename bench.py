@@ -315,7 +315,8 @@ def extra_engine(device, steps=2, warmup=1):
     """The engine API on a 64x64 grid of per-row tanh cells (batch 32, hidden 256, bf16, x at
     row 0 as in the reference engine), forward + backward: the persistent kernels (fast path)
     against the per-diagonal tick loop (the reference's schedule: one host tick per
-    anti-diagonal with gather, vmapped cell and scatter), same inputs and weights."""
+    anti-diagonal with gather, vmapped cell and scatter), eager and replayed as CUDA graphs
+    (GraphedWavefrontEngine), same inputs and weights."""
     import torch.nn as nn
     from wavefront import WavefrontConfig, WavefrontEngine
     from wavefront.grid_layer import TanhGridCell
@@ -332,12 +333,14 @@ def extra_engine(device, steps=2, warmup=1):
     tick.load_state_dict(fast.state_dict())
     x = torch.randn(B, C, H, device=device).bfloat16()
     res = {}
-    for name, layers, n in (("persistent", fast, steps), ("per_diagonal", tick, 1)):
+    for name, layers, n in (("persistent", fast, steps), ("per_diagonal", tick, 1),
+                            ("per_diagonal_graphed", tick, steps)):
         eng = WavefrontEngine(cfg, layers).to(device)
+        run = eng.graphed(x) if name == "per_diagonal_graphed" else eng
 
         def step():
             xx = x.detach().requires_grad_(True)
-            g = eng(xx)
+            g = run(xx)
             (g[0].float().sum() + g[1][-1].float().sum()).backward()
         for _ in range(warmup):
             step()
@@ -345,7 +348,9 @@ def extra_engine(device, steps=2, warmup=1):
     return {"workload": "WavefrontEngine 64x64 per-row tanh cells, batch32 hidden256 bf16 fwd+bwd",
             "persistent_ms": round(res["persistent"], 3),
             "per_diagonal_ms": round(res["per_diagonal"], 3),
+            "per_diagonal_graphed_ms": round(res["per_diagonal_graphed"], 3),
             "speedup": res["per_diagonal"] / res["persistent"],
+            "graph_speedup": res["per_diagonal"] / res["per_diagonal_graphed"],
             "cells_per_s": R * C / (res["persistent"] * 1e-3)}
 
 

@@ -126,23 +126,33 @@ class TanhGridCell(nn.Module):
 _FAST_DEPS = [((-1, 0), 0), ((0, -1), 1)]
 
 
-def engine_fast_path(engine, x, initial_states):
-    """Run `engine` as the persistent grid kernels when its configuration is the tanh grid cell
-    the kernels implement; return None to fall back to the per-tick engine."""
+def fast_path_applies(engine, x) -> bool:
+    """Whether `engine(x)` runs as the persistent grid kernels: the tanh grid cell the kernels
+    implement, its two dependencies, bf16 compute, hidden 128/256, batch 16-64."""
     cfg = engine.config
     layers = list(engine.layers)
     # exactly this cell type: a subclass may change forward(), which the kernels would not see
     if not layers or not all(type(l) is TanhGridCell for l in layers):
-        return None
+        return False
     deps = [(tuple(o), p) for o, p in cfg.dependencies]
     if deps != _FAST_DEPS or cfg.num_ports != 2 or len(cfg.grid_shape) != 2:
-        return None
+        return False
     compute = torch.get_autocast_dtype("cuda") if torch.is_autocast_enabled("cuda") else x.dtype
     R, C = cfg.grid_shape
     Bsz, H = x.shape[0], cfg.dim
-    if (compute != torch.bfloat16 or H not in (128, 256) or Bsz not in (16, 32, 48, 64)
-            or tuple(x.shape) != (Bsz, C, H) or len(layers) != R):
+    return (compute == torch.bfloat16 and H in (128, 256) and Bsz in (16, 32, 48, 64)
+            and tuple(x.shape) == (Bsz, C, H) and len(layers) == R)
+
+
+def engine_fast_path(engine, x, initial_states):
+    """Run `engine` as the persistent grid kernels when its configuration is the tanh grid cell
+    the kernels implement; return None to fall back to the per-tick engine."""
+    if not fast_path_applies(engine, x):
         return None
+    cfg = engine.config
+    layers = list(engine.layers)
+    R, C = cfg.grid_shape
+    Bsz, H = x.shape[0], cfg.dim
     # initial_states reach no cell in the reference engine (its routing map never points into
     # the boundary dock), so they do not change the result; they are not differentiated here.
     W_l = torch.stack([l.W_l for l in layers])

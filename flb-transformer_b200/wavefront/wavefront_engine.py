@@ -35,6 +35,24 @@ import flb_native as nat
 import wavefront_backend
 
 
+def refresh_stacked_params(layers, stacked_params) -> None:
+    """Copy the layers' live parameters into the engine's stacked [num_layers, ...] copies."""
+    with torch.no_grad():
+        live, _ = stack_module_state(list(layers))
+        if live:
+            torch._foreach_copy_(list(stacked_params.values()), list(live.values()))
+
+
+def layer_grad_accumulators(ws, stacked_params, num_layers, device) -> dict:
+    """float32 [num_layers, *param] gradient accumulators, created once per workspace."""
+    if "layer_grad_accumulators" not in ws:
+        ws["layer_grad_accumulators"] = {
+            k: torch.zeros((num_layers,) + v.shape[1:], dtype=torch.float32, device=device)
+            for k, v in stacked_params.items()
+        }
+    return ws["layer_grad_accumulators"]
+
+
 class WavefrontEngineFunction(torch.autograd.Function):
     @staticmethod
     @custom_fwd(device_type="cuda")
@@ -56,10 +74,7 @@ class WavefrontEngineFunction(torch.autograd.Function):
         static_x = graph_workspace["static_x"]
         static_stacked_grids = graph_workspace["static_stacked_grids"]
 
-        with torch.no_grad():
-            live, _ = stack_module_state(list(layers))
-            if live:
-                torch._foreach_copy_(list(stacked_params.values()), list(live.values()))
+        refresh_stacked_params(layers, stacked_params)
         static_x.copy_(x)
 
         with torch.no_grad():
@@ -82,12 +97,7 @@ class WavefrontEngineFunction(torch.autograd.Function):
         num_layers = config.grid_shape[0]
         ws = ctx.graph_workspace
 
-        if "layer_grad_accumulators" not in ws:
-            ws["layer_grad_accumulators"] = {
-                k: torch.zeros((num_layers,) + v.shape[1:], dtype=torch.float32, device=x.device)
-                for k, v in ctx.stacked_params.items()
-            }
-        accs = ws["layer_grad_accumulators"]
+        accs = layer_grad_accumulators(ws, ctx.stacked_params, num_layers, x.device)
         for i, g in enumerate(grad_output_grids):
             if g is not None:
                 ws["static_grad_outputs"][i][:num_cells].copy_(g)
@@ -181,6 +191,12 @@ class WavefrontEngine(nn.Module):
             self.port_map, self.active_cells_buffer, self.active_layers_buffer,
             self.gathered_out_buffer, self.stacked_params, self.bwd_cache, self.graph_workspace,
             self.spatial_map_buffer, self.batched_forward, *states)
+
+    def graphed(self, x: torch.Tensor, warmup: int = 2):
+        """This engine's per-tick forward and backward captured as CUDA graphs for inputs shaped
+        like `x` (wavefront.wavefront_graph.GraphedWavefrontEngine)."""
+        from .wavefront_graph import GraphedWavefrontEngine
+        return GraphedWavefrontEngine(self, x, warmup=warmup)
 
     # ---- host-side set-up (reference :275-438) ------------------------------------------------
     def _init_buffers(self, x):

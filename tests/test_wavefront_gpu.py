@@ -119,6 +119,72 @@ def test_engine_flb_dependencies_against_pure_loop(cuda):
         assert torch.allclose(a.grad.cpu(), b.grad, atol=1e-5)
 
 
+class _FlbLikeCell(nn.Module):
+    """Three inputs (feedforward, lateral, feedback), four outputs, as the FLB block's ports."""
+
+    def __init__(self, dim):
+        super().__init__()
+        self.lin = nn.Linear(3 * dim, 4 * dim)
+        self.dim = dim
+
+    def forward(self, a, b, c):
+        o = torch.tanh(self.lin(torch.cat([a, b, c], -1)))
+        d = self.dim
+        return o[..., :d], o[..., d:2 * d], o[..., 2 * d:3 * d], o[..., 3 * d:]
+
+
+@pytest.mark.parametrize("dtype", [torch.float32, torch.bfloat16])
+def test_graphed_engine_matches_eager(cuda, dtype):
+    """CUDA-graph replay of the per-tick loops (GraphedWavefrontEngine) against the eager
+    engine: outputs, x.grad and parameter grads over three calls with new inputs, with an
+    in-place parameter update between calls (the graph re-reads the live parameters)."""
+    from wavefront import WavefrontConfig, WavefrontEngine, GraphedWavefrontEngine
+    torch.manual_seed(11)
+    deps = [((-1, 0), 0), ((0, -1), 1), ((1, -1), 2)]
+    cfg = WavefrontConfig(grid_shape=(4, 6), batch_size=3, dim=16, dependencies=deps,
+                          num_ports=4)
+    base = nn.ModuleList([_FlbLikeCell(16) for _ in range(4)])
+    la, lb = copy.deepcopy(base).to(cuda), copy.deepcopy(base).to(cuda)
+    eng_a = WavefrontEngine(cfg, la).to(cuda)
+    eng_b = WavefrontEngine(cfg, lb).to(cuda)
+    x0 = torch.randn(3, 6, 16, device=cuda).to(dtype)
+    graphed = GraphedWavefrontEngine(eng_b, x0)
+    tol = 1e-5 if dtype == torch.float32 else 2e-2
+    for it in range(3):
+        x = torch.randn(3, 6, 16, device=cuda).to(dtype)
+        xa = x.clone().requires_grad_(True)
+        xb = x.clone().requires_grad_(True)
+        oa = eng_a(xa)
+        ob = graphed(xb)
+        for p in range(4):
+            assert torch.allclose(oa[p].float(), ob[p].float(), atol=tol), (it, p)
+        (oa[0].float().sum() + oa[3].float().square().sum()).backward()
+        (ob[0].float().sum() + ob[3].float().square().sum()).backward()
+        assert torch.allclose(xa.grad.float(), xb.grad.float(), atol=tol), it
+        for pa, pb in zip(la.parameters(), lb.parameters()):
+            scale = max(1.0, pa.grad.abs().max().item())
+            assert torch.allclose(pa.grad, pb.grad, atol=tol * scale), it
+        with torch.no_grad():
+            for pa, pb in zip(la.parameters(), lb.parameters()):
+                pa.mul_(0.9)
+                pb.mul_(0.9)
+
+
+def test_graphed_engine_rejects_other_shapes_and_fast_path(cuda):
+    from wavefront import WavefrontConfig, WavefrontEngine, GraphedWavefrontEngine
+    from wavefront.grid_layer import TanhGridCell
+    cfg = WavefrontConfig(grid_shape=(2, 3), batch_size=2, dim=8,
+                          dependencies=[((-1, 0), 0), ((0, -1), 1), ((1, -1), 2)], num_ports=4)
+    eng = WavefrontEngine(cfg, nn.ModuleList([_FlbLikeCell(8) for _ in range(2)])).to(cuda)
+    g = GraphedWavefrontEngine(eng, torch.randn(2, 3, 8, device=cuda))
+    with pytest.raises(ValueError):
+        g(torch.randn(2, 4, 8, device=cuda))
+    fast_cfg = WavefrontConfig(grid_shape=(2, 3), batch_size=16, dim=128)
+    fast = WavefrontEngine(fast_cfg, nn.ModuleList([TanhGridCell(128) for _ in range(2)])).to(cuda)
+    with pytest.raises(ValueError):
+        GraphedWavefrontEngine(fast, torch.randn(16, 3, 128, device=cuda).bfloat16())
+
+
 def test_index_copy_modes(cuda):
     import flb_native as nat
     src = torch.randn(6, 3, 5, device=cuda)
