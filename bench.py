@@ -292,7 +292,7 @@ def extra_long_context(device, steps=3, warmup=1):
             "pairs_per_s": p / (ms * 1e-3), "tanh_per_s": p * A3["D"] / (ms * 1e-3)}
 
 
-def extra_grid(device, steps=3, warmup=1):
+def extra_grid(device, steps=3, warmup=1, with_cpu=True):
     try:
         from wavefront.grid_layer import wavefront_grid_layer, grid_inputs
     except ImportError:
@@ -306,9 +306,29 @@ def extra_grid(device, steps=3, warmup=1):
         step()
     ms = time_steps(step, steps, 1) / steps
     cells = 64 * 64
-    return {"workload": "wavefront grid 64x64 batch32 hidden256 bf16 fwd+bwd (U x at every cell)",
-            "ms": round(ms, 3), "cells_per_s": cells / (ms * 1e-3),
-            "tensor_tflops": 3 * 51.5e9 / (ms * 1e-3) / 1e12}
+    out = {"workload": "wavefront grid 64x64 batch32 hidden256 bf16 fwd+bwd (U x at every cell)",
+           "ms": round(ms, 3), "cells_per_s": cells / (ms * 1e-3),
+           "tensor_tflops": 3 * 51.5e9 / (ms * 1e-3) / 1e12}
+    if with_cpu:
+        out["cpu_baseline"] = cpu_grid_sample()
+    return out
+
+
+def cpu_grid_sample():
+    """The oracle's pure anti-diagonal loop (the reference test's cell loop restated, float32)
+    and its reverse sweep on the whole W4 grid on the host cores: one forward + backward."""
+    from oracle import wavefront as ow
+    torch.set_num_threads(os.cpu_count() or 1)
+    x, W_l, W_t, U, b, _, dh = ow.tanh_grid_make_inputs(32, 64, 64, 256, seed=3)
+    xs, Wls, Wts, Us, bs, dhs = (t.float() for t in (x, W_l, W_t, U, b, dh))
+    t0 = time.perf_counter()
+    h = ow.tanh_grid_forward(xs, Wls, Wts, Us, bs)
+    t1 = time.perf_counter()
+    ow.tanh_grid_backward(xs, Wls, Wts, Us, bs, h, dhs)
+    t2 = time.perf_counter()
+    return {"value": 64 * 64 / (t2 - t0), "unit": "cells/s", "cores": torch.get_num_threads(),
+            "kind": "port", "fwd_s": round(t1 - t0, 3), "bwd_s": round(t2 - t1, 3),
+            "sample": "whole W4 grid (64x64, batch 32, hidden 256), forward + backward, float32"}
 
 
 def extra_engine(device, steps=2, warmup=1):

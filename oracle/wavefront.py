@@ -146,6 +146,46 @@ def tanh_grid_forward(x, W_l, W_t, U, b, top=None):
     return torch.stack([torch.stack(r) for r in rows])
 
 
+def tanh_grid_backward(x, W_l, W_t, U, b, h, dh, top=None):
+    """Reverse sweep of tanh_grid_forward (the chain rule of the same loop, cells visited in
+    reverse row-major order), without an autograd graph. h [R, C, B, H] is the forward output,
+    dh its upstream gradient. Returns (dx, dW_l, dW_t, dU, db, dtop); dU is None when U is,
+    dtop when top is."""
+    B, R, C, H = x.shape
+    G = W_l.shape[0]
+    zero = torch.zeros(B, H, dtype=h.dtype)
+    dW_l, dW_t = torch.zeros_like(W_l), torch.zeros_like(W_t)
+    db = torch.zeros_like(b)
+    dU = torch.zeros_like(U) if U is not None else None
+    dx = torch.zeros_like(x)
+    dtop = torch.zeros(C, B, H, dtype=h.dtype) if top is not None else None
+    dz = [[None] * C for _ in range(R)]
+    for i in reversed(range(R)):
+        g = i if G > 1 else 0
+        g_down = (i + 1 if G > 1 else 0) if i + 1 < R else g
+        for j in reversed(range(C)):
+            gh = dh[i, j].clone()
+            if j + 1 < C:
+                gh = gh + dz[i][j + 1] @ W_l[g]
+            if i + 1 < R:
+                gh = gh + dz[i + 1][j] @ W_t[g_down]
+            d = gh * (1 - h[i, j] * h[i, j])
+            dz[i][j] = d
+            left = h[i, j - 1] if j > 0 else zero
+            up = h[i - 1, j] if i > 0 else (top[j] if top is not None else zero)
+            dW_l[g] += d.T @ left
+            dW_t[g] += d.T @ up
+            db[g] += d.sum(0)
+            if U is not None:
+                dU += d.T @ x[:, i, j, :]
+                dx[:, i, j, :] = d @ U
+            if i == 0 and top is not None:
+                dtop[j] = d @ W_t[g]
+        if i + 2 < R:
+            dz[i + 2] = None  # rows below i + 1 are no longer needed
+    return dx, dW_l, dW_t, dU, db, dtop
+
+
 def tanh_grid_make_inputs(B, R, C, H, G=1, seed=0, with_U=True, with_top=False):
     """Seeded inputs with the benchmark distributions: x ~ N(0,1) [B,R,C,H];
     W_l, W_t, U ~ N(0, 1/H); b = 0; upstream grad dh ~ N(0,1) [R,C,B,H]."""
