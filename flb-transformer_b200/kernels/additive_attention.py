@@ -129,6 +129,14 @@ def _save_scores_ok(q) -> bool:
             and BH * N * N * 4 <= SAVE_SCORES_LIMIT_BYTES)
 
 
+def _unwrap_functorch(t):
+    """The plain tensor inside torch.func's wrappers (first-order gradients only)."""
+    from torch._C._functorch import is_functorch_wrapped_tensor, get_unwrapped
+    while isinstance(t, torch.Tensor) and is_functorch_wrapped_tensor(t):
+        t = get_unwrapped(t)
+    return t
+
+
 class FusedAdditiveAttentionFunc(torch.autograd.Function):
     """Same structure as the reference Function (kernels/additive_attention.py:135-203):
     forward / setup_context / backward / vmap, and `apply(q, k, v, v_a)` returns one tensor.
@@ -151,8 +159,17 @@ class FusedAdditiveAttentionFunc(torch.autograd.Function):
         q, k, v, v_a = inputs[:4]
         causal = inputs[4] if len(inputs) > 4 else False
         exact = inputs[5] if len(inputs) > 5 else False
-        lse, table, idx, scores = output.__dict__.pop("_flb_aux")
         ctx.causal, ctx.exact = bool(causal), bool(exact)
+        # Under torch.func transforms (the wavefront engine's vjp of a cell that calls this op)
+        # `output` is a functorch wrapper, not the tensor forward returned, and the auxiliary
+        # tensors are not reachable; the backward then recomputes lse with one more forward.
+        aux = output.__dict__.pop("_flb_aux", None)
+        if aux is None:
+            ctx.recompute = True
+            ctx.save_for_backward(q, k, v, v_a, output)
+            return
+        lse, table, idx, scores = aux
+        ctx.recompute = False
         ctx.has_scores = scores is not None
         extra = (scores,) if scores is not None else ()
         ctx.save_for_backward(q, k, v, v_a, output, lse, table, idx, *extra)
@@ -161,8 +178,15 @@ class FusedAdditiveAttentionFunc(torch.autograd.Function):
     @torch.compiler.disable
     def backward(ctx, grad_out):
         saved = ctx.saved_tensors
-        q, k, v, v_a, out, lse, table, idx = saved[:8]
-        scores = saved[8] if ctx.has_scores else None
+        if ctx.recompute:
+            # functorch hands the saved inputs back wrapped; the kernels need their storage
+            q, k, v, v_a, _ = (_unwrap_functorch(t) for t in saved)
+            grad_out = _unwrap_functorch(grad_out)
+            out, lse, table, idx, _ = attention_forward(q, k, v, v_a, ctx.causal, ctx.exact)
+            scores = None
+        else:
+            q, k, v, v_a, out, lse, table, idx = saved[:8]
+            scores = saved[8] if ctx.has_scores else None
         dq, dk, dv, dva = attention_backward(q, k, v, v_a, out, lse, grad_out, table, idx,
                                              ctx.causal, ctx.exact, scores=scores)
         return dq, dk, dv, dva, None, None

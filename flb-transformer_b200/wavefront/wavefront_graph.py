@@ -65,6 +65,8 @@ class _GraphedEngineFunction(torch.autograd.Function):
                 ws["static_grad_outputs"][i][:nc].copy_(g)
             else:
                 ws["static_grad_outputs"][i][:nc].zero_()
+        if runner.g_bwd is None:
+            raise RuntimeError("GraphedWavefrontEngine was captured with backward=False")
         runner.g_bwd.replay()
         grad_x = ws["static_grad_x"].clone()
         grad_states = [ws["static_current_grad_grids"][p][nc:nc + dock].clone() if has else None
@@ -79,9 +81,9 @@ class _GraphedEngineFunction(torch.autograd.Function):
 class GraphedWavefrontEngine:
     """Forward and backward tick loops of `engine` captured as two CUDA graphs (see module
     docstring). `x` is an example input: its shape and dtype are frozen; its values are only
-    used for the warm-up runs."""
+    used for the warm-up runs. backward=False captures the forward only (inference)."""
 
-    def __init__(self, engine, x: torch.Tensor, warmup: int = 2):
+    def __init__(self, engine, x: torch.Tensor, warmup: int = 2, backward: bool = True):
         nat.require_cuda(x)
         from .grid_layer import fast_path_applies
         if fast_path_applies(engine, x):
@@ -114,15 +116,18 @@ class GraphedWavefrontEngine:
         with torch.cuda.stream(side):
             for _ in range(warmup):
                 self._forward_loop()
-                self._backward_loop()
+                if backward:
+                    self._backward_loop()
         torch.cuda.current_stream(x.device).wait_stream(side)
         pool = torch.cuda.graph_pool_handle()
         self.g_fwd = torch.cuda.CUDAGraph()
         with torch.cuda.graph(self.g_fwd, pool=pool):
             self._forward_loop()
-        self.g_bwd = torch.cuda.CUDAGraph()
-        with torch.cuda.graph(self.g_bwd, pool=pool):
-            self._backward_loop()
+        self.g_bwd = None
+        if backward:
+            self.g_bwd = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(self.g_bwd, pool=pool):
+                self._backward_loop()
 
     # the captured bodies: static buffers in, static buffers out
     def _forward_loop(self):

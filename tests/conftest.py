@@ -37,6 +37,11 @@ def wf_golden():
 
 
 @pytest.fixture(scope="session")
+def flb_golden():
+    return load_golden("flb_model.pt")
+
+
+@pytest.fixture(scope="session")
 def cuda():
     import torch
     if not torch.cuda.is_available():

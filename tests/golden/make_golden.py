@@ -13,7 +13,9 @@ Everything here runs on CPU:
     fetch_mapped_context, and the reference WavefrontEngine itself (its C++ tick loop from
     oracle/_ref, with the Triton gather replaced by a loop over fetch_mapped_context and
     torch.compile forced to eager), on the configurations of the reference's own tests
-    (wavefront/wavefront_test.py) and on a per-row tanh grid cell.
+    (wavefront/wavefront_test.py) and on a per-row tanh grid cell;
+  * the FLB model: the reference FLB_Transformer end to end (logits, aux loss, contexts,
+    parameter gradients of cross-entropy + aux) on a small configuration.
 The fixtures are small (under 2 MB in total) and are committed; this script is how they were made.
 """
 from __future__ import annotations
@@ -188,10 +190,54 @@ def wavefront_goldens():
     return out
 
 
+def flb_model_goldens():
+    """The reference FLB_Transformer (models/FLB_Model.py) end to end on CPU, eval mode, on a
+    small configuration: its attention op replaced by the reference's eager ground truth
+    (the Triton kernel has no CPU path), the engine as in wavefront_goldens()."""
+    import wavefront.wavefront_engine as we
+    import models.FLB_Model as fm
+    from kernels.kernel_tests import pure_torch_additive_attention
+    from wavefront.wavefront_kernel import fetch_mapped_context
+
+    def cpu_fetch(x, stacked_grids, routing_map, port_map, spatial_map, config, active, gathered):
+        n = math.prod(config.grid_shape)
+        grids = [stacked_grids[p][:n] for p in range(config.num_ports)]
+        gathered.zero_()
+        for s, cell in enumerate(active.tolist()):
+            if cell >= n:
+                continue
+            for d, t in enumerate(fetch_mapped_context(x, grids, cell, routing_map, config)):
+                gathered[d, s] = t
+        return gathered
+
+    we.run_fetch_kernel = cpu_fetch
+    fm.fused_additive_attention = pure_torch_additive_attention
+    torch.manual_seed(21)
+    V, D, L, S, B = 40, 32, 3, 5, 2
+    model = fm.FLB_Transformer(V, hidden_dim=D, num_layers=L, seq_len=S, batch_size=B)
+    with torch.no_grad():  # larger v_a than the 0.02 init so the attention weights matter
+        for layer in model.layers:
+            layer.flb_attention.v_a.normal_(0.0, 0.5)
+    model.eval()
+    tokens = torch.randint(0, V, (B, S), generator=torch.Generator().manual_seed(3))
+    targets = torch.randint(0, V, (B, S), generator=torch.Generator().manual_seed(4))
+    logits, aux, (lat, fdbk) = model(tokens)
+    loss = torch.nn.functional.cross_entropy(logits.reshape(-1, V), targets.reshape(-1)) + aux
+    loss.backward()
+    return dict(config=dict(vocab=V, hidden=D, layers=L, seq_len=S, batch=B),
+                state_dict={k: v.detach().clone() for k, v in model.state_dict().items()},
+                tokens=tokens, targets=targets, logits=logits.detach(), aux_loss=aux.detach(),
+                next_lat=lat.detach().clone(), next_fdbk=fdbk.detach().clone(),
+                loss=loss.detach(),
+                grads={k: p.grad.clone() for k, p in model.named_parameters()
+                       if p.grad is not None})
+
+
 def main():
     torch.save(attention_goldens(), os.path.join(HERE, "attention.pt"))
     torch.save(wavefront_goldens(), os.path.join(HERE, "wavefront.pt"))
-    for f in ("attention.pt", "wavefront.pt"):
+    torch.save(flb_model_goldens(), os.path.join(HERE, "flb_model.pt"))
+    for f in ("attention.pt", "wavefront.pt", "flb_model.pt"):
         print(f, os.path.getsize(os.path.join(HERE, f)), "bytes")
 
 

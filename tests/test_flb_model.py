@@ -1,0 +1,95 @@
+"""FLBTransformer (flb_model/) against the reference FLB_Transformer's outputs and gradients
+(tests/golden/flb_model.pt, made by running the reference on CPU), and its greedy decode."""
+import pytest
+import torch
+import torch.nn.functional as F
+
+
+def _model(c, device="cpu"):
+    from flb_model import FLBTransformer
+    return FLBTransformer(c["vocab"], hidden_dim=c["hidden"], num_layers=c["layers"],
+                          seq_len=c["seq_len"], batch_size=c["batch"]).to(device)
+
+
+def test_state_dict_layout_matches_reference(flb_golden):
+    """Same parameter and buffer names and shapes as the reference model: checkpoints load
+    either way (strict)."""
+    m = _model(flb_golden["config"])
+    ref = flb_golden["state_dict"]
+    mine = m.state_dict()
+    assert set(mine) == set(ref)
+    for k, v in ref.items():
+        assert mine[k].shape == v.shape, k
+    m.load_state_dict(ref, strict=True)
+
+
+@pytest.mark.gpu
+def test_flb_model_matches_reference(cuda, flb_golden):
+    """fp32 end to end with tanh.approx attention: logits, aux loss, next contexts and every
+    parameter gradient of cross-entropy + aux within 2e-3 of the reference (relative to each
+    tensor's magnitude for gradients)."""
+    g = flb_golden
+    c = g["config"]
+    m = _model(c, cuda)
+    m.load_state_dict(g["state_dict"])
+    m.eval()
+    logits, aux, (lat, fdbk) = m(g["tokens"].to(cuda))
+    assert torch.allclose(logits.cpu(), g["logits"], atol=2e-3)
+    assert abs(aux.item() - g["aux_loss"].item()) < 2e-3 * max(1.0, g["aux_loss"].abs().item())
+    assert torch.allclose(lat.cpu(), g["next_lat"], atol=2e-3)
+    assert torch.allclose(fdbk.cpu(), g["next_fdbk"], atol=2e-3)
+    loss = F.cross_entropy(logits.reshape(-1, c["vocab"]), g["targets"].to(cuda).reshape(-1)) + aux
+    loss.backward()
+    for k, p in m.named_parameters():
+        if k not in g["grads"]:
+            assert p.grad is None or not p.grad.any(), k
+            continue
+        ref = g["grads"][k]
+        scale = max(ref.abs().max().item(), 1e-3)
+        assert (p.grad.cpu() - ref).abs().max().item() <= 2e-3 * scale, k
+
+
+@pytest.mark.gpu
+def test_flb_model_graphed_engine_matches_eager(cuda, flb_golden):
+    """The model through a GraphedWavefrontEngine (forward + backward captured) gives the eager
+    engine's logits and gradients."""
+    g = flb_golden
+    c = g["config"]
+    ma, mb = _model(c, cuda), _model(c, cuda)
+    ma.load_state_dict(g["state_dict"])
+    mb.load_state_dict(g["state_dict"])
+    ma.eval()
+    mb.eval()
+    tok = g["tokens"].to(cuda)
+    graphed = mb.engine.graphed(mb.embedding(tok).detach())
+    for _ in range(2):
+        la, aa, _ = ma(tok)
+        lb, ab, _ = mb(tok, engine=graphed)
+        assert torch.allclose(la, lb, atol=1e-5)
+        (la.square().mean() + aa).backward()
+        (lb.square().mean() + ab).backward()
+    for (ka, pa), (kb, pb) in zip(ma.named_parameters(), mb.named_parameters()):
+        if pa.grad is None:
+            assert pb.grad is None or not pb.grad.any(), ka
+            continue
+        scale = max(pa.grad.abs().max().item(), 1e-3)
+        assert (pa.grad - pb.grad).abs().max().item() <= 1e-4 * scale, ka
+
+
+@pytest.mark.gpu
+def test_greedy_decode_graphed_equals_eager(cuda):
+    from flb_model import FLBTransformer, greedy_decode
+    torch.manual_seed(5)
+    m = FLBTransformer(50, hidden_dim=64, num_layers=3, seq_len=8, batch_size=2).to(cuda).eval()
+    with torch.no_grad():
+        for layer in m.layers:
+            layer.flb_attention.v_a.normal_(0.0, 0.5)
+    prompt = torch.randint(0, 50, (2, 8), device=cuda)
+    a = greedy_decode(m, prompt, 5, graphed=False)
+    b = greedy_decode(m, prompt, 5, graphed=True)
+    assert a.shape == (2, 5)
+    assert torch.equal(a, b)
+    # the first generated token is the argmax of the prompt's last-position logits
+    with torch.no_grad():
+        logits, _, _ = m(prompt)
+    assert torch.equal(a[:, 0], logits[:, -1].argmax(-1))
