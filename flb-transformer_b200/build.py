@@ -32,6 +32,7 @@ CU_SOURCES = [
     "attention_fast.cu",
     "wavefront_prims.cu",
     "wavefront_grid.cu",
+    "flb_block.cu",
     "microbench.cu",
     "umma_selftest.cu",
 ]

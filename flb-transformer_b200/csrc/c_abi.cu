@@ -50,6 +50,10 @@ int wf_gather(const void* x, const int64_t xs[3], const void* grids, const int64
 int wf_index_copy(const void* src, int src_dtype, const int64_t ss[3], const int64_t* src_rows,
                   void* dst, int dst_dtype, const int64_t ds[3], const int64_t* dst_rows,
                   int64_t n_rows, int64_t batch, int64_t dim, int accumulate, cudaStream_t s);
+size_t block_grid_workspace_bytes(int64_t L, int64_t S, int64_t B, int64_t D);
+int block_grid_fwd(const flb_block_weights* W, const void* x, void* grids, int64_t L, int64_t S,
+                   int64_t B, int64_t D, int64_t H, float eps, void* ws, size_t ws_bytes,
+                   cudaStream_t s);
 size_t grid_workspace_bytes(int64_t R, int64_t C, int64_t B, int64_t H, int64_t G, int has_U);
 int grid_fwd(const void* x, int x_layout, const void* W_l, const void* W_t, const void* U,
              const float* bias, const void* top, void* h_out, int64_t R, int64_t C, int64_t B,
@@ -184,6 +188,36 @@ int flb_wf_index_copy(const void* src, int src_dtype, const int64_t src_strides[
     return fail(FLB_ERR_SHAPE, "wf_index_copy: null pointer");
   return wf_index_copy(src, src_dtype, src_strides, src_rows, dst, dst_dtype, dst_strides,
                        dst_rows, n_rows, batch, dim, accumulate, as_stream(stream));
+}
+
+size_t flb_block_grid_workspace_bytes(int64_t L, int64_t S, int64_t batch, int64_t D) {
+  if (L < 1 || S < 1 || batch < 1 || D < 1) return 0;
+  return block_grid_workspace_bytes(L, S, batch, D);
+}
+
+int flb_block_grid_fwd(const flb_block_weights* weights, const void* x, void* grids, int64_t L,
+                       int64_t S, int64_t batch, int64_t D, int64_t heads, float ln_eps,
+                       void* workspace, size_t workspace_bytes, void* stream) {
+  if (!weights || !x || !grids) return fail(FLB_ERR_SHAPE, "block_grid_fwd: null pointer");
+  const flb_block_weights& w = *weights;
+  if (!w.ln_lat_w || !w.ln_lat_b || !w.ln_fdbk_w || !w.ln_fdbk_b || !w.w_prior_lat ||
+      !w.w_prior_fdbk || !w.w_gate_l || !w.b_gate_l || !w.w_gate_x || !w.b_gate_x || !w.w_qkv ||
+      !w.w_o || !w.v_a)
+    return fail(FLB_ERR_SHAPE, "block_grid_fwd: null weight pointer");
+  if (L < 1 || S < 1 || batch < 1 || D < 16 || heads < 1)
+    return fail(FLB_ERR_SHAPE, "block_grid_fwd: sizes must be positive (D >= 16)");
+  if (D % 16 != 0 || D % heads != 0)
+    return fail(FLB_ERR_SHAPE, "block_grid_fwd: D must be a multiple of 16 and of heads");
+  if ((L * S + L) * batch * D * 4 > ((int64_t)1 << 40) || 3 * batch * D > (1 << 30))
+    return fail(FLB_ERR_SHAPE, "block_grid_fwd: grid too large");
+  const size_t need = block_grid_workspace_bytes(L, S, batch, D);
+  if (!workspace || workspace_bytes < need)
+    return fail(FLB_ERR_WORKSPACE, "block_grid_fwd: workspace smaller than flb_block_grid_workspace_bytes()");
+  if (((uintptr_t)x | (uintptr_t)grids | (uintptr_t)w.w_prior_lat | (uintptr_t)w.w_prior_fdbk |
+       (uintptr_t)w.w_gate_l | (uintptr_t)w.w_gate_x | (uintptr_t)w.w_qkv | (uintptr_t)w.w_o) & 15u)
+    return fail(FLB_ERR_ALIGN, "block_grid_fwd: bf16 tensors must be 16-byte aligned");
+  return block_grid_fwd(weights, x, grids, L, S, batch, D, heads, ln_eps, workspace,
+                        workspace_bytes, as_stream(stream));
 }
 
 size_t flb_grid_workspace_bytes(int64_t R, int64_t C, int64_t B, int64_t H, int64_t G, int has_U) {

@@ -30,6 +30,7 @@
 #include "common.cuh"
 #include "sm100.cuh"
 #include "tma_host.cuh"
+#include "blas.cuh"
 
 namespace flb {
 
@@ -290,41 +291,6 @@ __global__ void sum_rows_kernel(const float* __restrict__ src, float* __restrict
   float s = 0.f;
   for (int r = first; r < R; ++r) s += src[(int64_t)r * n + e];
   dst[e] = s;
-}
-
-// ---- cuBLAS (plain GEMMs only: hoisted U x, weight gradients, dx, dtop) ------------------------
-struct Blas {
-  cublasHandle_t h = nullptr;
-  int dev = -1;
-};
-thread_local Blas t_blas;
-
-int blas(cudaStream_t s, void* ws, size_t ws_bytes, cublasHandle_t* out) {
-  int dev = 0;
-  cudaGetDevice(&dev);
-  if (t_blas.h == nullptr || t_blas.dev != dev) {
-    if (cublasCreate(&t_blas.h) != CUBLAS_STATUS_SUCCESS) return fail(FLB_ERR_CUDA, "cublasCreate failed");
-    t_blas.dev = dev;
-  }
-  if (cublasSetStream(t_blas.h, s) != CUBLAS_STATUS_SUCCESS) return fail(FLB_ERR_CUDA, "cublasSetStream failed");
-  if (cublasSetWorkspace(t_blas.h, ws, ws_bytes) != CUBLAS_STATUS_SUCCESS)
-    return fail(FLB_ERR_CUDA, "cublasSetWorkspace failed");
-  *out = t_blas.h;
-  return FLB_OK;
-}
-
-// Row-major C[M x N] (+)= op(A)[M x K] . op(B)[K x N], bf16 inputs, fp32 output, batched with
-// element strides sA, sB, sC.
-int gemm_rm(cublasHandle_t h, bool ta, bool tb, int M, int N, int K, const void* A, int lda,
-            long long sA, const void* Bm, int ldb, long long sB, float* Cm, int ldc, long long sC,
-            int batch, float beta, cudaDataType ctype = CUDA_R_32F) {
-  const float alpha = 1.f;
-  cublasStatus_t st = cublasGemmStridedBatchedEx(
-      h, tb ? CUBLAS_OP_T : CUBLAS_OP_N, ta ? CUBLAS_OP_T : CUBLAS_OP_N, N, M, K, &alpha, Bm,
-      CUDA_R_16BF, ldb, sB, A, CUDA_R_16BF, lda, sA, &beta, Cm, ctype, ldc, sC, batch,
-      CUBLAS_COMPUTE_32F, CUBLAS_GEMM_DEFAULT);
-  if (st != CUBLAS_STATUS_SUCCESS) return fail(FLB_ERR_CUDA, "cublasGemmStridedBatchedEx failed (" + std::to_string((int)st) + ")");
-  return FLB_OK;
 }
 
 // ---- workspace layout ------------------------------------------------------------------------------

@@ -48,6 +48,9 @@ PROTOTYPES = {
                              _i64, _i64, _i64, _i32, _vp]),
     "flb_wf_index_copy": (_i32, [_vp, _i32, _i64p, _vp, _vp, _i32, _i64p, _vp, _i64, _i64, _i64,
                                  _i32, _vp]),
+    "flb_block_grid_workspace_bytes": (_sz, [_i64, _i64, _i64, _i64]),
+    "flb_block_grid_fwd": (_i32, [_vp, _vp, _vp, _i64, _i64, _i64, _i64, _i64, ctypes.c_float,
+                                  _vp, _sz, _vp]),
     "flb_grid_workspace_bytes": (_sz, [_i64, _i64, _i64, _i64, _i64, _i32]),
     "flb_grid_fwd": (_i32, [_vp, _i32, _vp, _vp, _vp, _vp, _vp, _vp, _i64, _i64, _i64, _i64, _i64,
                             _vp, _sz, _i32, _vp]),
@@ -61,6 +64,14 @@ PROTOTYPES = {
     "flb_microbench": (_i32, [_i32, _vp, _dblp]),
     "flb_selftest_umma": (_i32, [_i32, _i32, _vp, _vp, _vp, _vp, _vp]),
 }
+
+
+class BlockWeights(ctypes.Structure):
+    """flb_block_weights of include/flb_b200.h (device pointers, same field order)."""
+    _fields_ = [(n, ctypes.c_void_p) for n in (
+        "ln_lat_w", "ln_lat_b", "ln_fdbk_w", "ln_fdbk_b", "w_prior_lat", "w_prior_fdbk",
+        "w_gate_l", "b_gate_l", "w_gate_x", "b_gate_x", "w_qkv", "w_o", "v_a")]
+
 
 for _name, (_res, _args) in PROTOTYPES.items():
     _fn = getattr(lib, _name)

@@ -172,6 +172,16 @@ class WavefrontEngine(nn.Module):
         fast = engine_fast_path(self, x, initial_states)
         if fast is not None:
             return fast
+        from .flb_cells import native_flb_applies, no_grad_needed, native_flb_forward
+        if no_grad_needed(self, x) and native_flb_applies(self, x):
+            # FLB block cells, inference: the whole grid in flb_block_grid_fwd (no tick loop
+            # through Python; initial states reach no cell, as in the per-tick path)
+            self._init_buffers(x)
+            ws = self.graph_workspace
+            ws["static_x"].copy_(x)
+            native_flb_forward(self, ws["static_x"], ws["static_stacked_grids"])
+            n = math.prod(self.config.grid_shape)
+            return tuple(ws["static_stacked_grids"][p][:n] for p in range(self.config.num_ports))
         if initial_states is None:
             initial_states = {}
         self._init_buffers(x)

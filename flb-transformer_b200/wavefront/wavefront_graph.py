@@ -21,7 +21,8 @@ Contract (what capture freezes):
     (and the reference's): the next call overwrites them;
   * the cell must be capturable (no host synchronisation, no data-dependent shapes).
 Tanh grid cells that take the persistent-kernel fast path need no graph; the runner refuses
-them (call the engine directly).
+them (call the engine directly). An inference capture (backward=False) of FLB block cells
+captures the native whole-grid forward (wavefront.flb_cells) instead of the tick loop.
 """
 from __future__ import annotations
 
@@ -95,6 +96,9 @@ class GraphedWavefrontEngine:
         self.num_layers = cfg.grid_shape[0]
         self.x_shape, self.x_dtype = tuple(x.shape), x.dtype
         engine._init_buffers(x)
+        from .flb_cells import native_flb_applies
+        # inference graphs of FLB block cells capture the native whole-grid forward
+        self.native_flb = (not backward) and native_flb_applies(engine, x)
         ws = engine.graph_workspace
         self.accs = layer_grad_accumulators(ws, engine.stacked_params, self.num_layers, x.device)
         # (layer index, stacked-parameter name, parameter) in the order grads are returned
@@ -133,6 +137,10 @@ class GraphedWavefrontEngine:
     def _forward_loop(self):
         eng, cfg = self.engine, self.engine.config
         ws = eng.graph_workspace
+        if self.native_flb:
+            from .flb_cells import native_flb_forward
+            native_flb_forward(eng, ws["static_x"], ws["static_stacked_grids"])
+            return
         refresh_stacked_params(eng.layers, eng.stacked_params)
         with torch.no_grad():
             wavefront_backend.execute_forward(

@@ -187,6 +187,42 @@ int flb_grid_fwd_static(const void* W_l, const void* W_t, const float* bias, con
                         void* h_out, int64_t R, int64_t C, int64_t B, int64_t H, int64_t G,
                         int check_timeout, void* stream);
 
+/* ------------------------------------------------------------------------------------------
+ * FLB block cells (inference forward).
+ * Replaces the per-tick evaluation of FLB_Block cells by the engine (batched_forward under
+ * torch.vmap, wavefront/wavefront_engine.py:185-198, models/FLB_Model.py:32-96) for the FLB
+ * grid: L layers x S positions, dependencies top -> port 0, left -> port 1, bottom-left ->
+ * port 2, four ports, 8-head additive attention over the three tokens.
+ * Weights are per-layer stacks (nn.Linear layout [out, in], bf16) and float32 vectors; w_qkv is
+ * [L, 3D, D] = W_q, W_k, W_v of each layer stacked by rows.
+ * ------------------------------------------------------------------------------------------ */
+typedef struct flb_block_weights {
+  const float* ln_lat_w;   /* [L, D] norm_lat weight, bias */
+  const float* ln_lat_b;
+  const float* ln_fdbk_w;  /* [L, D] norm_fdbk weight, bias */
+  const float* ln_fdbk_b;
+  const void* w_prior_lat;   /* bf16 [L, D, D] proj_lateral */
+  const void* w_prior_fdbk;  /* bf16 [L, D, D] proj_feedback */
+  const void* w_gate_l;      /* bf16 [L, D, D] flb_attention.linear_gate_L; bias f32 [L, D] */
+  const float* b_gate_l;
+  const void* w_gate_x;      /* bf16 [L, D, D] flb_attention.linear_gate_X; bias f32 [L, D] */
+  const float* b_gate_x;
+  const void* w_qkv;         /* bf16 [L, 3D, D] W_q | W_k | W_v */
+  const void* w_o;           /* bf16 [L, D, D] W_o */
+  const float* v_a;          /* [L, H, D/H] */
+} flb_block_weights;
+
+size_t flb_block_grid_workspace_bytes(int64_t L, int64_t S, int64_t batch, int64_t D);
+
+/* Whole-grid forward of FLB block cells, tick by tick on `stream` (no host synchronisation).
+ * x: bf16 [batch, S, D] (row 0's top input). grids: bf16 [4, L*S + L, batch, D], the engine's
+ * port grids (cell l*S + t; the last L rows are its boundary dock and are not touched); every
+ * cell of ports 0-3 is written: h_x, h_lat, h_fdbk and the auxiliary loss term. D must be a
+ * multiple of 16 and of `heads`; ln_eps is the LayerNorms' epsilon. */
+int flb_block_grid_fwd(const flb_block_weights* weights, const void* x, void* grids,
+                       int64_t L, int64_t S, int64_t batch, int64_t D, int64_t heads,
+                       float ln_eps, void* workspace, size_t workspace_bytes, void* stream);
+
 /* Failure-detection check of the grid kernels' bounded dependency waits (no reference
  * counterpart). Runs flb_grid_fwd with the flag of cell (drop_row, drop_col) never released and
  * the flag-wait bound lowered to spin_limit polls: the cells waiting on it give up, record the

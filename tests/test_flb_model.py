@@ -93,3 +93,76 @@ def test_greedy_decode_graphed_equals_eager(cuda):
     with torch.no_grad():
         logits, _, _ = m(prompt)
     assert torch.equal(a[:, 0], logits[:, -1].argmax(-1))
+
+
+def _bf16_model(seed, V=50, D=64, L=4, S=6, B=3):
+    from flb_model import FLBTransformer
+    torch.manual_seed(seed)
+    m = FLBTransformer(V, hidden_dim=D, num_layers=L, seq_len=S, batch_size=B).cuda().eval()
+    with torch.no_grad():
+        for name, p in m.named_parameters():
+            if name.endswith("v_a"):
+                p.normal_(0.0, 0.5)
+            elif "bias" in name and "norm" not in name:
+                p.normal_(0.0, 0.1)
+    return m
+
+
+def _max_rel(a, b):
+    return ((a.float() - b.float()).abs().max() / b.float().abs().max().clamp_min(1e-6)).item()
+
+
+@pytest.mark.gpu
+def test_native_flb_forward_matches_generic_path(cuda):
+    """Inference under bf16 autocast: the native whole-grid forward (flb_block_grid_fwd) against
+    the per-tick vmapped path of the same engine: every port grid, logits and contexts."""
+    m = _bf16_model(7)
+    tok = torch.randint(0, 50, (3, 6), device=cuda)
+    with torch.no_grad(), torch.autocast("cuda", dtype=torch.bfloat16):
+        x = m.embedding(tok)
+        m.engine.native_cells = False
+        gen = [g.clone() for g in m.engine(x)]
+        lg, ag, cg = m(tok)
+        m.engine.native_cells = True
+        nat_ = [g.clone() for g in m.engine(x)]
+        ln_, an, cn = m(tok)
+    for p in range(4):
+        assert nat_[p].dtype == torch.bfloat16
+        assert _max_rel(nat_[p], gen[p]) < 3e-2, p
+    assert _max_rel(ln_, lg) < 3e-2
+    assert abs(an.item() - ag.item()) <= 3e-2 * abs(ag.item()) + 1e-6
+    for a, b in zip(cn, cg):
+        assert _max_rel(a, b) < 3e-2
+
+
+@pytest.mark.gpu
+def test_native_flb_forward_against_reference(cuda, flb_golden):
+    """The native path (bf16) against the reference model in fp32 on the golden case: its error
+    stays within that of the per-tick path at the same precision (plus a small margin)."""
+    g = flb_golden
+    c = g["config"]
+    m = _model(c, cuda)
+    m.load_state_dict(g["state_dict"])
+    m.eval()
+    tok = g["tokens"].to(cuda)
+    ref = g["logits"].to(cuda)
+    with torch.no_grad(), torch.autocast("cuda", dtype=torch.bfloat16):
+        m.engine.native_cells = False
+        lg, _, _ = m(tok)
+        m.engine.native_cells = True
+        ln_, _, _ = m(tok)
+    e_gen, e_nat = _max_rel(lg, ref), _max_rel(ln_, ref)
+    assert e_nat <= 2 * e_gen + 1e-2, (e_nat, e_gen)
+
+
+@pytest.mark.gpu
+def test_native_flb_decode_graphed_equals_eager(cuda):
+    """Greedy decode under bf16 autocast: the CUDA-graph replay of the native forward gives the
+    same tokens as eager native forwards."""
+    from flb_model import greedy_decode
+    m = _bf16_model(9, S=8, B=2)
+    prompt = torch.randint(0, 50, (2, 8), device=cuda)
+    with torch.autocast("cuda", dtype=torch.bfloat16):
+        a = greedy_decode(m, prompt, 6, graphed=False)
+        b = greedy_decode(m, prompt, 6, graphed=True)
+    assert torch.equal(a, b)
