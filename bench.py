@@ -18,9 +18,11 @@ region. `roofline` reports the dominant kernel against the MUFU tanh rate measur
 device by flb_microbench (tanh is the binding pipe of this operator). `cpu_baseline` times the
 oracle (the reference's eager math restated on CPU) on a bounded sample on this host.
 
-Extras (default on, N=1 only): the long-context forward (B4 H8 N8192 D128 causal) and the
-wavefront grid layer (64x64 grid, batch 32, hidden 256, forward + backward), each timed with
-CUDA events, reported under "extras".
+Extras (default on, N=1 only), each timed with CUDA events, reported under "extras": the
+long-context forward (B4 H8 N8192 D128 causal); the wavefront grid layer (64x64 grid, batch 32,
+hidden 256, forward + backward) with its host-CPU baseline; the engine API on a 64x64 grid
+(persistent kernels, per-tick loop eager and graph-replayed); the FLB model end to end (12
+layers, d768, 16 x 1024 prompt, forward and greedy decode steps, bf16 inference).
 
 --impl reference times the reference's eager CPU math (oracle port) on a bounded sample of the
 same workload with every host thread, rank 0 only.
@@ -374,6 +376,42 @@ def extra_engine(device, steps=2, warmup=1):
             "cells_per_s": R * C / (res["persistent"] * 1e-3)}
 
 
+def extra_flb_e2e(device, steps=3, decode_steps=8):
+    """The FLB model end to end: 12 layers, d_model 768 (8 heads of additive attention per
+    cell, as FLB_Block fixes), vocab 32000, weights ~ N(0, 0.02), a 16 x 1024 prompt of uniform
+    token ids; bf16 autocast, inference. The grid runs as the native FLB cell forward replayed
+    as one CUDA graph per forward; a decode step re-runs the sliding 1024-token window (the
+    model carries no usable context) and appends the argmax token."""
+    from flb_model import FLBTransformer, greedy_decode
+    V, D, L, S, B = 32000, 768, 12, 1024, 16
+    torch.manual_seed(0)
+    m = FLBTransformer(V, hidden_dim=D, num_layers=L, seq_len=S, batch_size=B)
+    with torch.no_grad():
+        for name, p in m.named_parameters():
+            if p.dim() >= 2 or name.endswith("v_a"):
+                p.normal_(0.0, 0.02)
+            elif "norm" not in name:
+                p.zero_()
+    m = m.to(device).eval()
+    prompt = torch.randint(0, V, (B, S), device=device,
+                           generator=torch.Generator(device=device).manual_seed(1))
+    with torch.no_grad(), torch.autocast("cuda", dtype=torch.bfloat16):
+        t0 = time.perf_counter()
+        g = m.engine.graphed(m.embedding(prompt), backward=False)
+        torch.cuda.synchronize()
+        capture_s = time.perf_counter() - t0
+        m(prompt, engine=g)
+        fwd_ms = time_steps(lambda: m(prompt, engine=g), steps, 1) / steps
+        greedy_decode(m, prompt, 1, engine=g)
+        dec_ms = time_steps(lambda: greedy_decode(m, prompt, decode_steps, engine=g), 1, 1)
+    return {"workload": "FLB model 12 layers d768 vocab32000, prompt 16x1024, bf16 inference",
+            "native_cells": bool(g.native_flb), "capture_s": round(capture_s, 2),
+            "forward_ms": round(fwd_ms, 2), "cells_per_s": L * S / (fwd_ms * 1e-3),
+            "prompt_tokens_per_s": B * S / (fwd_ms * 1e-3),
+            "decode_steps": decode_steps, "decode_ms_per_step": round(dec_ms / decode_steps, 2),
+            "decode_tokens_per_s": B * decode_steps / (dec_ms * 1e-3)}
+
+
 # ------------------------------------------------------------------ arms
 def run_flb(args):
     import flb_native as nat
@@ -447,6 +485,7 @@ def run_flb(args):
         if g is not None:
             out["extras"]["grid"] = g
         out["extras"]["engine"] = extra_engine(device)
+        out["extras"]["flb_e2e"] = extra_flb_e2e(device)
     if rank == 0:
         print(json.dumps(out), flush=True)
     if world > 1:

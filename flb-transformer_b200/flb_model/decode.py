@@ -12,14 +12,14 @@ import torch
 
 
 @torch.no_grad()
-def greedy_decode(model, prompt: torch.Tensor, steps: int, graphed: bool = True):
-    """prompt [batch, seq_len] int64 token ids -> [batch, steps] generated ids."""
+def greedy_decode(model, prompt: torch.Tensor, steps: int, graphed: bool = True, engine=None):
+    """prompt [batch, seq_len] int64 token ids -> [batch, steps] generated ids. `engine` may
+    pass in a GraphedWavefrontEngine captured earlier (for repeated decodes)."""
     from wavefront.wavefront_graph import GraphedWavefrontEngine
     if prompt.dim() != 2 or prompt.shape[1] != model.config.grid_shape[1]:
         raise ValueError(f"prompt must be [batch, {model.config.grid_shape[1]}]")
-    engine = None
     window = prompt.clone()
-    if graphed and steps > 0:
+    if engine is None and graphed and steps > 0:
         x = model.emb_dropout(model.embedding(window))
         engine = GraphedWavefrontEngine(model.engine, x, backward=False)
     out = torch.empty(prompt.shape[0], steps, dtype=prompt.dtype, device=prompt.device)

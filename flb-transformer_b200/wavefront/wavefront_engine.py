@@ -202,11 +202,11 @@ class WavefrontEngine(nn.Module):
             self.gathered_out_buffer, self.stacked_params, self.bwd_cache, self.graph_workspace,
             self.spatial_map_buffer, self.batched_forward, *states)
 
-    def graphed(self, x: torch.Tensor, warmup: int = 2):
-        """This engine's per-tick forward and backward captured as CUDA graphs for inputs shaped
-        like `x` (wavefront.wavefront_graph.GraphedWavefrontEngine)."""
+    def graphed(self, x: torch.Tensor, warmup: int = 2, backward: bool = True):
+        """This engine's per-tick forward (and backward) captured as CUDA graphs for inputs
+        shaped like `x` (wavefront.wavefront_graph.GraphedWavefrontEngine)."""
         from .wavefront_graph import GraphedWavefrontEngine
-        return GraphedWavefrontEngine(self, x, warmup=warmup)
+        return GraphedWavefrontEngine(self, x, warmup=warmup, backward=backward)
 
     # ---- host-side set-up (reference :275-438) ------------------------------------------------
     def _init_buffers(self, x):
