@@ -525,9 +525,11 @@ struct BwdCfg {
   static constexpr int OFF_P = OFF_Q + 2 * TILE;
   static constexpr int OFF_SC = OFF_P + BM * BN * 2;
   static constexpr int DS_LD = BN + 8;                     // row pitch (halves) of the dS tile
-  static constexpr int OFF_DS = OFF_SC + 2 * SC_BOX;       // fp16 [128 x DS_LD]
-  static constexpr int OFF_DQ = OFF_DS + BM * DS_LD * 2;   // fp32 [128 x 64]
-  static constexpr int SMEM = OFF_DQ + BM * D * 4 + 1024;
+  // dS and dQ tiles carry one extra row: a zero dS row and a dummy dQ row that an odd last
+  // row of phase B's two-row step points at, so that step needs no branch
+  static constexpr int OFF_DS = OFF_SC + 2 * SC_BOX;             // fp16 [129 x DS_LD]
+  static constexpr int OFF_DQ = OFF_DS + (BM + 1) * DS_LD * 2;   // fp32 [129 x 64]
+  static constexpr int SMEM = OFF_DQ + (BM + 1) * D * 4 + 1024;
   static constexpr int TMEM_COLS = 256;                    // dP: [0,128), dV: [128,192)
   static_assert(OFF_P % 1024 == 0 && OFF_SC % 1024 == 0, "swizzled boxes need 1 KB alignment");
 };
@@ -612,7 +614,9 @@ attn_bwd_tc_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constan
     tmem_relinquish();
   }
   float* sDQ = reinterpret_cast<float*>(sm + C::OFF_DQ);
-  for (int i = tid; i < C::BM * D; i += NT) sDQ[i] = 0.f;
+  for (int i = tid; i < (C::BM + 1) * D; i += NT) sDQ[i] = 0.f;
+  if (tid < C::DS_LD)
+    reinterpret_cast<__half*>(sm + C::OFF_DS)[C::BM * C::DS_LD + tid] = __float2half(0.f);
   // phase B ownership: warp w holds keys 8w..8w+7 of the block, lane l holds head dims 2l, 2l+1
   __half2 kr[8];
 #pragma unroll
@@ -858,19 +862,20 @@ attn_bwd_tc_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constan
       const __half2* qp = sQh + r_lo * (D / 2) + lane;
       const uint4* dsp = reinterpret_cast<const uint4*>(sDS + warp * 8) + r_lo * DS_ROW;
       float* dqp = sDQ + r_lo * D + lane;
+      const uint4* dsp_zero = reinterpret_cast<const uint4*>(sDS + warp * 8) + C::BM * DS_ROW;
+      float* dqp_dummy = sDQ + C::BM * D + lane;
       __half2 ta[8], tb[8];
       if (r_lo < rmax) tanh_row(qp, ta);
-      // two rows per iteration; near the end the clamped row offset recomputes the last row
-      // rather than branch
+      // two rows per iteration, branch-free: an odd last row pairs with the zero dS row (its
+      // contributions are exactly zero) and the dummy dQ row; the clamped Q offsets read valid
+      // rows whose results go unused
 #pragma unroll 1
       for (int r = r_lo; r < rmax; r += 2) {
         const bool two = r + 1 < rmax, three = r + 2 < rmax;
         tanh_row(qp + (two ? D / 2 : 0), tb);
         __half2 dw2 = sums_row(dsp, dqp, ta);  // dw over both rows: |sum| <= 16 * 512
-        if (two) {
-          tanh_row(qp + (three ? D : D / 2), ta);
-          dw2 = __hadd2(dw2, sums_row(dsp + DS_ROW, dqp + D, tb));
-        }
+        tanh_row(qp + (three ? D : (two ? D / 2 : 0)), ta);
+        dw2 = __hadd2(dw2, sums_row(two ? dsp + DS_ROW : dsp_zero, two ? dqp + D : dqp_dummy, tb));
         qp += D;
         dsp += 2 * DS_ROW;
         dqp += 2 * D;
