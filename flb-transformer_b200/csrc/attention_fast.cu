@@ -826,7 +826,6 @@ attn_bwd_tc_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constan
       __half2 dk2[8];
 #pragma unroll
       for (int j = 0; j < 8; ++j) dk2[j] = hz;
-      int pending = 0;  // rows accumulated in dk2 since the last flush
       // rows are addressed through running pointers (row strides: Q 32 half2, dS DS_LD halves,
       // dQ partials D floats)
       constexpr int DS_ROW = C::DS_LD / 8;  // uint4 per dS row
@@ -869,37 +868,33 @@ attn_bwd_tc_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constan
       // two rows per iteration, branch-free: an odd last row pairs with the zero dS row (its
       // contributions are exactly zero) and the dummy dQ row; the clamped Q offsets read valid
       // rows whose results go unused
+      // chunks of 32 rows: dk2 holds at most 32 rows (|sum| <= 32 * 512) and is moved to the
+      // fp32 accumulators after each chunk
 #pragma unroll 1
-      for (int r = r_lo; r < rmax; r += 2) {
-        const bool two = r + 1 < rmax, three = r + 2 < rmax;
-        tanh_row(qp + (two ? D / 2 : 0), tb);
-        __half2 dw2 = sums_row(dsp, dqp, ta);  // dw over both rows: |sum| <= 16 * 512
-        tanh_row(qp + (three ? D : (two ? D / 2 : 0)), ta);
-        dw2 = __hadd2(dw2, sums_row(two ? dsp + DS_ROW : dsp_zero, two ? dqp + D : dqp_dummy, tb));
-        qp += D;
-        dsp += 2 * DS_ROW;
-        dqp += 2 * D;
-        const float2 dwf = __half22float2(dw2);
-        dwa0 = fmaf(dwf.x, ds_unscale, dwa0);
-        dwa1 = fmaf(dwf.y, ds_unscale, dwa1);
-        // dk2 holds at most 32 rows: |sum| <= 32 * 512
-        pending += 2;
-        if (pending >= 32) {
-#pragma unroll
-          for (int j = 0; j < 8; ++j) {
-            const float2 f = __half22float2(dk2[j]);
-            dka[j][0] = fmaf(f.x, ds_unscale, dka[j][0]);
-            dka[j][1] = fmaf(f.y, ds_unscale, dka[j][1]);
-            dk2[j] = hz;
-          }
-          pending = 0;
+      for (int c0 = r_lo; c0 < rmax; c0 += 32) {
+        const int cend = min(c0 + 32, rmax);
+#pragma unroll 1
+        for (int r = c0; r < cend; r += 2) {
+          const bool two = r + 1 < rmax, three = r + 2 < rmax;
+          tanh_row(qp + (two ? D / 2 : 0), tb);
+          __half2 dw2 = sums_row(dsp, dqp, ta);  // dw over both rows: |sum| <= 16 * 512
+          tanh_row(qp + (three ? D : (two ? D / 2 : 0)), ta);
+          dw2 = __hadd2(dw2, sums_row(two ? dsp + DS_ROW : dsp_zero, two ? dqp + D : dqp_dummy,
+                                      tb));
+          qp += D;
+          dsp += 2 * DS_ROW;
+          dqp += 2 * D;
+          const float2 dwf = __half22float2(dw2);
+          dwa0 = fmaf(dwf.x, ds_unscale, dwa0);
+          dwa1 = fmaf(dwf.y, ds_unscale, dwa1);
         }
-      }
 #pragma unroll
-      for (int j = 0; j < 8; ++j) {
-        const float2 f = __half22float2(dk2[j]);
-        dka[j][0] = fmaf(f.x, ds_unscale, dka[j][0]);
-        dka[j][1] = fmaf(f.y, ds_unscale, dka[j][1]);
+        for (int j = 0; j < 8; ++j) {
+          const float2 f = __half22float2(dk2[j]);
+          dka[j][0] = fmaf(f.x, ds_unscale, dka[j][0]);
+          dka[j][1] = fmaf(f.y, ds_unscale, dka[j][1]);
+          dk2[j] = hz;
+        }
       }
     }
     __syncthreads();
