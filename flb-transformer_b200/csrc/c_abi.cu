@@ -208,6 +208,8 @@ int flb_block_grid_fwd(const flb_block_weights* weights, const void* x, void* gr
     return fail(FLB_ERR_SHAPE, "block_grid_fwd: sizes must be positive (D >= 16)");
   if (D % 16 != 0 || D % heads != 0)
     return fail(FLB_ERR_SHAPE, "block_grid_fwd: D must be a multiple of 16 and of heads");
+  if (D > 1024 || D / heads > 128)
+    return fail(FLB_ERR_UNSUPPORTED, "block_grid_fwd: D <= 1024 and D / heads <= 128 required");
   if ((L * S + L) * batch * D * 4 > ((int64_t)1 << 40) || 3 * batch * D > (1 << 30))
     return fail(FLB_ERR_SHAPE, "block_grid_fwd: grid too large");
   const size_t need = block_grid_workspace_bytes(L, S, batch, D);

@@ -22,8 +22,6 @@
 // P @ V) over the 3 tokens.
 #include <cuda_bf16.h>
 
-#include <algorithm>
-
 #include "blas.cuh"
 #include "common.cuh"
 
@@ -49,6 +47,9 @@ __device__ __forceinline__ int64_t cell_row(int l, int t, int S) { return (int64
 
 // 1. LayerNorm of the left (which 0) and bottom-left (which 1) neighbours; zero boundary rows
 //    (t = 0, or l = L-1 for the bottom-left) normalise to the LayerNorm bias as in torch.
+//    One warp per row, the row held in registers as 16-byte chunks (D <= 1024).
+constexpr int kMaxChunks = 4;  // per lane: 4 x 8 bf16 -> D <= 32 * 32 = 1024
+
 __global__ void blk_ln_kernel(const bf16* __restrict__ g_left, const bf16* __restrict__ g_diag,
                               const float* __restrict__ lw0, const float* __restrict__ lb0,
                               const float* __restrict__ lw1, const float* __restrict__ lb1,
@@ -62,26 +63,46 @@ __global__ void blk_ln_kernel(const bf16* __restrict__ g_left, const bf16* __res
   const bf16* src = nullptr;
   if (which == 0 && t > 0) src = g_left + (cell_row(l, t - 1, S) * B + b) * D;
   if (which == 1 && t > 0 && l + 1 < L) src = g_diag + (cell_row(l + 1, t - 1, S) * B + b) * D;
-  const float* w = (which ? lw1 : lw0) + (int64_t)l * D;
-  const float* bb = (which ? lb1 : lb0) + (int64_t)l * D;
+  const int nch = D / 8;
+  float v[kMaxChunks][8];
   float s = 0.f, ss = 0.f;
-  if (src) {
-    for (int j = lane; j < D / 2; j += 32) {
-      const float2 v = __bfloat1622float2(reinterpret_cast<const __nv_bfloat162*>(src)[j]);
-      s += v.x + v.y;
-      ss += v.x * v.x + v.y * v.y;
+#pragma unroll
+  for (int k = 0; k < kMaxChunks; ++k) {
+    const int c = lane + 32 * k;
+    uint4 raw = make_uint4(0, 0, 0, 0);
+    if (src && c < nch) raw = reinterpret_cast<const uint4*>(src)[c];
+    const uint32_t* r = reinterpret_cast<const uint32_t*>(&raw);
+#pragma unroll
+    for (int e = 0; e < 4; ++e) {
+      const float2 f = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&r[e]));
+      v[k][2 * e] = f.x;
+      v[k][2 * e + 1] = f.y;
+      s += f.x + f.y;
+      ss += f.x * f.x + f.y * f.y;
     }
   }
   s = warp_sum(s);
   ss = warp_sum(ss);
   const float mean = s / D;
   const float rstd = rsqrtf(fmaxf(ss / D - mean * mean, 0.f) + eps);
-  __nv_bfloat162* dst = reinterpret_cast<__nv_bfloat162*>(out + (int64_t)row * D);
-  for (int j = lane; j < D / 2; j += 32) {
-    float2 v = make_float2(0.f, 0.f);
-    if (src) v = __bfloat1622float2(reinterpret_cast<const __nv_bfloat162*>(src)[j]);
-    dst[j] = __floats2bfloat162_rn((v.x - mean) * rstd * w[2 * j] + bb[2 * j],
-                                   (v.y - mean) * rstd * w[2 * j + 1] + bb[2 * j + 1]);
+  const float4* w4 = reinterpret_cast<const float4*>((which ? lw1 : lw0) + (int64_t)l * D);
+  const float4* b4 = reinterpret_cast<const float4*>((which ? lb1 : lb0) + (int64_t)l * D);
+  uint4* dst = reinterpret_cast<uint4*>(out + (int64_t)row * D);
+#pragma unroll
+  for (int k = 0; k < kMaxChunks; ++k) {
+    const int c = lane + 32 * k;
+    if (c >= nch) break;
+    const float4 wa = w4[2 * c], wb = w4[2 * c + 1], ba = b4[2 * c], bb = b4[2 * c + 1];
+    const float wv[8] = {wa.x, wa.y, wa.z, wa.w, wb.x, wb.y, wb.z, wb.w};
+    const float bv[8] = {ba.x, ba.y, ba.z, ba.w, bb.x, bb.y, bb.z, bb.w};
+    uint32_t o[4];
+#pragma unroll
+    for (int e = 0; e < 4; ++e) {
+      const __nv_bfloat162 h = __floats2bfloat162_rn((v[k][2 * e] - mean) * rstd * wv[2 * e] + bv[2 * e],
+                                                     (v[k][2 * e + 1] - mean) * rstd * wv[2 * e + 1] + bv[2 * e + 1]);
+      o[e] = *reinterpret_cast<const uint32_t*>(&h);
+    }
+    dst[c] = make_uint4(o[0], o[1], o[2], o[3]);
   }
 }
 
@@ -92,26 +113,25 @@ __device__ __forceinline__ const bf16* top_row(const bf16* g0, const bf16* x, in
 }
 
 // 3./4. gates: dst = m * sigmoid(z + bias[l]) with m = lat_prior (mode 0) or the top neighbour
-//    (mode 1); dst rows have a pitch of 3D (a token slot of the [cells, B, 3, D] token tensor)
+//    (mode 1); dst rows have a pitch of 3D (a token slot of the [cells, B, 3, D] token tensor).
+//    Grid: x over bf16 pairs of a row, y over the tick's (cell, batch) rows.
 __global__ void blk_gate_kernel(const bf16* __restrict__ z, const float* __restrict__ bias,
                                 const bf16* __restrict__ m, const bf16* __restrict__ g0,
                                 const bf16* __restrict__ x, int mode, bf16* __restrict__ dst,
-                                int T, int l0, int n, int S, int B, int D) {
-  const int64_t pairs = (int64_t)n * B * (D / 2);
-  for (int64_t e = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; e < pairs;
-       e += (int64_t)gridDim.x * blockDim.x) {
-    const int j = (int)(e % (D / 2));
-    const int64_t rb = e / (D / 2);  // i * B + b
-    const int i = (int)(rb / B), b = (int)(rb % B);
-    const int l = l0 + 2 * i, t = (T - l) / 2;
-    const float2 zz = __bfloat1622float2(reinterpret_cast<const __nv_bfloat162*>(z + rb * D)[j]);
-    const bf16* mrow = mode == 0 ? m + rb * D : top_row(g0, x, l, t, b, S, B, D);
-    const float2 mm = __bfloat1622float2(reinterpret_cast<const __nv_bfloat162*>(mrow)[j]);
-    const float* bl = bias + (int64_t)l * D + 2 * j;
-    const float s0 = 1.f / (1.f + __expf(-(zz.x + bl[0])));
-    const float s1 = 1.f / (1.f + __expf(-(zz.y + bl[1])));
-    reinterpret_cast<__nv_bfloat162*>(dst + rb * 3 * D)[j] = __floats2bfloat162_rn(mm.x * s0, mm.y * s1);
-  }
+                                int T, int l0, int S, int B, int D) {
+  const int j = blockIdx.x * blockDim.x + threadIdx.x;
+  if (j >= D / 2) return;
+  const int rb = blockIdx.y;  // i * B + b
+  const int i = rb / B, b = rb - i * B;
+  const int l = l0 + 2 * i, t = (T - l) / 2;
+  const float2 zz = __bfloat1622float2(reinterpret_cast<const __nv_bfloat162*>(z + (int64_t)rb * D)[j]);
+  const bf16* mrow = mode == 0 ? m + (int64_t)rb * D : top_row(g0, x, l, t, b, S, B, D);
+  const float2 mm = __bfloat1622float2(reinterpret_cast<const __nv_bfloat162*>(mrow)[j]);
+  const float2 bl = reinterpret_cast<const float2*>(bias + (int64_t)l * D)[j];
+  const float s0 = 1.f / (1.f + __expf(-(zz.x + bl.x)));
+  const float s1 = 1.f / (1.f + __expf(-(zz.y + bl.y)));
+  reinterpret_cast<__nv_bfloat162*>(dst + (int64_t)rb * 3 * D)[j] =
+      __floats2bfloat162_rn(mm.x * s0, mm.y * s1);
 }
 
 // 6. additive attention over the 3 tokens, one warp per (cell, batch row, head). qkv rows are
@@ -133,7 +153,10 @@ __global__ void blk_attn3_kernel(const bf16* __restrict__ qkv, const float* __re
   for (int a = 0; a < 3; ++a)
 #pragma unroll
     for (int c = 0; c < 3; ++c) s[a][c] = 0.f;
-  for (int d = lane; d < dh; d += 32) {
+#pragma unroll
+  for (int kk = 0; kk < 4; ++kk) {  // dh <= 128
+    const int d = lane + 32 * kk;
+    if (d >= dh) break;
     float q[3], k[3];
 #pragma unroll
     for (int r = 0; r < 3; ++r) {
@@ -166,7 +189,10 @@ __global__ void blk_attn3_kernel(const bf16* __restrict__ qkv, const float* __re
     for (int c = 0; c < 3; ++c) p[a][c] /= l;
   }
   bf16* out = att + rb * 3 * D + h * dh;
-  for (int d = lane; d < dh; d += 32) {
+#pragma unroll
+  for (int kk = 0; kk < 4; ++kk) {
+    const int d = lane + 32 * kk;
+    if (d >= dh) break;
     float v[3];
 #pragma unroll
     for (int r = 0; r < 3; ++r) v[r] = __bfloat162float(base[r * 3 * D + 2 * D + d]);
@@ -176,38 +202,36 @@ __global__ void blk_attn3_kernel(const bf16* __restrict__ qkv, const float* __re
   }
 }
 
-// 8. residuals and the auxiliary loss, written into the four port grids at the tick's cells
+// 8. residuals and the auxiliary loss, written into the four port grids at the tick's cells.
+//    Grid: x over bf16 pairs of a row, y over the tick's (cell, batch) rows.
 __global__ void blk_out_kernel(const bf16* __restrict__ o, const bf16* __restrict__ lat_prior,
                                const bf16* __restrict__ tok, const bf16* __restrict__ x,
                                bf16* __restrict__ grids, int64_t port_stride, int T, int l0,
-                               int n, int S, int B, int D) {
-  const int64_t pairs = (int64_t)n * B * (D / 2);
-  for (int64_t e = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; e < pairs;
-       e += (int64_t)gridDim.x * blockDim.x) {
-    const int j = (int)(e % (D / 2));
-    const int64_t rb = e / (D / 2);
-    const int i = (int)(rb / B), b = (int)(rb % B);
-    const int l = l0 + 2 * i, t = (T - l) / 2;
-    auto ld2 = [&](const bf16* p) {
-      return __bfloat1622float2(reinterpret_cast<const __nv_bfloat162*>(p)[j]);
-    };
-    const float2 o0 = ld2(o + (rb * 3 + 0) * D), o1 = ld2(o + (rb * 3 + 1) * D),
-                 o2 = ld2(o + (rb * 3 + 2) * D);
-    const float2 top = ld2(top_row(grids, x, l, t, b, S, B, D));
-    const float2 lp = ld2(lat_prior + rb * D), fp = ld2(tok + (rb * 3 + 2) * D);
-    // the outputs as stored (bf16), as the aux term sees them
-    const __nv_bfloat162 hx = __floats2bfloat162_rn(o0.x + top.x, o0.y + top.y);
-    const __nv_bfloat162 hl = __floats2bfloat162_rn(o1.x + lp.x, o1.y + lp.y);
-    const __nv_bfloat162 hf = __floats2bfloat162_rn(o2.x + fp.x, o2.y + fp.y);
-    const float2 hlf = __bfloat1622float2(hl), hff = __bfloat1622float2(hf);
-    const float ax = (lp.x - hlf.x) * (lp.x - hlf.x) + (fp.x - hff.x) * (fp.x - hff.x);
-    const float ay = (lp.y - hlf.y) * (lp.y - hlf.y) + (fp.y - hff.y) * (fp.y - hff.y);
-    const int64_t off = (cell_row(l, t, S) * B + b) * D;
-    reinterpret_cast<__nv_bfloat162*>(grids + off)[j] = hx;
-    reinterpret_cast<__nv_bfloat162*>(grids + port_stride + off)[j] = hl;
-    reinterpret_cast<__nv_bfloat162*>(grids + 2 * port_stride + off)[j] = hf;
-    reinterpret_cast<__nv_bfloat162*>(grids + 3 * port_stride + off)[j] = __floats2bfloat162_rn(ax, ay);
-  }
+                               int S, int B, int D) {
+  const int j = blockIdx.x * blockDim.x + threadIdx.x;
+  if (j >= D / 2) return;
+  const int rb = blockIdx.y;
+  const int i = rb / B, b = rb - i * B;
+  const int l = l0 + 2 * i, t = (T - l) / 2;
+  auto ld2 = [&](const bf16* p) {
+    return __bfloat1622float2(reinterpret_cast<const __nv_bfloat162*>(p)[j]);
+  };
+  const int64_t r3 = (int64_t)rb * 3;
+  const float2 o0 = ld2(o + r3 * D), o1 = ld2(o + (r3 + 1) * D), o2 = ld2(o + (r3 + 2) * D);
+  const float2 top = ld2(top_row(grids, x, l, t, b, S, B, D));
+  const float2 lp = ld2(lat_prior + (int64_t)rb * D), fp = ld2(tok + (r3 + 2) * D);
+  // the outputs as stored (bf16), as the aux term sees them
+  const __nv_bfloat162 hx = __floats2bfloat162_rn(o0.x + top.x, o0.y + top.y);
+  const __nv_bfloat162 hl = __floats2bfloat162_rn(o1.x + lp.x, o1.y + lp.y);
+  const __nv_bfloat162 hf = __floats2bfloat162_rn(o2.x + fp.x, o2.y + fp.y);
+  const float2 hlf = __bfloat1622float2(hl), hff = __bfloat1622float2(hf);
+  const float ax = (lp.x - hlf.x) * (lp.x - hlf.x) + (fp.x - hff.x) * (fp.x - hff.x);
+  const float ay = (lp.y - hlf.y) * (lp.y - hlf.y) + (fp.y - hff.y) * (fp.y - hff.y);
+  const int64_t off = (cell_row(l, t, S) * B + b) * D;
+  reinterpret_cast<__nv_bfloat162*>(grids + off)[j] = hx;
+  reinterpret_cast<__nv_bfloat162*>(grids + port_stride + off)[j] = hl;
+  reinterpret_cast<__nv_bfloat162*>(grids + 2 * port_stride + off)[j] = hf;
+  reinterpret_cast<__nv_bfloat162*>(grids + 3 * port_stride + off)[j] = __floats2bfloat162_rn(ax, ay);
 }
 
 constexpr size_t kBlkBlasWs = 32u << 20;
@@ -268,7 +292,6 @@ int block_grid_fwd(const flb_block_weights* W, const void* x, void* grids, int64
   const long long DD = D * D, BD = B * D;
   const int Li = (int)L, Si = (int)S, Bi = (int)B, Di = (int)D, Hi = (int)H;
   const int ticks = (int)(L + 2 * S - 2);
-  const int blocks_ew = 4 * num_sms();
   int launches = 0;
   for (int T = 0; T < ticks; ++T) {
     const Tick tk = tick_of(T, Li, Si);
@@ -296,16 +319,15 @@ int block_grid_fwd(const flb_block_weights* W, const void* x, void* grids, int64
     if ((st = gemm_rm(hb, false, true, Bi, Di, Di, w.tok + 2 * D, 3 * Di, 3 * BD, Wgl, Di, 2 * DD,
                       w.z, Di, BD, n, 0.f, CUDA_R_16BF)) != FLB_OK)
       return st;
-    const int64_t pairs = (int64_t)n * B * D / 2;
-    const int gblocks = (int)std::min<int64_t>((pairs + 255) / 256, blocks_ew);
-    blk_gate_kernel<<<gblocks, 256, 0, s>>>(w.z, W->b_gate_l, w.lat, g, xb, 0, w.tok + D, T, l0, n,
+    const dim3 ew_grid((unsigned)((D / 2 + 127) / 128), (unsigned)(n * Bi));
+    blk_gate_kernel<<<ew_grid, 128, 0, s>>>(w.z, W->b_gate_l, w.lat, g, xb, 0, w.tok + D, T, l0,
                                             Si, Bi, Di);
     // sensory gate
     if ((st = gemm_rm(hb, false, true, Bi, Di, Di, w.tok + D, 3 * Di, 3 * BD, Wgx, Di, 2 * DD, w.z,
                       Di, BD, n, 0.f, CUDA_R_16BF)) != FLB_OK)
       return st;
-    blk_gate_kernel<<<gblocks, 256, 0, s>>>(w.z, W->b_gate_x, nullptr, g, xb, 1, w.tok, T, l0, n,
-                                            Si, Bi, Di);
+    blk_gate_kernel<<<ew_grid, 128, 0, s>>>(w.z, W->b_gate_x, nullptr, g, xb, 1, w.tok, T, l0, Si,
+                                            Bi, Di);
     // q | k | v of the 3 tokens: [n, 3B, D] x [3D, D]^T
     if ((st = gemm_rm(hb, false, true, 3 * Bi, 3 * Di, Di, w.tok, Di, 3 * BD, Wqkv, Di, 6 * DD,
                       w.qkv, 3 * Di, 9 * BD, n, 0.f, CUDA_R_16BF)) != FLB_OK)
@@ -315,7 +337,7 @@ int block_grid_fwd(const flb_block_weights* W, const void* x, void* grids, int64
     if ((st = gemm_rm(hb, false, true, 3 * Bi, Di, Di, w.att, Di, 3 * BD, Wo, Di, 2 * DD, w.o, Di,
                       3 * BD, n, 0.f, CUDA_R_16BF)) != FLB_OK)
       return st;
-    blk_out_kernel<<<gblocks, 256, 0, s>>>(w.o, w.lat, w.tok, xb, g, port_stride, T, l0, n, Si, Bi,
+    blk_out_kernel<<<ew_grid, 128, 0, s>>>(w.o, w.lat, w.tok, xb, g, port_stride, T, l0, Si, Bi,
                                            Di);
     launches += 6;  // own kernels (the GEMMs are cuBLAS's)
   }

@@ -52,7 +52,8 @@ def native_flb_applies(engine, x: torch.Tensor) -> bool:
     eps = layers[0].norm_lat.eps
     same = all(l.flb_attention.num_heads == H and l.norm_lat.eps == eps and l.norm_fdbk.eps == eps
                for l in layers)
-    return (same and compute == torch.bfloat16 and D % 16 == 0 and D % H == 0
+    return (same and compute == torch.bfloat16 and D % 16 == 0 and D % H == 0 and D <= 1024
+            and D // H <= 128
             and tuple(x.shape) == (cfg.batch_size, cfg.grid_shape[1], D))
 
 

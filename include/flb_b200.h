@@ -218,7 +218,8 @@ size_t flb_block_grid_workspace_bytes(int64_t L, int64_t S, int64_t batch, int64
  * x: bf16 [batch, S, D] (row 0's top input). grids: bf16 [4, L*S + L, batch, D], the engine's
  * port grids (cell l*S + t; the last L rows are its boundary dock and are not touched); every
  * cell of ports 0-3 is written: h_x, h_lat, h_fdbk and the auxiliary loss term. D must be a
- * multiple of 16 and of `heads`; ln_eps is the LayerNorms' epsilon. */
+ * multiple of 16 and of `heads`, D <= 1024 and D / heads <= 128; ln_eps is the LayerNorms'
+ * epsilon. */
 int flb_block_grid_fwd(const flb_block_weights* weights, const void* x, void* grids,
                        int64_t L, int64_t S, int64_t batch, int64_t D, int64_t heads,
                        float ln_eps, void* workspace, size_t workspace_bytes, void* stream);
