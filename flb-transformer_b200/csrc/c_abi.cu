@@ -54,6 +54,11 @@ size_t block_grid_workspace_bytes(int64_t L, int64_t S, int64_t B, int64_t D);
 int block_grid_fwd(const flb_block_weights* W, const void* x, void* grids, int64_t L, int64_t S,
                    int64_t B, int64_t D, int64_t H, float eps, void* ws, size_t ws_bytes,
                    cudaStream_t s);
+size_t block_grid_bwd_workspace_bytes(int64_t L, int64_t S, int64_t B, int64_t D);
+int block_grid_bwd(const flb_block_weights* W, const void* x, const void* grids,
+                   const void* const* dgrids, float* dx, const flb_block_grads* G, int64_t L,
+                   int64_t S, int64_t B, int64_t D, int64_t H, float eps, void* ws,
+                   size_t ws_bytes, cudaStream_t s);
 size_t grid_workspace_bytes(int64_t R, int64_t C, int64_t B, int64_t H, int64_t G, int has_U);
 int grid_fwd(const void* x, int x_layout, const void* W_l, const void* W_t, const void* U,
              const float* bias, const void* top, void* h_out, int64_t R, int64_t C, int64_t B,
@@ -86,6 +91,29 @@ static int check_attn_common(const void* q, const void* k, const void* v, const 
   const size_t es = (size_t)dtype_size(dtype);
   if (!aligned(q, es) || !aligned(k, es) || !aligned(v, es) || !aligned(w, 4) || !aligned(wi, 4))
     return fail(FLB_ERR_ALIGN, "attention: pointers must be aligned to their element size");
+  return FLB_OK;
+}
+
+static int check_block_args(const flb_block_weights* weights, const void* x, const void* grids,
+                            int64_t L, int64_t S, int64_t batch, int64_t D, int64_t heads) {
+  if (!weights || !x || !grids) return fail(FLB_ERR_SHAPE, "block_grid: null pointer");
+  const flb_block_weights& w = *weights;
+  if (!w.ln_lat_w || !w.ln_lat_b || !w.ln_fdbk_w || !w.ln_fdbk_b || !w.w_prior_lat ||
+      !w.w_prior_fdbk || !w.w_gate_l || !w.b_gate_l || !w.w_gate_x || !w.b_gate_x || !w.w_qkv ||
+      !w.w_o || !w.v_a)
+    return fail(FLB_ERR_SHAPE, "block_grid: null weight pointer");
+  if (L < 1 || S < 1 || batch < 1 || D < 16 || heads < 1)
+    return fail(FLB_ERR_SHAPE, "block_grid: sizes must be positive (D >= 16)");
+  if (D % 16 != 0 || D % heads != 0)
+    return fail(FLB_ERR_SHAPE, "block_grid: D must be a multiple of 16 and of heads");
+  if (D > 1024 || D / heads > 128)
+    return fail(FLB_ERR_UNSUPPORTED, "block_grid: D <= 1024 and D / heads <= 128 required");
+  if ((L * S + L) * batch * D * 4 > ((int64_t)1 << 40) || 3 * batch * D > (1 << 30) ||
+      L + 2 * S > (1 << 30))
+    return fail(FLB_ERR_SHAPE, "block_grid: grid too large");
+  if (((uintptr_t)x | (uintptr_t)grids | (uintptr_t)w.w_prior_lat | (uintptr_t)w.w_prior_fdbk |
+       (uintptr_t)w.w_gate_l | (uintptr_t)w.w_gate_x | (uintptr_t)w.w_qkv | (uintptr_t)w.w_o) & 15u)
+    return fail(FLB_ERR_ALIGN, "block_grid: bf16 tensors must be 16-byte aligned");
   return FLB_OK;
 }
 
@@ -198,28 +226,42 @@ size_t flb_block_grid_workspace_bytes(int64_t L, int64_t S, int64_t batch, int64
 int flb_block_grid_fwd(const flb_block_weights* weights, const void* x, void* grids, int64_t L,
                        int64_t S, int64_t batch, int64_t D, int64_t heads, float ln_eps,
                        void* workspace, size_t workspace_bytes, void* stream) {
-  if (!weights || !x || !grids) return fail(FLB_ERR_SHAPE, "block_grid_fwd: null pointer");
-  const flb_block_weights& w = *weights;
-  if (!w.ln_lat_w || !w.ln_lat_b || !w.ln_fdbk_w || !w.ln_fdbk_b || !w.w_prior_lat ||
-      !w.w_prior_fdbk || !w.w_gate_l || !w.b_gate_l || !w.w_gate_x || !w.b_gate_x || !w.w_qkv ||
-      !w.w_o || !w.v_a)
-    return fail(FLB_ERR_SHAPE, "block_grid_fwd: null weight pointer");
-  if (L < 1 || S < 1 || batch < 1 || D < 16 || heads < 1)
-    return fail(FLB_ERR_SHAPE, "block_grid_fwd: sizes must be positive (D >= 16)");
-  if (D % 16 != 0 || D % heads != 0)
-    return fail(FLB_ERR_SHAPE, "block_grid_fwd: D must be a multiple of 16 and of heads");
-  if (D > 1024 || D / heads > 128)
-    return fail(FLB_ERR_UNSUPPORTED, "block_grid_fwd: D <= 1024 and D / heads <= 128 required");
-  if ((L * S + L) * batch * D * 4 > ((int64_t)1 << 40) || 3 * batch * D > (1 << 30))
-    return fail(FLB_ERR_SHAPE, "block_grid_fwd: grid too large");
+  int st = check_block_args(weights, x, grids, L, S, batch, D, heads);
+  if (st != FLB_OK) return st;
   const size_t need = block_grid_workspace_bytes(L, S, batch, D);
   if (!workspace || workspace_bytes < need)
     return fail(FLB_ERR_WORKSPACE, "block_grid_fwd: workspace smaller than flb_block_grid_workspace_bytes()");
-  if (((uintptr_t)x | (uintptr_t)grids | (uintptr_t)w.w_prior_lat | (uintptr_t)w.w_prior_fdbk |
-       (uintptr_t)w.w_gate_l | (uintptr_t)w.w_gate_x | (uintptr_t)w.w_qkv | (uintptr_t)w.w_o) & 15u)
-    return fail(FLB_ERR_ALIGN, "block_grid_fwd: bf16 tensors must be 16-byte aligned");
   return block_grid_fwd(weights, x, grids, L, S, batch, D, heads, ln_eps, workspace,
                         workspace_bytes, as_stream(stream));
+}
+
+size_t flb_block_grid_bwd_workspace_bytes(int64_t L, int64_t S, int64_t batch, int64_t D) {
+  if (L < 1 || S < 1 || batch < 1 || D < 1) return 0;
+  return block_grid_bwd_workspace_bytes(L, S, batch, D);
+}
+
+int flb_block_grid_bwd(const flb_block_weights* weights, const void* x, const void* grids,
+                       const void* dgrid0, const void* dgrid1, const void* dgrid2,
+                       const void* dgrid3, float* dx, const flb_block_grads* grads, int64_t L,
+                       int64_t S, int64_t batch, int64_t D, int64_t heads, float ln_eps,
+                       void* workspace, size_t workspace_bytes, void* stream) {
+  int st = check_block_args(weights, x, grids, L, S, batch, D, heads);
+  if (st != FLB_OK) return st;
+  if (!dx || !grads) return fail(FLB_ERR_SHAPE, "block_grid_bwd: null dx or grads");
+  const flb_block_grads& g = *grads;
+  if (!g.ln_lat_w || !g.ln_lat_b || !g.ln_fdbk_w || !g.ln_fdbk_b || !g.w_prior_lat ||
+      !g.w_prior_fdbk || !g.w_gate_l || !g.b_gate_l || !g.w_gate_x || !g.b_gate_x || !g.w_qkv ||
+      !g.w_o || !g.v_a)
+    return fail(FLB_ERR_SHAPE, "block_grid_bwd: null gradient pointer");
+  if (((uintptr_t)dgrid0 | (uintptr_t)dgrid1 | (uintptr_t)dgrid2 | (uintptr_t)dgrid3 |
+       (uintptr_t)dx) & 15u)
+    return fail(FLB_ERR_ALIGN, "block_grid_bwd: gradient grids and dx must be 16-byte aligned");
+  const size_t need = block_grid_bwd_workspace_bytes(L, S, batch, D);
+  if (!workspace || workspace_bytes < need)
+    return fail(FLB_ERR_WORKSPACE, "block_grid_bwd: workspace smaller than flb_block_grid_bwd_workspace_bytes()");
+  const void* dg[4] = {dgrid0, dgrid1, dgrid2, dgrid3};
+  return block_grid_bwd(weights, x, grids, dg, dx, grads, L, S, batch, D, heads, ln_eps,
+                        workspace, workspace_bytes, as_stream(stream));
 }
 
 size_t flb_grid_workspace_bytes(int64_t R, int64_t C, int64_t B, int64_t H, int64_t G, int has_U) {

@@ -22,6 +22,8 @@
 // P @ V) over the 3 tokens.
 #include <cuda_bf16.h>
 
+#include <algorithm>
+
 #include "blas.cuh"
 #include "common.cuh"
 
@@ -278,6 +280,59 @@ size_t block_grid_workspace_bytes(int64_t L, int64_t S, int64_t B, int64_t D) {
   return block_ws_layout(max_cells_per_tick(L, S), B, D, nullptr, nullptr);
 }
 
+namespace {
+
+// Forward buffers of one tick (bf16): LayerNorm outputs [2][n][B][D], lat_prior [n][B][D],
+// tokens [n][B][3][D] (x', lat', fdbk_prior), gate pre-activations [n][B][D] (the forward reuses
+// one buffer for both), q|k|v [n][3B][3D], attention output [n][3B][D].
+struct TickBufs {
+  bf16 *ln, *lat, *tok, *zl, *zx, *qkv, *att;
+};
+
+// stages 1-6 of a tick (everything up to the attention output)
+int tick_forward(cublasHandle_t hb, const flb_block_weights* W, const bf16* xb, const bf16* g,
+                 int64_t port_stride, const TickBufs& b, int T, int l0, int n, int L, int S, int B,
+                 int D, int H, float eps, cudaStream_t s) {
+  const long long DD = (long long)D * D, BD = (long long)B * D;
+  int st;
+  blk_ln_kernel<<<(2 * n * B + 7) / 8, 256, 0, s>>>(g + port_stride, g + 2 * port_stride,
+                                                    W->ln_lat_w, W->ln_lat_b, W->ln_fdbk_w,
+                                                    W->ln_fdbk_b, b.ln, T, l0, n, L, S, B, D, eps);
+  const bf16* Wpl = reinterpret_cast<const bf16*>(W->w_prior_lat) + (int64_t)l0 * DD;
+  const bf16* Wpf = reinterpret_cast<const bf16*>(W->w_prior_fdbk) + (int64_t)l0 * DD;
+  const bf16* Wgl = reinterpret_cast<const bf16*>(W->w_gate_l) + (int64_t)l0 * DD;
+  const bf16* Wgx = reinterpret_cast<const bf16*>(W->w_gate_x) + (int64_t)l0 * DD;
+  const bf16* Wqkv = reinterpret_cast<const bf16*>(W->w_qkv) + (int64_t)l0 * 3 * DD;
+  // priors: lat_prior -> b.lat; fdbk_prior -> token slot 2 (row pitch 3D)
+  if ((st = gemm_rm(hb, false, true, B, D, D, b.ln, D, BD, Wpl, D, 2 * DD, b.lat, D, BD, n, 0.f,
+                    CUDA_R_16BF)) != FLB_OK)
+    return st;
+  if ((st = gemm_rm(hb, false, true, B, D, D, b.ln + n * BD, D, BD, Wpf, D, 2 * DD, b.tok + 2 * D,
+                    3 * D, 3 * BD, n, 0.f, CUDA_R_16BF)) != FLB_OK)
+    return st;
+  // lateral gate
+  if ((st = gemm_rm(hb, false, true, B, D, D, b.tok + 2 * D, 3 * D, 3 * BD, Wgl, D, 2 * DD, b.zl, D,
+                    BD, n, 0.f, CUDA_R_16BF)) != FLB_OK)
+    return st;
+  const dim3 ew_grid((unsigned)((D / 2 + 127) / 128), (unsigned)(n * B));
+  blk_gate_kernel<<<ew_grid, 128, 0, s>>>(b.zl, W->b_gate_l, b.lat, g, xb, 0, b.tok + D, T, l0, S,
+                                          B, D);
+  // sensory gate
+  if ((st = gemm_rm(hb, false, true, B, D, D, b.tok + D, 3 * D, 3 * BD, Wgx, D, 2 * DD, b.zx, D, BD,
+                    n, 0.f, CUDA_R_16BF)) != FLB_OK)
+    return st;
+  blk_gate_kernel<<<ew_grid, 128, 0, s>>>(b.zx, W->b_gate_x, nullptr, g, xb, 1, b.tok, T, l0, S, B,
+                                          D);
+  // q | k | v of the 3 tokens: [n, 3B, D] x [3D, D]^T
+  if ((st = gemm_rm(hb, false, true, 3 * B, 3 * D, D, b.tok, D, 3 * BD, Wqkv, D, 6 * DD, b.qkv,
+                    3 * D, 9 * BD, n, 0.f, CUDA_R_16BF)) != FLB_OK)
+    return st;
+  blk_attn3_kernel<<<(n * B * H + 7) / 8, 256, 0, s>>>(b.qkv, W->v_a, b.att, l0, n, B, D, H);
+  return FLB_OK;
+}
+
+}  // namespace
+
 int block_grid_fwd(const flb_block_weights* W, const void* x, void* grids, int64_t L, int64_t S,
                    int64_t B, int64_t D, int64_t H, float eps, void* ws, size_t ws_bytes,
                    cudaStream_t s) {
@@ -292,57 +347,515 @@ int block_grid_fwd(const flb_block_weights* W, const void* x, void* grids, int64
   const long long DD = D * D, BD = B * D;
   const int Li = (int)L, Si = (int)S, Bi = (int)B, Di = (int)D, Hi = (int)H;
   const int ticks = (int)(L + 2 * S - 2);
+  const TickBufs tb{w.ln, w.lat, w.tok, w.z, w.z, w.qkv, w.att};
   int launches = 0;
   for (int T = 0; T < ticks; ++T) {
     const Tick tk = tick_of(T, Li, Si);
     const int n = tk.n, l0 = tk.l0;
     if (n == 0) continue;
-    const int rows_ln = 2 * n * Bi;
-    blk_ln_kernel<<<(rows_ln + 7) / 8, 256, 0, s>>>(g + port_stride, g + 2 * port_stride,
-                                                    W->ln_lat_w, W->ln_lat_b, W->ln_fdbk_w,
-                                                    W->ln_fdbk_b, w.ln, T, l0, n, Li, Si, Bi, Di,
-                                                    eps);
-    // priors: lat_prior -> w.lat [n, B, D]; fdbk_prior -> token slot 2 (row pitch 3D)
-    const bf16* Wpl = reinterpret_cast<const bf16*>(W->w_prior_lat) + (int64_t)l0 * DD;
-    const bf16* Wpf = reinterpret_cast<const bf16*>(W->w_prior_fdbk) + (int64_t)l0 * DD;
-    const bf16* Wgl = reinterpret_cast<const bf16*>(W->w_gate_l) + (int64_t)l0 * DD;
-    const bf16* Wgx = reinterpret_cast<const bf16*>(W->w_gate_x) + (int64_t)l0 * DD;
-    const bf16* Wqkv = reinterpret_cast<const bf16*>(W->w_qkv) + (int64_t)l0 * 3 * DD;
+    if ((st = tick_forward(hb, W, xb, g, port_stride, tb, T, l0, n, Li, Si, Bi, Di, Hi, eps, s)) !=
+        FLB_OK)
+      return st;
     const bf16* Wo = reinterpret_cast<const bf16*>(W->w_o) + (int64_t)l0 * DD;
-    if ((st = gemm_rm(hb, false, true, Bi, Di, Di, w.ln, Di, BD, Wpl, Di, 2 * DD, w.lat, Di, BD, n,
-                      0.f, CUDA_R_16BF)) != FLB_OK)
-      return st;
-    if ((st = gemm_rm(hb, false, true, Bi, Di, Di, w.ln + n * BD, Di, BD, Wpf, Di, 2 * DD,
-                      w.tok + 2 * D, 3 * Di, 3 * BD, n, 0.f, CUDA_R_16BF)) != FLB_OK)
-      return st;
-    // lateral gate
-    if ((st = gemm_rm(hb, false, true, Bi, Di, Di, w.tok + 2 * D, 3 * Di, 3 * BD, Wgl, Di, 2 * DD,
-                      w.z, Di, BD, n, 0.f, CUDA_R_16BF)) != FLB_OK)
-      return st;
-    const dim3 ew_grid((unsigned)((D / 2 + 127) / 128), (unsigned)(n * Bi));
-    blk_gate_kernel<<<ew_grid, 128, 0, s>>>(w.z, W->b_gate_l, w.lat, g, xb, 0, w.tok + D, T, l0,
-                                            Si, Bi, Di);
-    // sensory gate
-    if ((st = gemm_rm(hb, false, true, Bi, Di, Di, w.tok + D, 3 * Di, 3 * BD, Wgx, Di, 2 * DD, w.z,
-                      Di, BD, n, 0.f, CUDA_R_16BF)) != FLB_OK)
-      return st;
-    blk_gate_kernel<<<ew_grid, 128, 0, s>>>(w.z, W->b_gate_x, nullptr, g, xb, 1, w.tok, T, l0, Si,
-                                            Bi, Di);
-    // q | k | v of the 3 tokens: [n, 3B, D] x [3D, D]^T
-    if ((st = gemm_rm(hb, false, true, 3 * Bi, 3 * Di, Di, w.tok, Di, 3 * BD, Wqkv, Di, 6 * DD,
-                      w.qkv, 3 * Di, 9 * BD, n, 0.f, CUDA_R_16BF)) != FLB_OK)
-      return st;
-    const int tasks = n * Bi * Hi;
-    blk_attn3_kernel<<<(tasks + 7) / 8, 256, 0, s>>>(w.qkv, W->v_a, w.att, l0, n, Bi, Di, Hi);
     if ((st = gemm_rm(hb, false, true, 3 * Bi, Di, Di, w.att, Di, 3 * BD, Wo, Di, 2 * DD, w.o, Di,
                       3 * BD, n, 0.f, CUDA_R_16BF)) != FLB_OK)
       return st;
+    const dim3 ew_grid((unsigned)((D / 2 + 127) / 128), (unsigned)(n * Bi));
     blk_out_kernel<<<ew_grid, 128, 0, s>>>(w.o, w.lat, w.tok, xb, g, port_stride, T, l0, Si, Bi,
                                            Di);
     launches += 6;  // own kernels (the GEMMs are cuBLAS's)
   }
   count_launches(launches);
   return check_cuda(cudaGetLastError(), "flb block grid launch");
+}
+
+// =============================================================================================
+// Backward of the FLB block grid (training). Ticks in reverse; per tick the forward stages are
+// recomputed from the saved port grids, then (for all of the tick's cells at once):
+//   residual/aux -> d_o, d_top, d_lat_prior, d_fdbk_prior          [own kernel]
+//   d_att = d_o W_o, dW_o += d_o^T att                              [GEMMs]
+//   3-token attention backward -> d_q | d_k | d_v, dv_a             [own kernel]
+//   dT = d_qkv W_qkv, dW_qkv += d_qkv^T T                           [GEMMs]
+//   sensory gate backward (routes d_top), lateral gate backward      [own kernels + GEMMs]
+//   prior GEMMs, then the LayerNorm backward (routes d_left, d_diag) [GEMMs + own kernel]
+// Each port output has exactly one consumer (top -> the cell above, left -> the next column,
+// bottom-left -> the cell below in the next column) and consumers run at later ticks, so the
+// routed gradients are plain additions into fp32 gradient grids, complete when the producing
+// cell's tick comes. Weight gradients accumulate into per-layer fp32 stacks (the cells of a
+// tick are distinct layers). Math: the chain rule of models/FLB_Model.py:32-96 and of the
+// attention (kernels/additive_attention.py:91-130) on 3 tokens.
+// =============================================================================================
+
+namespace {
+
+__device__ __forceinline__ float sigm(float z) { return 1.f / (1.f + __expf(-z)); }
+
+// external bf16 port grads (or zero) -> fp32 gradient grids of ports 0-2, [L*S][B][D] each
+__global__ void blk_dg_init_kernel(const bf16* __restrict__ g0, const bf16* __restrict__ g1,
+                                   const bf16* __restrict__ g2, float* __restrict__ dG,
+                                   int64_t per_port) {
+  for (int64_t e = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; e < 3 * per_port;
+       e += (int64_t)gridDim.x * blockDim.x) {
+    const int p = (int)(e / per_port);
+    const int64_t r = e - p * per_port;
+    const bf16* src = p == 0 ? g0 : (p == 1 ? g1 : g2);
+    dG[e] = src ? __bfloat162float(src[r]) : 0.f;
+  }
+}
+
+// residuals and aux: grid (pairs, n*B rows)
+__global__ void blk_bwd_out_kernel(const float* __restrict__ dG, int64_t per_port,
+                                   const bf16* __restrict__ ext3, const bf16* __restrict__ grids,
+                                   int64_t port_stride, const bf16* __restrict__ lat,
+                                   const bf16* __restrict__ tok, bf16* __restrict__ d_o,
+                                   float* __restrict__ d_top, float* __restrict__ d_lp,
+                                   float* __restrict__ d_fp, int T, int l0, int S, int B, int D) {
+  const int j = blockIdx.x * blockDim.x + threadIdx.x;
+  if (j >= D / 2) return;
+  const int rb = blockIdx.y;
+  const int i = rb / B, b = rb - i * B;
+  const int l = l0 + 2 * i, t = (T - l) / 2;
+  const int64_t off = (cell_row(l, t, S) * B + b) * D;
+  const float2 dhx = reinterpret_cast<const float2*>(dG + off)[j];
+  const float2 dhl = reinterpret_cast<const float2*>(dG + per_port + off)[j];
+  const float2 dhf = reinterpret_cast<const float2*>(dG + 2 * per_port + off)[j];
+  float2 da = make_float2(0.f, 0.f);
+  if (ext3) da = __bfloat1622float2(reinterpret_cast<const __nv_bfloat162*>(ext3 + off)[j]);
+  auto ld2 = [&](const bf16* p) {
+    return __bfloat1622float2(reinterpret_cast<const __nv_bfloat162*>(p)[j]);
+  };
+  const float2 hl = ld2(grids + port_stride + off), hf = ld2(grids + 2 * port_stride + off);
+  const int64_t r3 = (int64_t)rb * 3;
+  const float2 lp = ld2(lat + (int64_t)rb * D), fp = ld2(tok + (r3 + 2) * D);
+  reinterpret_cast<__nv_bfloat162*>(d_o + r3 * D)[j] = __floats2bfloat162_rn(dhx.x, dhx.y);
+  reinterpret_cast<__nv_bfloat162*>(d_o + (r3 + 1) * D)[j] = __floats2bfloat162_rn(dhl.x, dhl.y);
+  reinterpret_cast<__nv_bfloat162*>(d_o + (r3 + 2) * D)[j] = __floats2bfloat162_rn(dhf.x, dhf.y);
+  reinterpret_cast<float2*>(d_top + (int64_t)rb * D)[j] = dhx;
+  reinterpret_cast<float2*>(d_lp + (int64_t)rb * D)[j] =
+      make_float2(dhl.x + 2.f * (lp.x - hl.x) * da.x, dhl.y + 2.f * (lp.y - hl.y) * da.y);
+  reinterpret_cast<float2*>(d_fp + (int64_t)rb * D)[j] =
+      make_float2(dhf.x + 2.f * (fp.x - hf.x) * da.x, dhf.y + 2.f * (fp.y - hf.y) * da.y);
+}
+
+// 3-token attention backward, one warp per (cell, batch row, head)
+__global__ void blk_attn3_bwd_kernel(const bf16* __restrict__ qkv, const float* __restrict__ v_a,
+                                     const bf16* __restrict__ d_att, bf16* __restrict__ d_qkv,
+                                     float* __restrict__ d_va, int l0, int n, int B, int D, int H) {
+  const int warps = blockDim.x >> 5, lane = threadIdx.x & 31;
+  const int task = blockIdx.x * warps + (threadIdx.x >> 5);
+  if (task >= n * B * H) return;
+  const int h = task % H;
+  const int64_t rb = task / H;
+  const int i = (int)(rb / B);
+  const int dh = D / H;
+  const int64_t wrow = ((int64_t)(l0 + 2 * i) * H + h) * dh;
+  const float* w = v_a + wrow;
+  const bf16* base = qkv + rb * 3 * (3 * D) + h * dh;
+  const bf16* dob = d_att + rb * 3 * D + h * dh;
+  float q[4][3], k[4][3], v[4][3], dout[4][3], wd[4];
+  float s[3][3], dp[3][3];
+#pragma unroll
+  for (int a = 0; a < 3; ++a)
+#pragma unroll
+    for (int c = 0; c < 3; ++c) s[a][c] = dp[a][c] = 0.f;
+#pragma unroll
+  for (int kk = 0; kk < 4; ++kk) {
+    const int d = lane + 32 * kk;
+    const bool ok = d < dh;
+#pragma unroll
+    for (int r = 0; r < 3; ++r) {
+      q[kk][r] = ok ? __bfloat162float(base[r * 3 * D + d]) : 0.f;
+      k[kk][r] = ok ? __bfloat162float(base[r * 3 * D + D + d]) : 0.f;
+      v[kk][r] = ok ? __bfloat162float(base[r * 3 * D + 2 * D + d]) : 0.f;
+      dout[kk][r] = ok ? __bfloat162float(dob[r * D + d]) : 0.f;
+    }
+    wd[kk] = ok ? w[d] : 0.f;
+#pragma unroll
+    for (int a = 0; a < 3; ++a)
+#pragma unroll
+      for (int c = 0; c < 3; ++c) {
+        s[a][c] = fmaf(wd[kk], ok ? tanh_approx(q[kk][a] + k[kk][c]) : 0.f, s[a][c]);
+        dp[a][c] = fmaf(dout[kk][a], v[kk][c], dp[a][c]);
+      }
+  }
+  const float scale = rsqrtf((float)dh);
+  float p[3][3], ds[3][3];
+#pragma unroll
+  for (int a = 0; a < 3; ++a) {
+    float m = -INFINITY;
+#pragma unroll
+    for (int c = 0; c < 3; ++c) {
+      s[a][c] = warp_sum(s[a][c]) * scale;
+      dp[a][c] = warp_sum(dp[a][c]);
+      m = fmaxf(m, s[a][c]);
+    }
+    float l = 0.f;
+#pragma unroll
+    for (int c = 0; c < 3; ++c) {
+      p[a][c] = __expf(s[a][c] - m);
+      l += p[a][c];
+    }
+    float dot = 0.f;
+#pragma unroll
+    for (int c = 0; c < 3; ++c) {
+      p[a][c] /= l;
+      dot += p[a][c] * dp[a][c];
+    }
+#pragma unroll
+    for (int c = 0; c < 3; ++c) ds[a][c] = p[a][c] * (dp[a][c] - dot) * scale;
+  }
+  bf16* dbase = d_qkv + rb * 3 * (3 * D) + h * dh;
+#pragma unroll
+  for (int kk = 0; kk < 4; ++kk) {
+    const int d = lane + 32 * kk;
+    if (d >= dh) break;
+    float dq[3] = {0.f, 0.f, 0.f}, dk[3] = {0.f, 0.f, 0.f}, dw = 0.f;
+#pragma unroll
+    for (int a = 0; a < 3; ++a)
+#pragma unroll
+      for (int c = 0; c < 3; ++c) {
+        const float tt = tanh_approx(q[kk][a] + k[kk][c]);
+        const float g = ds[a][c] * wd[kk] * (1.f - tt * tt);
+        dq[a] += g;
+        dk[c] += g;
+        dw = fmaf(ds[a][c], tt, dw);
+      }
+#pragma unroll
+    for (int r = 0; r < 3; ++r) {
+      const float dv = p[0][r] * dout[kk][0] + p[1][r] * dout[kk][1] + p[2][r] * dout[kk][2];
+      dbase[r * 3 * D + d] = __float2bfloat16_rn(dq[r]);
+      dbase[r * 3 * D + D + d] = __float2bfloat16_rn(dk[r]);
+      dbase[r * 3 * D + 2 * D + d] = __float2bfloat16_rn(dv);
+    }
+    atomicAdd(d_va + wrow + d, dw);
+  }
+}
+
+// sensory gate backward: grid (pairs, cells), loop over the batch rows. Finishes d_top and routes
+// it (to the port-0 gradient of the cell above, or to dx for layer 0).
+__global__ void blk_gx_bwd_kernel(const float* __restrict__ dT, const bf16* __restrict__ zx,
+                                  const float* __restrict__ b_gx, const bf16* __restrict__ grids,
+                                  const bf16* __restrict__ x, const float* __restrict__ d_top,
+                                  float* __restrict__ dG0, float* __restrict__ dx,
+                                  bf16* __restrict__ d_zx, float* __restrict__ d_lr,
+                                  float* __restrict__ d_fp, float* __restrict__ db_gx, int T,
+                                  int l0, int S, int B, int D) {
+  const int j = blockIdx.x * blockDim.x + threadIdx.x;
+  if (j >= D / 2) return;
+  const int i = blockIdx.y;
+  const int l = l0 + 2 * i, t = (T - l) / 2;
+  const float2 bias = reinterpret_cast<const float2*>(b_gx + (int64_t)l * D)[j];
+  float2 acc = make_float2(0.f, 0.f);
+  for (int b = 0; b < B; ++b) {
+    const int64_t rb = (int64_t)i * B + b;
+    const float2 dxr = reinterpret_cast<const float2*>(dT + (rb * 3) * D)[j];
+    const float2 z = __bfloat1622float2(reinterpret_cast<const __nv_bfloat162*>(zx + rb * D)[j]);
+    const float2 top = __bfloat1622float2(
+        reinterpret_cast<const __nv_bfloat162*>(top_row(grids, x, l, t, b, S, B, D))[j]);
+    const float s0 = sigm(z.x + bias.x), s1 = sigm(z.y + bias.y);
+    const float2 dt0 = reinterpret_cast<const float2*>(d_top + rb * D)[j];
+    const float2 dtop = make_float2(dt0.x + dxr.x * s0, dt0.y + dxr.y * s1);
+    if (l > 0) {
+      float2* dst = reinterpret_cast<float2*>(dG0 + (cell_row(l - 1, t, S) * B + b) * D) + j;
+      const float2 o = *dst;
+      *dst = make_float2(o.x + dtop.x, o.y + dtop.y);
+    } else {
+      reinterpret_cast<float2*>(dx + ((int64_t)b * S + t) * D)[j] = dtop;
+    }
+    const float dz0 = dxr.x * top.x * s0 * (1.f - s0), dz1 = dxr.y * top.y * s1 * (1.f - s1);
+    reinterpret_cast<__nv_bfloat162*>(d_zx + rb * D)[j] = __floats2bfloat162_rn(dz0, dz1);
+    acc.x += dz0;
+    acc.y += dz1;
+    reinterpret_cast<float2*>(d_lr + rb * D)[j] =
+        reinterpret_cast<const float2*>(dT + (rb * 3 + 1) * D)[j];
+    const float2 dtf = reinterpret_cast<const float2*>(dT + (rb * 3 + 2) * D)[j];
+    float2* fp = reinterpret_cast<float2*>(d_fp + rb * D) + j;
+    const float2 o = *fp;
+    *fp = make_float2(o.x + dtf.x, o.y + dtf.y);
+  }
+  float2* db = reinterpret_cast<float2*>(db_gx + (int64_t)l * D) + j;
+  const float2 o = *db;
+  *db = make_float2(o.x + acc.x, o.y + acc.y);
+}
+
+// lateral gate backward: grid (pairs, cells), loop over the batch rows; finishes d_lat_prior
+__global__ void blk_gl_bwd_kernel(const float* __restrict__ d_lr, const bf16* __restrict__ zl,
+                                  const float* __restrict__ b_gl, const bf16* __restrict__ lat,
+                                  float* __restrict__ d_lp, bf16* __restrict__ d_lp_h,
+                                  bf16* __restrict__ d_zl, float* __restrict__ db_gl, int l0,
+                                  int B, int D) {
+  const int j = blockIdx.x * blockDim.x + threadIdx.x;
+  if (j >= D / 2) return;
+  const int i = blockIdx.y;
+  const int l = l0 + 2 * i;
+  const float2 bias = reinterpret_cast<const float2*>(b_gl + (int64_t)l * D)[j];
+  float2 acc = make_float2(0.f, 0.f);
+  for (int b = 0; b < B; ++b) {
+    const int64_t rb = (int64_t)i * B + b;
+    const float2 dl = reinterpret_cast<const float2*>(d_lr + rb * D)[j];
+    const float2 z = __bfloat1622float2(reinterpret_cast<const __nv_bfloat162*>(zl + rb * D)[j]);
+    const float2 lp = __bfloat1622float2(reinterpret_cast<const __nv_bfloat162*>(lat + rb * D)[j]);
+    const float s0 = sigm(z.x + bias.x), s1 = sigm(z.y + bias.y);
+    const float2 o = reinterpret_cast<const float2*>(d_lp + rb * D)[j];
+    const float2 dlp = make_float2(o.x + dl.x * s0, o.y + dl.y * s1);
+    reinterpret_cast<__nv_bfloat162*>(d_lp_h + rb * D)[j] = __floats2bfloat162_rn(dlp.x, dlp.y);
+    const float dz0 = dl.x * lp.x * s0 * (1.f - s0), dz1 = dl.y * lp.y * s1 * (1.f - s1);
+    reinterpret_cast<__nv_bfloat162*>(d_zl + rb * D)[j] = __floats2bfloat162_rn(dz0, dz1);
+    acc.x += dz0;
+    acc.y += dz1;
+  }
+  float2* db = reinterpret_cast<float2*>(db_gl + (int64_t)l * D) + j;
+  const float2 o = *db;
+  *db = make_float2(o.x + acc.x, o.y + acc.y);
+}
+
+__global__ void blk_cast_kernel(const float* __restrict__ src, bf16* __restrict__ dst,
+                                int64_t pairs) {
+  for (int64_t e = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; e < pairs;
+       e += (int64_t)gridDim.x * blockDim.x) {
+    const float2 v = reinterpret_cast<const float2*>(src)[e];
+    reinterpret_cast<__nv_bfloat162*>(dst)[e] = __floats2bfloat162_rn(v.x, v.y);
+  }
+}
+
+// LayerNorm backward: one block per (which, cell), its warps over the batch rows. Routes the
+// input gradient to the producer's port gradient (left -> port 1 of (l, t-1), bottom-left ->
+// port 2 of (l+1, t-1)) and accumulates dgamma / dbeta of the cell's layer.
+__global__ void blk_ln_bwd_kernel(const bf16* __restrict__ grids, int64_t port_stride,
+                                  const float* __restrict__ dA, const float* __restrict__ lw0,
+                                  const float* __restrict__ lw1, float* __restrict__ dG,
+                                  int64_t per_port, float* __restrict__ dw0,
+                                  float* __restrict__ db0, float* __restrict__ dw1,
+                                  float* __restrict__ db1, int T, int l0, int n, int L, int S,
+                                  int B, int D, float eps) {
+  extern __shared__ float red[];  // [2][D]: dgamma, dbeta partials of this block
+  const int which = blockIdx.x / n, i = blockIdx.x % n;
+  const int l = l0 + 2 * i, t = (T - l) / 2;
+  const int warps = blockDim.x >> 5, warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  for (int e = threadIdx.x; e < 2 * D; e += blockDim.x) red[e] = 0.f;
+  __syncthreads();
+  const float* gamma = (which ? lw1 : lw0) + (int64_t)l * D;
+  const bool has_src = t > 0 && (which == 0 || l + 1 < L);
+  const int64_t src_cell = which == 0 ? cell_row(l, t - 1, S) : cell_row(l + 1, t - 1, S);
+  const bf16* src_port = grids + (which ? 2 : 1) * port_stride;
+  float* dst_port = dG + (which ? 2 : 1) * per_port;
+  const int nch = D / 8;
+  for (int b = warp; b < B; b += warps) {
+    const float* da = dA + ((int64_t)(which * n + i) * B + b) * D;
+    float xv[kMaxChunks][8];
+    float s = 0.f, ss = 0.f;
+#pragma unroll
+    for (int k = 0; k < kMaxChunks; ++k) {
+      const int c = lane + 32 * k;
+      uint4 raw = make_uint4(0, 0, 0, 0);
+      if (has_src && c < nch) raw = reinterpret_cast<const uint4*>(src_port + (src_cell * B + b) * D)[c];
+      const uint32_t* r = reinterpret_cast<const uint32_t*>(&raw);
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        const float2 f = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&r[e]));
+        xv[k][2 * e] = f.x;
+        xv[k][2 * e + 1] = f.y;
+        s += f.x + f.y;
+        ss += f.x * f.x + f.y * f.y;
+      }
+    }
+    s = warp_sum(s);
+    ss = warp_sum(ss);
+    const float mean = s / D;
+    const float rstd = rsqrtf(fmaxf(ss / D - mean * mean, 0.f) + eps);
+    float c1 = 0.f, c2 = 0.f;
+#pragma unroll
+    for (int k = 0; k < kMaxChunks; ++k) {
+      const int c = lane + 32 * k;
+      if (c >= nch) break;
+#pragma unroll
+      for (int e = 0; e < 8; ++e) {
+        const int d = 8 * c + e;
+        const float xh = (xv[k][e] - mean) * rstd;
+        const float g = da[d];
+        const float dxh = g * gamma[d];
+        c1 += dxh;
+        c2 += dxh * xh;
+        atomicAdd(&red[d], g * xh);
+        atomicAdd(&red[D + d], g);
+        xv[k][e] = xh;
+      }
+    }
+    c1 = warp_sum(c1) / D;
+    c2 = warp_sum(c2) / D;
+    if (has_src) {
+      float* dst = dst_port + (src_cell * B + b) * D;
+#pragma unroll
+      for (int k = 0; k < kMaxChunks; ++k) {
+        const int c = lane + 32 * k;
+        if (c >= nch) break;
+#pragma unroll
+        for (int e = 0; e < 8; ++e) {
+          const int d = 8 * c + e;
+          dst[d] += rstd * (da[d] * gamma[d] - c1 - xv[k][e] * c2);
+        }
+      }
+    }
+  }
+  __syncthreads();
+  float* dw = (which ? dw1 : dw0) + (int64_t)l * D;
+  float* db = (which ? db1 : db0) + (int64_t)l * D;
+  for (int d = threadIdx.x; d < D; d += blockDim.x) {
+    dw[d] += red[d];
+    db[d] += red[D + d];
+  }
+}
+
+struct BlockBwdWs {
+  TickBufs f;
+  bf16 *d_o, *d_att, *d_qkv, *d_zx, *d_zl, *d_lp_h, *d_fp_h;
+  float *dT, *d_top, *d_lp, *d_fp, *d_lr, *dA, *dG, *dx;
+  void* blas;
+};
+
+size_t block_bwd_ws_layout(int64_t L, int64_t S, int64_t B, int64_t D, BlockBwdWs* w, void* base) {
+  const int64_t nmax = max_cells_per_tick(L, S);
+  auto al = [](size_t x) { return (x + 255) & ~(size_t)255; };
+  const size_t rowh = (size_t)nmax * B * D * sizeof(bf16), rowf = (size_t)nmax * B * D * 4;
+  size_t off = 0;
+  uint8_t* p = reinterpret_cast<uint8_t*>(base);
+  auto take = [&](size_t bytes) -> uint8_t* {
+    uint8_t* r = p ? p + off : nullptr;
+    off += al(bytes);
+    return r;
+  };
+  BlockBwdWs t;
+  t.f.ln = (bf16*)take(2 * rowh);
+  t.f.lat = (bf16*)take(rowh);
+  t.f.tok = (bf16*)take(3 * rowh);
+  t.f.zl = (bf16*)take(rowh);
+  t.f.zx = (bf16*)take(rowh);
+  t.f.qkv = (bf16*)take(9 * rowh);
+  t.f.att = (bf16*)take(3 * rowh);
+  t.d_o = (bf16*)take(3 * rowh);
+  t.d_att = (bf16*)take(3 * rowh);
+  t.d_qkv = (bf16*)take(9 * rowh);
+  t.d_zx = (bf16*)take(rowh);
+  t.d_zl = (bf16*)take(rowh);
+  t.d_lp_h = (bf16*)take(rowh);
+  t.d_fp_h = (bf16*)take(rowh);
+  t.dT = (float*)take(3 * rowf);
+  t.d_top = (float*)take(rowf);
+  t.d_lp = (float*)take(rowf);
+  t.d_fp = (float*)take(rowf);
+  t.d_lr = (float*)take(rowf);
+  t.dA = (float*)take(2 * rowf);
+  t.dG = (float*)take((size_t)3 * L * S * B * D * 4);
+  t.dx = nullptr;
+  t.blas = take(kBlkBlasWs);
+  if (w) *w = t;
+  return off;
+}
+
+}  // namespace
+
+size_t block_grid_bwd_workspace_bytes(int64_t L, int64_t S, int64_t B, int64_t D) {
+  return block_bwd_ws_layout(L, S, B, D, nullptr, nullptr);
+}
+
+int block_grid_bwd(const flb_block_weights* W, const void* x, const void* grids,
+                   const void* const* dgrids, float* dx, const flb_block_grads* G, int64_t L,
+                   int64_t S, int64_t B, int64_t D, int64_t H, float eps, void* ws,
+                   size_t ws_bytes, cudaStream_t s) {
+  BlockBwdWs w;
+  block_bwd_ws_layout(L, S, B, D, &w, ws);
+  cublasHandle_t hb;
+  int st = blas(s, w.blas, kBlkBlasWs, &hb);
+  if (st != FLB_OK) return st;
+  const bf16* xb = reinterpret_cast<const bf16*>(x);
+  const bf16* g = reinterpret_cast<const bf16*>(grids);
+  const int64_t port_stride = (L * S + L) * B * D;
+  const int64_t per_port = L * S * B * D;
+  const long long DD = D * D, BD = B * D;
+  const int Li = (int)L, Si = (int)S, Bi = (int)B, Di = (int)D, Hi = (int)H;
+  const int ticks = (int)(L + 2 * S - 2);
+  const int ew = 4 * num_sms();
+  blk_dg_init_kernel<<<ew, 256, 0, s>>>((const bf16*)dgrids[0], (const bf16*)dgrids[1],
+                                        (const bf16*)dgrids[2], w.dG, per_port);
+  cudaError_t ce = cudaMemsetAsync(dx, 0, (size_t)B * S * D * 4, s);
+  if (ce != cudaSuccess) return check_cuda(ce, "block_grid_bwd dx reset");
+  const bf16* ext3 = (const bf16*)dgrids[3];
+  int launches = 1;
+  for (int T = ticks - 1; T >= 0; --T) {
+    const Tick tk = tick_of(T, Li, Si);
+    const int n = tk.n, l0 = tk.l0;
+    if (n == 0) continue;
+    if ((st = tick_forward(hb, W, xb, g, port_stride, w.f, T, l0, n, Li, Si, Bi, Di, Hi, eps, s)) !=
+        FLB_OK)
+      return st;
+    const dim3 ew_grid((unsigned)((D / 2 + 127) / 128), (unsigned)(n * Bi));
+    const dim3 cell_grid((unsigned)((D / 2 + 127) / 128), (unsigned)n);
+    blk_bwd_out_kernel<<<ew_grid, 128, 0, s>>>(w.dG, per_port, ext3, g, port_stride, w.f.lat,
+                                               w.f.tok, w.d_o, w.d_top, w.d_lp, w.d_fp, T, l0, Si,
+                                               Bi, Di);
+    const bf16* Wo = reinterpret_cast<const bf16*>(W->w_o) + (int64_t)l0 * DD;
+    const bf16* Wqkv = reinterpret_cast<const bf16*>(W->w_qkv) + (int64_t)l0 * 3 * DD;
+    const bf16* Wgx = reinterpret_cast<const bf16*>(W->w_gate_x) + (int64_t)l0 * DD;
+    const bf16* Wgl = reinterpret_cast<const bf16*>(W->w_gate_l) + (int64_t)l0 * DD;
+    const bf16* Wpl = reinterpret_cast<const bf16*>(W->w_prior_lat) + (int64_t)l0 * DD;
+    const bf16* Wpf = reinterpret_cast<const bf16*>(W->w_prior_fdbk) + (int64_t)l0 * DD;
+    // output projection
+    if ((st = gemm_rm(hb, false, false, 3 * Bi, Di, Di, w.d_o, Di, 3 * BD, Wo, Di, 2 * DD, w.d_att,
+                      Di, 3 * BD, n, 0.f, CUDA_R_16BF)) != FLB_OK)
+      return st;
+    if ((st = gemm_rm(hb, true, false, Di, Di, 3 * Bi, w.d_o, Di, 3 * BD, w.f.att, Di, 3 * BD,
+                      G->w_o + (int64_t)l0 * DD, Di, 2 * DD, n, 1.f)) != FLB_OK)
+      return st;
+    blk_attn3_bwd_kernel<<<(n * Bi * Hi + 7) / 8, 256, 0, s>>>(w.f.qkv, W->v_a, w.d_att, w.d_qkv,
+                                                               G->v_a, l0, n, Bi, Di, Hi);
+    // q | k | v projections
+    if ((st = gemm_rm(hb, false, false, 3 * Bi, Di, 3 * Di, w.d_qkv, 3 * Di, 9 * BD, Wqkv, Di,
+                      6 * DD, w.dT, Di, 3 * BD, n, 0.f)) != FLB_OK)
+      return st;
+    if ((st = gemm_rm(hb, true, false, 3 * Di, Di, 3 * Bi, w.d_qkv, 3 * Di, 9 * BD, w.f.tok, Di,
+                      3 * BD, G->w_qkv + (int64_t)l0 * 3 * DD, Di, 6 * DD, n, 1.f)) != FLB_OK)
+      return st;
+    // sensory gate
+    blk_gx_bwd_kernel<<<cell_grid, 128, 0, s>>>(w.dT, w.f.zx, W->b_gate_x, g, xb, w.d_top, w.dG,
+                                                dx, w.d_zx, w.d_lr, w.d_fp, G->b_gate_x, T, l0, Si,
+                                                Bi, Di);
+    if ((st = gemm_rm(hb, false, false, Bi, Di, Di, w.d_zx, Di, BD, Wgx, Di, 2 * DD, w.d_lr, Di, BD,
+                      n, 1.f)) != FLB_OK)
+      return st;
+    if ((st = gemm_rm(hb, true, false, Di, Di, Bi, w.d_zx, Di, BD, w.f.tok + D, 3 * Di, 3 * BD,
+                      G->w_gate_x + (int64_t)l0 * DD, Di, 2 * DD, n, 1.f)) != FLB_OK)
+      return st;
+    // lateral gate
+    blk_gl_bwd_kernel<<<cell_grid, 128, 0, s>>>(w.d_lr, w.f.zl, W->b_gate_l, w.f.lat, w.d_lp,
+                                                w.d_lp_h, w.d_zl, G->b_gate_l, l0, Bi, Di);
+    if ((st = gemm_rm(hb, false, false, Bi, Di, Di, w.d_zl, Di, BD, Wgl, Di, 2 * DD, w.d_fp, Di, BD,
+                      n, 1.f)) != FLB_OK)
+      return st;
+    if ((st = gemm_rm(hb, true, false, Di, Di, Bi, w.d_zl, Di, BD, w.f.tok + 2 * D, 3 * Di, 3 * BD,
+                      G->w_gate_l + (int64_t)l0 * DD, Di, 2 * DD, n, 1.f)) != FLB_OK)
+      return st;
+    blk_cast_kernel<<<(unsigned)std::min<int64_t>((n * BD / 2 + 255) / 256, ew), 256, 0, s>>>(
+        w.d_fp, w.d_fp_h, n * BD / 2);
+    // priors
+    if ((st = gemm_rm(hb, false, false, Bi, Di, Di, w.d_lp_h, Di, BD, Wpl, Di, 2 * DD, w.dA, Di, BD,
+                      n, 0.f)) != FLB_OK)
+      return st;
+    if ((st = gemm_rm(hb, false, false, Bi, Di, Di, w.d_fp_h, Di, BD, Wpf, Di, 2 * DD,
+                      w.dA + n * BD, Di, BD, n, 0.f)) != FLB_OK)
+      return st;
+    if ((st = gemm_rm(hb, true, false, Di, Di, Bi, w.d_lp_h, Di, BD, w.f.ln, Di, BD,
+                      G->w_prior_lat + (int64_t)l0 * DD, Di, 2 * DD, n, 1.f)) != FLB_OK)
+      return st;
+    if ((st = gemm_rm(hb, true, false, Di, Di, Bi, w.d_fp_h, Di, BD, w.f.ln + n * BD, Di, BD,
+                      G->w_prior_fdbk + (int64_t)l0 * DD, Di, 2 * DD, n, 1.f)) != FLB_OK)
+      return st;
+    blk_ln_bwd_kernel<<<2 * n, 512, 2 * D * sizeof(float), s>>>(
+        g, port_stride, w.dA, W->ln_lat_w, W->ln_fdbk_w, w.dG, per_port, G->ln_lat_w,
+        G->ln_lat_b, G->ln_fdbk_w, G->ln_fdbk_b, T, l0, n, Li, Si, Bi, Di, eps);
+    launches += 10;  // own kernels (4 recompute + 6 backward)
+  }
+  count_launches(launches);
+  return check_cuda(cudaGetLastError(), "flb block grid backward launch");
 }
 
 }  // namespace flb

@@ -51,6 +51,9 @@ PROTOTYPES = {
     "flb_block_grid_workspace_bytes": (_sz, [_i64, _i64, _i64, _i64]),
     "flb_block_grid_fwd": (_i32, [_vp, _vp, _vp, _i64, _i64, _i64, _i64, _i64, ctypes.c_float,
                                   _vp, _sz, _vp]),
+    "flb_block_grid_bwd_workspace_bytes": (_sz, [_i64, _i64, _i64, _i64]),
+    "flb_block_grid_bwd": (_i32, [_vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _i64, _i64, _i64,
+                                  _i64, _i64, ctypes.c_float, _vp, _sz, _vp]),
     "flb_grid_workspace_bytes": (_sz, [_i64, _i64, _i64, _i64, _i64, _i32]),
     "flb_grid_fwd": (_i32, [_vp, _i32, _vp, _vp, _vp, _vp, _vp, _vp, _i64, _i64, _i64, _i64, _i64,
                             _vp, _sz, _i32, _vp]),
@@ -71,6 +74,11 @@ class BlockWeights(ctypes.Structure):
     _fields_ = [(n, ctypes.c_void_p) for n in (
         "ln_lat_w", "ln_lat_b", "ln_fdbk_w", "ln_fdbk_b", "w_prior_lat", "w_prior_fdbk",
         "w_gate_l", "b_gate_l", "w_gate_x", "b_gate_x", "w_qkv", "w_o", "v_a")]
+
+
+class BlockGrads(ctypes.Structure):
+    """flb_block_grads of include/flb_b200.h (float32 device pointers, same field order)."""
+    _fields_ = [(n, ctypes.c_void_p) for n, _ in BlockWeights._fields_]
 
 
 for _name, (_res, _args) in PROTOTYPES.items():

@@ -1,17 +1,20 @@
-"""Native forward of FLB block cells on the wavefront grid (inference).
+"""Native forward and backward of FLB block cells on the wavefront grid.
 
 When an engine's layers are FLB blocks (the reference's FLB_Block / FLB_Attention_Layer, or
 flb_model's FLBBlock / FLBAttentionLayer: same math and parameter names) on the FLB grid
-configuration (dependencies top -> port 0, left -> port 1, bottom-left -> port 2, four ports)
-and no gradient is needed, the engine evaluates the whole grid with flb_block_grid_fwd: per
-tick a handful of launches over all of the tick's cells (strided GEMMs on the stacked weights
-read in place, LayerNorm, gate, three-token attention and residual kernels) instead of the
-per-tick gather, weight index_select, vmapped cell and scatters. bf16 compute only (the
-reference model runs under bf16 autocast). Training (a backward) keeps the generic path.
+configuration (dependencies top -> port 0, left -> port 1, bottom-left -> port 2, four ports),
+the engine evaluates the whole grid with flb_block_grid_fwd: per tick a handful of launches
+over all of the tick's cells (strided GEMMs on the stacked weights read in place, LayerNorm,
+gate, three-token attention and residual kernels) instead of the per-tick gather, weight
+index_select, vmapped cell and scatters. With gradients required it runs behind
+FLBGridFunction, whose backward is flb_block_grid_bwd (ticks in reverse, per-tick recompute,
+per-layer fp32 weight-gradient stacks). bf16 compute only (the reference model runs under bf16
+autocast).
 """
 from __future__ import annotations
 
 import ctypes
+import math
 
 import torch
 
@@ -108,3 +111,76 @@ def native_flb_forward(engine, static_x: torch.Tensor, grids: torch.Tensor, weig
     nat.check(nat.lib.flb_block_grid_fwd(
         ctypes.cast(ctypes.pointer(w.struct), ctypes.c_void_p), static_x.data_ptr(), grids.data_ptr(), L, S, B, D, w.heads,
         w.eps, nat.ptr(ws), ws_bytes, nat.stream_of(grids)), "flb_block_grid_fwd")
+
+
+# parameter name inside a block -> (gradient stack, slice of its per-layer entry)
+def _grad_slot(name: str, D: int):
+    table = {
+        "norm_lat.weight": ("ln_lat_w", None), "norm_lat.bias": ("ln_lat_b", None),
+        "norm_fdbk.weight": ("ln_fdbk_w", None), "norm_fdbk.bias": ("ln_fdbk_b", None),
+        "proj_lateral.weight": ("w_prior_lat", None),
+        "proj_feedback.weight": ("w_prior_fdbk", None),
+        "flb_attention.linear_gate_L.weight": ("w_gate_l", None),
+        "flb_attention.linear_gate_L.bias": ("b_gate_l", None),
+        "flb_attention.linear_gate_X.weight": ("w_gate_x", None),
+        "flb_attention.linear_gate_X.bias": ("b_gate_x", None),
+        "flb_attention.W_q.weight": ("w_qkv", slice(0, D)),
+        "flb_attention.W_k.weight": ("w_qkv", slice(D, 2 * D)),
+        "flb_attention.W_v.weight": ("w_qkv", slice(2 * D, 3 * D)),
+        "flb_attention.W_o.weight": ("w_o", None),
+        "flb_attention.v_a": ("v_a", None),
+    }
+    return table[name]
+
+
+class FLBGridFunction(torch.autograd.Function):
+    """The FLB grid, forward and backward in the native kernels. apply(engine, x, *params) with
+    params = every block's parameters in (layer, named_parameters) order; returns the four port
+    grids (views of the engine's static grids, as the per-tick engine returns)."""
+
+    @staticmethod
+    def forward(ctx, engine, x, *params):
+        engine._init_buffers(x)
+        ws = engine.graph_workspace
+        ws["static_x"].copy_(x)
+        w = BlockWeightStacks(list(engine.layers))
+        native_flb_forward(engine, ws["static_x"], ws["static_stacked_grids"], weights=w)
+        ctx.engine, ctx.weights = engine, w
+        ctx.x_meta = (x.shape, x.dtype)
+        n = math.prod(engine.config.grid_shape)
+        return tuple(ws["static_stacked_grids"][p][:n] for p in range(engine.config.num_ports))
+
+    @staticmethod
+    def backward(ctx, *grad_grids):
+        engine, w = ctx.engine, ctx.weights
+        cfg = engine.config
+        L, S = cfg.grid_shape
+        B, D = cfg.batch_size, cfg.dim
+        ws = engine.graph_workspace
+        dev = ws["static_x"].device
+        gstacks = {k: torch.zeros(v.shape, dtype=torch.float32, device=dev) for k, v in w.t.items()}
+        gstruct = nat.BlockGrads(**{k: v.data_ptr() for k, v in gstacks.items()})
+        dg = [g.to(torch.bfloat16).contiguous() if g is not None else None for g in grad_grids]
+        dx = torch.empty((B, S, D), dtype=torch.float32, device=dev)
+        ws_bytes = nat.lib.flb_block_grid_bwd_workspace_bytes(L, S, B, D)
+        wsb = nat.workspace(ws_bytes, dev)
+        nat.check(nat.lib.flb_block_grid_bwd(
+            ctypes.cast(ctypes.pointer(w.struct), ctypes.c_void_p), ws["static_x"].data_ptr(),
+            ws["static_stacked_grids"].data_ptr(), *[nat.ptr(g) for g in dg], dx.data_ptr(),
+            ctypes.cast(ctypes.pointer(gstruct), ctypes.c_void_p), L, S, B, D, w.heads, w.eps,
+            nat.ptr(wsb), ws_bytes, nat.stream_of(dx)), "flb_block_grid_bwd")
+        grads = []
+        for li, layer in enumerate(engine.layers):
+            for name, p in layer.named_parameters():
+                key, sl = _grad_slot(name, D)
+                gl = gstacks[key][li]
+                if sl is not None:
+                    gl = gl[sl]
+                grads.append(gl.reshape(p.shape).to(p.dtype))
+        shape, dtype = ctx.x_meta
+        return (None, dx.to(dtype).reshape(shape), *grads)
+
+
+def native_flb_train_forward(engine, x):
+    params = [p for layer in engine.layers for _, p in layer.named_parameters()]
+    return FLBGridFunction.apply(engine, x, *params)

@@ -172,8 +172,12 @@ class WavefrontEngine(nn.Module):
         fast = engine_fast_path(self, x, initial_states)
         if fast is not None:
             return fast
-        from .flb_cells import native_flb_applies, no_grad_needed, native_flb_forward
-        if no_grad_needed(self, x) and native_flb_applies(self, x):
+        from .flb_cells import (native_flb_applies, no_grad_needed, native_flb_forward,
+                                native_flb_train_forward)
+        if native_flb_applies(self, x) and not no_grad_needed(self, x):
+            # FLB block cells, training: flb_block_grid_fwd / flb_block_grid_bwd
+            return native_flb_train_forward(self, x)
+        if native_flb_applies(self, x):
             # FLB block cells, inference: the whole grid in flb_block_grid_fwd (no tick loop
             # through Python; initial states reach no cell, as in the per-tick path)
             self._init_buffers(x)

@@ -224,6 +224,39 @@ int flb_block_grid_fwd(const flb_block_weights* weights, const void* x, void* gr
                        int64_t L, int64_t S, int64_t batch, int64_t D, int64_t heads,
                        float ln_eps, void* workspace, size_t workspace_bytes, void* stream);
 
+/* Gradient accumulators of flb_block_grid_bwd: float32 stacks shaped like the matching fields
+ * of flb_block_weights (w_qkv: [L, 3D, D], v_a: [L, H, D/H]). Gradients are ADDED into them. */
+typedef struct flb_block_grads {
+  float* ln_lat_w;
+  float* ln_lat_b;
+  float* ln_fdbk_w;
+  float* ln_fdbk_b;
+  float* w_prior_lat;
+  float* w_prior_fdbk;
+  float* w_gate_l;
+  float* b_gate_l;
+  float* w_gate_x;
+  float* b_gate_x;
+  float* w_qkv;
+  float* w_o;
+  float* v_a;
+} flb_block_grads;
+
+size_t flb_block_grid_bwd_workspace_bytes(int64_t L, int64_t S, int64_t batch, int64_t D);
+
+/* Backward of flb_block_grid_fwd (training). Replaces the engine's per-tick backward for FLB
+ * blocks (execute_backward with the vmapped vjp of the cell, csrc/wavefront_backend.cpp:48-132,
+ * wavefront/wavefront_engine.py:200-236). Arguments as for flb_block_grid_fwd, with `grids`
+ * the port grids that forward wrote; dgrid0..dgrid3: bf16 [L*S, batch, D] upstream gradients
+ * of the four port grids (NULL = zero). dx: float32 [batch, S, D] gradient of x (overwritten).
+ * grads: weight-gradient accumulators (added into). Every tick recomputes its forward stages
+ * from the saved grids; nothing but the grids is kept from the forward. */
+int flb_block_grid_bwd(const flb_block_weights* weights, const void* x, const void* grids,
+                       const void* dgrid0, const void* dgrid1, const void* dgrid2,
+                       const void* dgrid3, float* dx, const flb_block_grads* grads,
+                       int64_t L, int64_t S, int64_t batch, int64_t D, int64_t heads,
+                       float ln_eps, void* workspace, size_t workspace_bytes, void* stream);
+
 /* Failure-detection check of the grid kernels' bounded dependency waits (no reference
  * counterpart). Runs flb_grid_fwd with the flag of cell (drop_row, drop_col) never released and
  * the flag-wait bound lowered to spin_limit polls: the cells waiting on it give up, record the

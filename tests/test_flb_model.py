@@ -166,3 +166,48 @@ def test_native_flb_decode_graphed_equals_eager(cuda):
         a = greedy_decode(m, prompt, 6, graphed=False)
         b = greedy_decode(m, prompt, 6, graphed=True)
     assert torch.equal(a, b)
+
+
+def _train_grads(m, tok, targets, native):
+    m.engine.native_cells = native
+    m.zero_grad(set_to_none=True)
+    with torch.autocast("cuda", dtype=torch.bfloat16):
+        logits, aux, _ = m(tok)
+    loss = F.cross_entropy(logits.float().reshape(-1, logits.shape[-1]), targets.reshape(-1)) + aux
+    loss.backward()
+    return {k: p.grad.detach().float().clone() for k, p in m.named_parameters()
+            if p.grad is not None}, loss.item()
+
+
+@pytest.mark.gpu
+def test_native_flb_training_matches_generic_path(cuda):
+    """Training under bf16 autocast: the native backward (flb_block_grid_bwd) against the
+    per-tick vjp path of the same engine — loss and every parameter gradient, the embedding's
+    included (it carries dx)."""
+    m = _bf16_model(13)
+    tok = torch.randint(0, 50, (3, 6), device=cuda)
+    targets = torch.randint(0, 50, (3, 6), device=cuda)
+    gn, ln_ = _train_grads(m, tok, targets, True)
+    gg, lg = _train_grads(m, tok, targets, False)
+    assert abs(ln_ - lg) <= 2e-2 * abs(lg)
+    assert set(gn) == set(gg)
+    for k in gg:
+        assert _max_rel(gn[k], gg[k]) < 6e-2, (k, _max_rel(gn[k], gg[k]))
+
+
+@pytest.mark.gpu
+def test_native_flb_training_against_reference(cuda, flb_golden):
+    """Native bf16 gradients against the reference model's fp32 gradients (golden): within
+    twice the per-tick path's bf16 error plus a small margin, for every parameter."""
+    g = flb_golden
+    c = g["config"]
+    m = _model(c, cuda)
+    m.load_state_dict(g["state_dict"])
+    m.eval()
+    tok, targets = g["tokens"].to(cuda), g["targets"].to(cuda)
+    gn, _ = _train_grads(m, tok, targets, True)
+    gg, _ = _train_grads(m, tok, targets, False)
+    for k, ref in g["grads"].items():
+        ref = ref.to(cuda)
+        e_nat, e_gen = _max_rel(gn[k], ref), _max_rel(gg[k], ref)
+        assert e_nat <= 2 * e_gen + 3e-2, (k, e_nat, e_gen)
