@@ -152,33 +152,46 @@ class FLBGridFunction(torch.autograd.Function):
 
     @staticmethod
     def backward(ctx, *grad_grids):
-        engine, w = ctx.engine, ctx.weights
-        cfg = engine.config
-        L, S = cfg.grid_shape
-        B, D = cfg.batch_size, cfg.dim
-        ws = engine.graph_workspace
-        dev = ws["static_x"].device
-        gstacks = {k: torch.zeros(v.shape, dtype=torch.float32, device=dev) for k, v in w.t.items()}
-        gstruct = nat.BlockGrads(**{k: v.data_ptr() for k, v in gstacks.items()})
-        dg = [g.to(torch.bfloat16).contiguous() if g is not None else None for g in grad_grids]
-        dx = torch.empty((B, S, D), dtype=torch.float32, device=dev)
-        ws_bytes = nat.lib.flb_block_grid_bwd_workspace_bytes(L, S, B, D)
-        wsb = nat.workspace(ws_bytes, dev)
-        nat.check(nat.lib.flb_block_grid_bwd(
-            ctypes.cast(ctypes.pointer(w.struct), ctypes.c_void_p), ws["static_x"].data_ptr(),
-            ws["static_stacked_grids"].data_ptr(), *[nat.ptr(g) for g in dg], dx.data_ptr(),
-            ctypes.cast(ctypes.pointer(gstruct), ctypes.c_void_p), L, S, B, D, w.heads, w.eps,
-            nat.ptr(wsb), ws_bytes, nat.stream_of(dx)), "flb_block_grid_bwd")
-        grads = []
-        for li, layer in enumerate(engine.layers):
-            for name, p in layer.named_parameters():
-                key, sl = _grad_slot(name, D)
-                gl = gstacks[key][li]
-                if sl is not None:
-                    gl = gl[sl]
-                grads.append(gl.reshape(p.shape).to(p.dtype))
+        gstacks, dx = native_flb_backward(ctx.engine, ctx.weights, grad_grids)
         shape, dtype = ctx.x_meta
-        return (None, dx.to(dtype).reshape(shape), *grads)
+        return (None, dx.to(dtype).reshape(shape), *flb_param_grads(ctx.engine, gstacks))
+
+
+def native_flb_backward(engine, w, grad_grids):
+    """flb_block_grid_bwd over the engine's saved grids: (fp32 gradient stacks keyed like the
+    weight stacks, dx float32 [batch, seq, dim])."""
+    cfg = engine.config
+    L, S = cfg.grid_shape
+    B, D = cfg.batch_size, cfg.dim
+    ws = engine.graph_workspace
+    dev = ws["static_x"].device
+    gstacks = {k: torch.zeros(v.shape, dtype=torch.float32, device=dev) for k, v in w.t.items()}
+    gstruct = nat.BlockGrads(**{k: v.data_ptr() for k, v in gstacks.items()})
+    dg = [g.to(torch.bfloat16).contiguous() if g is not None else None for g in grad_grids]
+    dx = torch.empty((B, S, D), dtype=torch.float32, device=dev)
+    ws_bytes = nat.lib.flb_block_grid_bwd_workspace_bytes(L, S, B, D)
+    wsb = nat.workspace(ws_bytes, dev)
+    nat.check(nat.lib.flb_block_grid_bwd(
+        ctypes.cast(ctypes.pointer(w.struct), ctypes.c_void_p), ws["static_x"].data_ptr(),
+        ws["static_stacked_grids"].data_ptr(), *[nat.ptr(g) for g in dg], dx.data_ptr(),
+        ctypes.cast(ctypes.pointer(gstruct), ctypes.c_void_p), L, S, B, D, w.heads, w.eps,
+        nat.ptr(wsb), ws_bytes, nat.stream_of(dx)), "flb_block_grid_bwd")
+    return gstacks, dx
+
+
+def flb_param_grads(engine, gstacks):
+    """Per-parameter gradients (each parameter's shape and dtype, in (layer, named_parameters)
+    order) from the fp32 gradient stacks."""
+    D = engine.config.dim
+    grads = []
+    for li, layer in enumerate(engine.layers):
+        for name, p in layer.named_parameters():
+            key, sl = _grad_slot(name, D)
+            gl = gstacks[key][li]
+            if sl is not None:
+                gl = gl[sl]
+            grads.append(gl.reshape(p.shape).to(p.dtype, copy=True))
+    return grads
 
 
 def native_flb_train_forward(engine, x):

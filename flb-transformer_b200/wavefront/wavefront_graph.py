@@ -21,8 +21,8 @@ Contract (what capture freezes):
     (and the reference's): the next call overwrites them;
   * the cell must be capturable (no host synchronisation, no data-dependent shapes).
 Tanh grid cells that take the persistent-kernel fast path need no graph; the runner refuses
-them (call the engine directly). An inference capture (backward=False) of FLB block cells
-captures the native whole-grid forward (wavefront.flb_cells) instead of the tick loop.
+them (call the engine directly). FLB block cells (bf16) capture the native whole-grid forward
+and backward (wavefront.flb_cells) instead of the tick loops.
 """
 from __future__ import annotations
 
@@ -69,6 +69,11 @@ class _GraphedEngineFunction(torch.autograd.Function):
         if runner.g_bwd is None:
             raise RuntimeError("GraphedWavefrontEngine was captured with backward=False")
         runner.g_bwd.replay()
+        if runner.native_flb:
+            from .flb_cells import flb_param_grads
+            grad_params = flb_param_grads(eng, runner.flb_grads)
+            return (None, runner.flb_dx.to(ws["static_x"].dtype).clone(), None,
+                    *([None] * len(ctx.has_states)), *grad_params)
         grad_x = ws["static_grad_x"].clone()
         grad_states = [ws["static_current_grad_grids"][p][nc:nc + dock].clone() if has else None
                        for p, has in enumerate(ctx.has_states)]
@@ -97,8 +102,8 @@ class GraphedWavefrontEngine:
         self.x_shape, self.x_dtype = tuple(x.shape), x.dtype
         engine._init_buffers(x)
         from .flb_cells import native_flb_applies
-        # inference graphs of FLB block cells capture the native whole-grid forward
-        self.native_flb = (not backward) and native_flb_applies(engine, x)
+        # FLB block cells: the graphs capture the native whole-grid forward and backward
+        self.native_flb = native_flb_applies(engine, x)
         ws = engine.graph_workspace
         self.accs = layer_grad_accumulators(ws, engine.stacked_params, self.num_layers, x.device)
         # (layer index, stacked-parameter name, parameter) in the order grads are returned
@@ -138,8 +143,10 @@ class GraphedWavefrontEngine:
         eng, cfg = self.engine, self.engine.config
         ws = eng.graph_workspace
         if self.native_flb:
-            from .flb_cells import native_flb_forward
-            native_flb_forward(eng, ws["static_x"], ws["static_stacked_grids"])
+            from .flb_cells import native_flb_forward, BlockWeightStacks
+            self.flb_weights = BlockWeightStacks(list(eng.layers))
+            native_flb_forward(eng, ws["static_x"], ws["static_stacked_grids"],
+                               weights=self.flb_weights)
             return
         refresh_stacked_params(eng.layers, eng.stacked_params)
         with torch.no_grad():
@@ -153,6 +160,12 @@ class GraphedWavefrontEngine:
     def _backward_loop(self):
         eng, cfg = self.engine, self.engine.config
         ws = eng.graph_workspace
+        if self.native_flb:
+            from .flb_cells import native_flb_backward
+            n = self.num_cells
+            self.flb_grads, self.flb_dx = native_flb_backward(
+                eng, self.flb_weights, [g[:n] for g in ws["static_grad_outputs"]])
+            return
         wavefront_backend.execute_backward(
             eng.active_cells_buffer.shape[0], cfg.num_ports, len(cfg.dependencies),
             self.num_cells, eng.compiled_backward, eng.active_cells_buffer,

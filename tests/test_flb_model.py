@@ -211,3 +211,35 @@ def test_native_flb_training_against_reference(cuda, flb_golden):
         ref = ref.to(cuda)
         e_nat, e_gen = _max_rel(gn[k], ref), _max_rel(gg[k], ref)
         assert e_nat <= 2 * e_gen + 3e-2, (k, e_nat, e_gen)
+
+
+@pytest.mark.gpu
+def test_native_flb_graphed_training_matches_eager(cuda):
+    """The native FLB forward and backward captured by GraphedWavefrontEngine give the eager
+    native path's loss and gradients, over two steps with an in-place parameter update."""
+    ma = _bf16_model(17)
+    mb = _bf16_model(17)
+    tok = torch.randint(0, 50, (3, 6), device=cuda)
+    targets = torch.randint(0, 50, (3, 6), device=cuda)
+    with torch.autocast("cuda", dtype=torch.bfloat16):
+        graphed = mb.engine.graphed(mb.embedding(tok).detach())
+    assert graphed.native_flb
+    for step in range(2):
+        outs = []
+        for m, eng in ((ma, None), (mb, graphed)):
+            m.zero_grad(set_to_none=True)
+            with torch.autocast("cuda", dtype=torch.bfloat16):
+                logits, aux, _ = m(tok, engine=eng)
+            loss = F.cross_entropy(logits.float().reshape(-1, 50), targets.reshape(-1)) + aux
+            loss.backward()
+            outs.append((loss.item(), {k: p.grad.float().clone() for k, p in m.named_parameters()
+                                       if p.grad is not None}))
+        (la, ga), (lb, gb) = outs
+        assert abs(la - lb) <= 1e-3 * abs(la)
+        assert set(ga) == set(gb)
+        for k in ga:
+            assert _max_rel(gb[k], ga[k]) < 1e-2, (step, k)
+        with torch.no_grad():
+            for pa, pb in zip(ma.parameters(), mb.parameters()):
+                pa.mul_(0.95)
+                pb.mul_(0.95)
