@@ -379,9 +379,9 @@ def extra_engine(device, steps=2, warmup=1):
 def extra_flb_e2e(device, steps=3, decode_steps=8):
     """The FLB model end to end: 12 layers, d_model 768 (8 heads of additive attention per
     cell, as FLB_Block fixes), vocab 32000, weights ~ N(0, 0.02), a 16 x 1024 prompt of uniform
-    token ids; bf16 autocast, inference. The grid runs as the native FLB cell forward replayed
-    as one CUDA graph per forward; a decode step re-runs the sliding 1024-token window (the
-    model carries no usable context) and appends the argmax token."""
+    token ids; bf16 autocast. The grid runs as the native FLB cells replayed as CUDA graphs:
+    the inference forward, greedy decode steps (each re-runs the sliding 1024-token window: the
+    model carries no usable context) and a training step (cross-entropy + aux, backward)."""
     from flb_model import FLBTransformer, greedy_decode
     V, D, L, S, B = 32000, 768, 12, 1024, 16
     torch.manual_seed(0)
@@ -404,12 +404,30 @@ def extra_flb_e2e(device, steps=3, decode_steps=8):
         fwd_ms = time_steps(lambda: m(prompt, engine=g), steps, 1) / steps
         greedy_decode(m, prompt, 1, engine=g)
         dec_ms = time_steps(lambda: greedy_decode(m, prompt, decode_steps, engine=g), 1, 1)
-    return {"workload": "FLB model 12 layers d768 vocab32000, prompt 16x1024, bf16 inference",
-            "native_cells": bool(g.native_flb), "capture_s": round(capture_s, 2),
+    del g
+    # training step (forward + backward, cross-entropy + aux), forward and backward captured
+    m.train()
+    targets = torch.randint(0, V, (B, S), device=device,
+                            generator=torch.Generator(device=device).manual_seed(2))
+    with torch.autocast("cuda", dtype=torch.bfloat16):
+        gt = m.engine.graphed(m.embedding(prompt).detach())
+
+    def train_step():
+        m.zero_grad(set_to_none=True)
+        with torch.autocast("cuda", dtype=torch.bfloat16):
+            logits, aux, _ = m(prompt, engine=gt)
+        loss = torch.nn.functional.cross_entropy(logits.float().reshape(-1, V),
+                                                 targets.reshape(-1)) + aux
+        loss.backward()
+    train_step()
+    train_ms = time_steps(train_step, steps, 1) / steps
+    return {"workload": "FLB model 12 layers d768 vocab32000, prompt 16x1024, bf16",
+            "native_cells": bool(gt.native_flb), "capture_s": round(capture_s, 2),
             "forward_ms": round(fwd_ms, 2), "cells_per_s": L * S / (fwd_ms * 1e-3),
             "prompt_tokens_per_s": B * S / (fwd_ms * 1e-3),
             "decode_steps": decode_steps, "decode_ms_per_step": round(dec_ms / decode_steps, 2),
-            "decode_tokens_per_s": B * decode_steps / (dec_ms * 1e-3)}
+            "decode_tokens_per_s": B * decode_steps / (dec_ms * 1e-3),
+            "train_step_ms": round(train_ms, 2), "train_tokens_per_s": B * S / (train_ms * 1e-3)}
 
 
 # ------------------------------------------------------------------ arms
