@@ -14,21 +14,24 @@ struct BlasHandle {
   cublasHandle_t h = nullptr;
   int dev = -1;
 };
-inline thread_local BlasHandle t_blas_handle;
+// slot 0: the caller's stream; slot 1: a library side stream running concurrently with it
+inline thread_local BlasHandle t_blas_handle[2];
 
-inline int blas(cudaStream_t s, void* ws, size_t ws_bytes, cublasHandle_t* out) {
+inline int blas(cudaStream_t s, void* ws, size_t ws_bytes, cublasHandle_t* out, int slot = 0) {
   int dev = 0;
   cudaGetDevice(&dev);
-  if (t_blas_handle.h == nullptr || t_blas_handle.dev != dev) {
-    if (cublasCreate(&t_blas_handle.h) != CUBLAS_STATUS_SUCCESS)
-      return fail(FLB_ERR_CUDA, "cublasCreate failed");
-    t_blas_handle.dev = dev;
+  BlasHandle& bh = t_blas_handle[slot];
+  if (bh.h == nullptr || bh.dev != dev) {
+    if (bh.h != nullptr) cublasDestroy(bh.h);
+    bh.h = nullptr;
+    if (cublasCreate(&bh.h) != CUBLAS_STATUS_SUCCESS) return fail(FLB_ERR_CUDA, "cublasCreate failed");
+    bh.dev = dev;
   }
-  if (cublasSetStream(t_blas_handle.h, s) != CUBLAS_STATUS_SUCCESS)
+  if (cublasSetStream(bh.h, s) != CUBLAS_STATUS_SUCCESS)
     return fail(FLB_ERR_CUDA, "cublasSetStream failed");
-  if (cublasSetWorkspace(t_blas_handle.h, ws, ws_bytes) != CUBLAS_STATUS_SUCCESS)
+  if (cublasSetWorkspace(bh.h, ws, ws_bytes) != CUBLAS_STATUS_SUCCESS)
     return fail(FLB_ERR_CUDA, "cublasSetWorkspace failed");
-  *out = t_blas_handle.h;
+  *out = bh.h;
   return FLB_OK;
 }
 

@@ -111,6 +111,9 @@ static int check_block_args(const flb_block_weights* weights, const void* x, con
   if ((L * S + L) * batch * D * 4 > ((int64_t)1 << 40) || 3 * batch * D > (1 << 30) ||
       L + 2 * S > (1 << 30))
     return fail(FLB_ERR_SHAPE, "block_grid: grid too large");
+  const int64_t nmax = (L + 1) / 2 < S ? (L + 1) / 2 : S;
+  if (nmax * batch > 65535)
+    return fail(FLB_ERR_UNSUPPORTED, "block_grid: cells per tick x batch must be <= 65535");
   if (((uintptr_t)x | (uintptr_t)grids | (uintptr_t)w.w_prior_lat | (uintptr_t)w.w_prior_fdbk |
        (uintptr_t)w.w_gate_l | (uintptr_t)w.w_gate_x | (uintptr_t)w.w_qkv | (uintptr_t)w.w_o) & 15u)
     return fail(FLB_ERR_ALIGN, "block_grid: bf16 tensors must be 16-byte aligned");

@@ -23,6 +23,7 @@
 #include <cuda_bf16.h>
 
 #include <algorithm>
+#include <mutex>
 
 #include "blas.cuh"
 #include "common.cuh"
@@ -711,7 +712,38 @@ struct BlockBwdWs {
   bf16 *d_o, *d_att, *d_qkv, *d_zx, *d_zl, *d_lp_h, *d_fp_h;
   float *dT, *d_top, *d_lp, *d_fp, *d_lr, *dA, *dG, *dx;
   void* blas;
+  void* blas_side;
 };
+
+// A per-device side stream and fork/join events of the backward: the weight-gradient GEMMs of
+// a tick run on it while the input-gradient chain continues on the caller's stream. Created on
+// the first backward call on a device and kept until exit.
+struct SideStream {
+  cudaStream_t s = nullptr;
+  cudaEvent_t fork[5] = {}, join = nullptr;
+};
+
+int side_stream(SideStream** out) {
+  static std::mutex mu;
+  static SideStream per_dev[64];
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (dev < 0 || dev >= 64) return fail(FLB_ERR_UNSUPPORTED, "block_grid_bwd: device index >= 64");
+  std::lock_guard<std::mutex> lock(mu);
+  SideStream& ss = per_dev[dev];
+  if (ss.s == nullptr) {
+    cudaError_t e = cudaStreamCreateWithFlags(&ss.s, cudaStreamNonBlocking);
+    for (int i = 0; e == cudaSuccess && i < 5; ++i)
+      e = cudaEventCreateWithFlags(&ss.fork[i], cudaEventDisableTiming);
+    if (e == cudaSuccess) e = cudaEventCreateWithFlags(&ss.join, cudaEventDisableTiming);
+    if (e != cudaSuccess) {
+      ss.s = nullptr;
+      return check_cuda(e, "block_grid_bwd side stream");
+    }
+  }
+  *out = &ss;
+  return FLB_OK;
+}
 
 size_t block_bwd_ws_layout(int64_t L, int64_t S, int64_t B, int64_t D, BlockBwdWs* w, void* base) {
   const int64_t nmax = max_cells_per_tick(L, S);
@@ -748,6 +780,7 @@ size_t block_bwd_ws_layout(int64_t L, int64_t S, int64_t B, int64_t D, BlockBwdW
   t.dG = (float*)take((size_t)3 * L * S * B * D * 4);
   t.dx = nullptr;
   t.blas = take(kBlkBlasWs);
+  t.blas_side = take(kBlkBlasWs);
   if (w) *w = t;
   return off;
 }
@@ -764,9 +797,24 @@ int block_grid_bwd(const flb_block_weights* W, const void* x, const void* grids,
                    size_t ws_bytes, cudaStream_t s) {
   BlockBwdWs w;
   block_bwd_ws_layout(L, S, B, D, &w, ws);
-  cublasHandle_t hb;
-  int st = blas(s, w.blas, kBlkBlasWs, &hb);
+  SideStream* side;
+  int st = side_stream(&side);
   if (st != FLB_OK) return st;
+  cublasHandle_t hb, hs;
+  if ((st = blas(s, w.blas, kBlkBlasWs, &hb)) != FLB_OK) return st;
+  if ((st = blas(side->s, w.blas_side, kBlkBlasWs, &hs, 1)) != FLB_OK) return st;
+  // fork: the side stream waits for event k of the tick; join: the caller's stream waits for the
+  // side stream before the next tick reuses the tick buffers the side GEMMs read
+  auto fork = [&](int k) -> int {
+    cudaError_t e = cudaEventRecord(side->fork[k], s);
+    if (e == cudaSuccess) e = cudaStreamWaitEvent(side->s, side->fork[k], 0);
+    return check_cuda(e, "block_grid_bwd fork");
+  };
+  auto join = [&]() -> int {
+    cudaError_t e = cudaEventRecord(side->join, side->s);
+    if (e == cudaSuccess) e = cudaStreamWaitEvent(s, side->join, 0);
+    return check_cuda(e, "block_grid_bwd join");
+  };
   const bf16* xb = reinterpret_cast<const bf16*>(x);
   const bf16* g = reinterpret_cast<const bf16*>(grids);
   const int64_t port_stride = (L * S + L) * B * D;
@@ -803,7 +851,8 @@ int block_grid_bwd(const flb_block_weights* W, const void* x, const void* grids,
     if ((st = gemm_rm(hb, false, false, 3 * Bi, Di, Di, w.d_o, Di, 3 * BD, Wo, Di, 2 * DD, w.d_att,
                       Di, 3 * BD, n, 0.f, CUDA_R_16BF)) != FLB_OK)
       return st;
-    if ((st = gemm_rm(hb, true, false, Di, Di, 3 * Bi, w.d_o, Di, 3 * BD, w.f.att, Di, 3 * BD,
+    if ((st = fork(0)) != FLB_OK) return st;
+    if ((st = gemm_rm(hs, true, false, Di, Di, 3 * Bi, w.d_o, Di, 3 * BD, w.f.att, Di, 3 * BD,
                       G->w_o + (int64_t)l0 * DD, Di, 2 * DD, n, 1.f)) != FLB_OK)
       return st;
     blk_attn3_bwd_kernel<<<(n * Bi * Hi + 7) / 8, 256, 0, s>>>(w.f.qkv, W->v_a, w.d_att, w.d_qkv,
@@ -812,7 +861,8 @@ int block_grid_bwd(const flb_block_weights* W, const void* x, const void* grids,
     if ((st = gemm_rm(hb, false, false, 3 * Bi, Di, 3 * Di, w.d_qkv, 3 * Di, 9 * BD, Wqkv, Di,
                       6 * DD, w.dT, Di, 3 * BD, n, 0.f)) != FLB_OK)
       return st;
-    if ((st = gemm_rm(hb, true, false, 3 * Di, Di, 3 * Bi, w.d_qkv, 3 * Di, 9 * BD, w.f.tok, Di,
+    if ((st = fork(1)) != FLB_OK) return st;
+    if ((st = gemm_rm(hs, true, false, 3 * Di, Di, 3 * Bi, w.d_qkv, 3 * Di, 9 * BD, w.f.tok, Di,
                       3 * BD, G->w_qkv + (int64_t)l0 * 3 * DD, Di, 6 * DD, n, 1.f)) != FLB_OK)
       return st;
     // sensory gate
@@ -822,7 +872,8 @@ int block_grid_bwd(const flb_block_weights* W, const void* x, const void* grids,
     if ((st = gemm_rm(hb, false, false, Bi, Di, Di, w.d_zx, Di, BD, Wgx, Di, 2 * DD, w.d_lr, Di, BD,
                       n, 1.f)) != FLB_OK)
       return st;
-    if ((st = gemm_rm(hb, true, false, Di, Di, Bi, w.d_zx, Di, BD, w.f.tok + D, 3 * Di, 3 * BD,
+    if ((st = fork(2)) != FLB_OK) return st;
+    if ((st = gemm_rm(hs, true, false, Di, Di, Bi, w.d_zx, Di, BD, w.f.tok + D, 3 * Di, 3 * BD,
                       G->w_gate_x + (int64_t)l0 * DD, Di, 2 * DD, n, 1.f)) != FLB_OK)
       return st;
     // lateral gate
@@ -831,7 +882,8 @@ int block_grid_bwd(const flb_block_weights* W, const void* x, const void* grids,
     if ((st = gemm_rm(hb, false, false, Bi, Di, Di, w.d_zl, Di, BD, Wgl, Di, 2 * DD, w.d_fp, Di, BD,
                       n, 1.f)) != FLB_OK)
       return st;
-    if ((st = gemm_rm(hb, true, false, Di, Di, Bi, w.d_zl, Di, BD, w.f.tok + 2 * D, 3 * Di, 3 * BD,
+    if ((st = fork(3)) != FLB_OK) return st;
+    if ((st = gemm_rm(hs, true, false, Di, Di, Bi, w.d_zl, Di, BD, w.f.tok + 2 * D, 3 * Di, 3 * BD,
                       G->w_gate_l + (int64_t)l0 * DD, Di, 2 * DD, n, 1.f)) != FLB_OK)
       return st;
     blk_cast_kernel<<<(unsigned)std::min<int64_t>((n * BD / 2 + 255) / 256, ew), 256, 0, s>>>(
@@ -843,15 +895,17 @@ int block_grid_bwd(const flb_block_weights* W, const void* x, const void* grids,
     if ((st = gemm_rm(hb, false, false, Bi, Di, Di, w.d_fp_h, Di, BD, Wpf, Di, 2 * DD,
                       w.dA + n * BD, Di, BD, n, 0.f)) != FLB_OK)
       return st;
-    if ((st = gemm_rm(hb, true, false, Di, Di, Bi, w.d_lp_h, Di, BD, w.f.ln, Di, BD,
+    if ((st = fork(4)) != FLB_OK) return st;
+    if ((st = gemm_rm(hs, true, false, Di, Di, Bi, w.d_lp_h, Di, BD, w.f.ln, Di, BD,
                       G->w_prior_lat + (int64_t)l0 * DD, Di, 2 * DD, n, 1.f)) != FLB_OK)
       return st;
-    if ((st = gemm_rm(hb, true, false, Di, Di, Bi, w.d_fp_h, Di, BD, w.f.ln + n * BD, Di, BD,
+    if ((st = gemm_rm(hs, true, false, Di, Di, Bi, w.d_fp_h, Di, BD, w.f.ln + n * BD, Di, BD,
                       G->w_prior_fdbk + (int64_t)l0 * DD, Di, 2 * DD, n, 1.f)) != FLB_OK)
       return st;
     blk_ln_bwd_kernel<<<2 * n, 512, 2 * D * sizeof(float), s>>>(
         g, port_stride, w.dA, W->ln_lat_w, W->ln_fdbk_w, w.dG, per_port, G->ln_lat_w,
         G->ln_lat_b, G->ln_fdbk_w, G->ln_fdbk_b, T, l0, n, Li, Si, Bi, Di, eps);
+    if ((st = join()) != FLB_OK) return st;
     launches += 10;  // own kernels (4 recompute + 6 backward)
   }
   count_launches(launches);
