@@ -70,7 +70,22 @@ int grid_bwd(const void* x, int x_layout, const void* W_l, const void* W_t, cons
 int grid_fwd_impl(const void* x, int x_layout, const void* W_l, const void* W_t, const void* U,
                   const float* bias, const void* top, void* h_out, int64_t R, int64_t C,
                   int64_t B, int64_t H, int64_t G, void* ws, size_t ws_bytes, int check_timeout,
-                  cudaStream_t s, int64_t drop_cell, uint32_t spin_limit);
+                  cudaStream_t s, int64_t drop_cell, uint32_t spin_limit,
+                  const flb_grid_band* band, void* saved_top);
+size_t grid_band_block_bytes(int64_t C, int64_t B, int64_t H);
+int grid_band_fwd(const void* x, int x_layout, const void* W_l, const void* W_t, const void* U,
+                  const float* bias, const void* top, void* h_out, void* saved_top, int64_t R,
+                  int64_t C, int64_t B, int64_t H, int64_t G, const flb_grid_band* band, void* ws,
+                  size_t ws_bytes, int check_timeout, cudaStream_t s);
+int grid_band_bwd(const void* x, int x_layout, const void* W_l, const void* W_t, const void* U,
+                  const void* top, const void* h_out, const void* dh, float* dW_l, float* dW_t,
+                  float* dU, float* dbias, void* dx, void* dtop, int64_t R, int64_t C, int64_t B,
+                  int64_t H, int64_t G, const flb_grid_band* band, void* ws, size_t ws_bytes,
+                  int check_timeout, cudaStream_t s);
+int ipc_alloc(size_t bytes, void** dev_ptr, void* handle);
+int ipc_open(const void* handle, void** dev_ptr);
+int ipc_close(void* dev_ptr);
+int ipc_free(void* dev_ptr);
 int grid_fwd_static(const void* W_l, const void* W_t, const float* bias, const void* top,
                     void* h_out, int64_t R, int64_t C, int64_t B, int64_t H, int64_t G,
                     int check_timeout, cudaStream_t s);
@@ -297,7 +312,43 @@ int flb_grid_fwd_drop_flag_test(const void* x, int x_layout, const void* W_l, co
     return fail(FLB_ERR_SHAPE, "grid drop-flag test: cell outside the grid");
   return grid_fwd_impl(x, x_layout, W_l, W_t, U, bias, top, h_out, R, C, B, H, G, workspace,
                        workspace_bytes, 1, as_stream(stream), drop_row * C + drop_col,
-                       spin_limit);
+                       spin_limit, nullptr, nullptr);
+}
+
+size_t flb_grid_band_block_bytes(int64_t C, int64_t B, int64_t H) {
+  if (C < 1 || B < 1 || H < 1) return 0;
+  return grid_band_block_bytes(C, B, H);
+}
+
+int flb_ipc_alloc(size_t bytes, void** dev_ptr, void* handle) { return ipc_alloc(bytes, dev_ptr, handle); }
+int flb_ipc_open(const void* handle, void** dev_ptr) { return ipc_open(handle, dev_ptr); }
+int flb_ipc_close(void* dev_ptr) {
+  if (!dev_ptr) return fail(FLB_ERR_SHAPE, "ipc_close: null pointer");
+  return ipc_close(dev_ptr);
+}
+int flb_ipc_free(void* dev_ptr) {
+  if (!dev_ptr) return fail(FLB_ERR_SHAPE, "ipc_free: null pointer");
+  return ipc_free(dev_ptr);
+}
+
+int flb_grid_band_fwd(const void* x, int x_layout, const void* W_l, const void* W_t,
+                      const void* U, const float* bias, const void* top, void* h_out,
+                      void* saved_top, int64_t R, int64_t C, int64_t B, int64_t H, int64_t G,
+                      const flb_grid_band* band, void* workspace, size_t workspace_bytes,
+                      int check_timeout, void* stream) {
+  return grid_band_fwd(x, x_layout, W_l, W_t, U, bias, top, h_out, saved_top, R, C, B, H, G, band,
+                       workspace, workspace_bytes, check_timeout, as_stream(stream));
+}
+
+int flb_grid_band_bwd(const void* x, int x_layout, const void* W_l, const void* W_t,
+                      const void* U, const void* top, const void* h_out, const void* dh,
+                      float* dW_l, float* dW_t, float* dU, float* dbias, void* dx, void* dtop,
+                      int64_t R, int64_t C, int64_t B, int64_t H, int64_t G,
+                      const flb_grid_band* band, void* workspace, size_t workspace_bytes,
+                      int check_timeout, void* stream) {
+  return grid_band_bwd(x, x_layout, W_l, W_t, U, top, h_out, dh, dW_l, dW_t, dU, dbias, dx, dtop,
+                       R, C, B, H, G, band, workspace, workspace_bytes, check_timeout,
+                       as_stream(stream));
 }
 
 int flb_grid_fwd_static(const void* W_l, const void* W_t, const float* bias, const void* top,

@@ -24,6 +24,7 @@
 // cuBLAS GEMMs over dz and the saved h (and x), and db is reduced inside the sweep.
 #include <cublas_v2.h>
 
+#include <cstring>
 #include <mutex>
 #include <string>
 
@@ -55,6 +56,35 @@ __device__ __forceinline__ bool wait_flag(const int* p, int want, uint32_t limit
   }
   return false;
 }
+// System scope: flags written by another GPU over NVLink, or written into another GPU's memory.
+__device__ __forceinline__ int ld_acquire_sys(const int* p) {
+  int v;
+  asm volatile("ld.acquire.sys.global.b32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  return v;
+}
+__device__ __forceinline__ void st_release_sys(int* p, int v) {
+  asm volatile("st.release.sys.global.b32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+__device__ __forceinline__ bool wait_flag_sys(const int* p, int want, uint32_t limit) {
+  for (uint32_t i = 0; i < limit; ++i) {
+    if (ld_acquire_sys(p) == want) return true;
+    if (i > 64) __nanosleep(128);
+  }
+  return false;
+}
+// Shared -> global tile store (no multicast) and its bulk-group completion.
+__device__ __forceinline__ void tma_store_3d(const void* tmap, const void* src, int c0, int c1,
+                                             int c2) {
+  asm volatile(
+      "cp.async.bulk.tensor.3d.global.shared::cta.bulk_group [%0, {%2, %3, %4}], [%1];" ::"l"(tmap),
+      "r"(sm100::smem_u32(src)), "r"(c0), "r"(c1), "r"(c2)
+      : "memory");
+}
+__device__ __forceinline__ void bulk_commit() { asm volatile("cp.async.bulk.commit_group;" ::: "memory"); }
+__device__ __forceinline__ void bulk_wait_read_all() {
+  asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory");
+}
+__device__ __forceinline__ void bulk_wait_all() { asm volatile("cp.async.bulk.wait_group 0;" ::: "memory"); }
 
 __device__ __forceinline__ void tma_load_4d(void* dst, const void* tmap, uint64_t* bar, int c0,
                                             int c1, int c2, int c3) {
@@ -90,6 +120,20 @@ struct GridParams {
   int* err;
   int64_t drop_cell;     // failure-detection check: this cell's flag is never released (-1: none)
   uint32_t spin_limit;   // flag polls before a wait gives up
+  // Row bands: this launch is rows row0 .. row0 + R - 1 of a taller grid (weights are indexed by
+  // global row), and its edge rows exchange [C, B, H] halos with the neighbouring bands on other
+  // GPUs. The in-edge row (forward: row 0, backward: row R - 1) reads its other-row input from the
+  // local receive buffer (tmTop) once the neighbour's per-column flags say it landed, then
+  // acknowledges; the out-edge row (forward: row R - 1, backward: row 0) also stores its output
+  // into the neighbour's receive buffer, after that neighbour acknowledged the previous epoch.
+  int row0;
+  const int* halo_in_flags;  // local [C][2], set to epoch by the neighbour (null: no in-halo)
+  int* halo_in_ack;          // neighbour's [C][2], set to epoch here once a column is loaded
+  __nv_bfloat16* halo_out;   // neighbour's receive buffer [C, B, H] (null: no out-halo)
+  int* halo_out_flags;       // neighbour's [C][2]
+  const int* halo_out_ack;   // local [C][2], the neighbour's acknowledgements
+  int epoch;                 // this call's halo epoch (>= 1; the previous call's is epoch - 1)
+  int save_top;              // forward: keep the received halo rows through tmSave
 };
 
 // One kernel body for both directions. Forward (reverse = 0): rows ascend, cells walk right,
@@ -100,7 +144,7 @@ __global__ void __launch_bounds__(128, 1)
 grid_sweep_kernel(const __grid_constant__ CUtensorMap tmWa, const __grid_constant__ CUtensorMap tmWb,
                   const __grid_constant__ CUtensorMap tmIn, const __grid_constant__ CUtensorMap tmTop,
                   const __grid_constant__ CUtensorMap tmE1, const __grid_constant__ CUtensorMap tmE2,
-                  GridParams p) {
+                  const __grid_constant__ CUtensorMap tmSave, GridParams p) {
   using namespace sm100;
   using Cfg = GridCfg<H>;
   constexpr int NH = H / 128;  // feature halves (CTAs per row)
@@ -143,10 +187,13 @@ grid_sweep_kernel(const __grid_constant__ CUtensorMap tmWa, const __grid_constan
 
   for (int ri = worker; ri < R; ri += nworkers) {
     const int r = p.reverse ? (R - 1 - ri) : ri;
-    const int g = (p.G > 1) ? r : 0;
+    const int g = (p.G > 1) ? p.row0 + r : 0;
     // The other-row edge uses the weights of the row that consumes it: forward, cell (r, c)
     // reads h[r-1][c] through its own W_t[r]; backward, dz[r+1][c] flows back through W_t[r+1].
-    const int g_other = (p.G > 1 && p.reverse) ? min(r + 1, R - 1) : g;
+    const int g_other = (p.G > 1 && p.reverse) ? min(p.row0 + r + 1, p.G - 1) : g;
+    const bool in_edge = p.reverse ? (r == R - 1) : (r == 0);
+    const bool halo_in = in_edge && p.halo_in_flags != nullptr;
+    const bool halo_out = (p.reverse ? (r == 0) : (r == R - 1)) && p.halo_out != nullptr;
     if (ri == worker || p.G > 1) {
       if (tid == 0) {
         mbar_arrive_expect_tx(&bar_w, Cfg::KATOMS * Cfg::W_ATOM);
@@ -192,6 +239,14 @@ grid_sweep_kernel(const __grid_constant__ CUtensorMap tmWa, const __grid_constan
         if (r_nb >= 0 && r_nb < R)
           for (int hh = 0; hh < NH; ++hh) ok &= wait_flag(p.flags + ((int64_t)r_nb * C + c) * 2 + hh, 1, p.spin_limit);
         if (!ok) atomicExch(p.err, 2);
+        bool ok_halo = true;
+        if (halo_in)  // the neighbour band's edge row, both feature halves, this epoch
+          for (int hh = 0; hh < NH; ++hh)
+            ok_halo &= wait_flag_sys(p.halo_in_flags + c * 2 + hh, p.epoch, p.spin_limit);
+        if (halo_out)  // the neighbour has loaded the previous epoch's column c: it may be rewritten
+          for (int hh = 0; hh < NH; ++hh)
+            ok_halo &= wait_flag_sys(p.halo_out_ack + c * 2 + hh, p.epoch - 1, p.spin_limit);
+        if (!ok_halo) atomicExch(p.err, 6);
         fence_async_global();  // order the acquired generic stores before the TMA reads
         uint8_t* sIn = sm + Cfg::OFF_IN;
         mbar_arrive_expect_tx(&bar_in, Cfg::KATOMS * B * 128);
@@ -199,12 +254,21 @@ grid_sweep_kernel(const __grid_constant__ CUtensorMap tmWa, const __grid_constan
         for (int a = 0; a < H / 64; ++a) {
           // out-of-grid coordinates are zero-filled: the zero boundary
           tma_load_4d(sIn + a * B * 128, &tmIn, &bar_in, a * 64, 0, c_nb, r);
-          if (!p.reverse && r == 0 && p.has_top)
+          if (in_edge && p.has_top)
             tma_load_3d(sIn + (H / 64 + a) * B * 128, &tmTop, &bar_in, a * 64, 0, c);
           else
             tma_load_4d(sIn + (H / 64 + a) * B * 128, &tmIn, &bar_in, a * 64, 0, c, r_nb);
         }
         if (!mbar_wait(&bar_in, n_cell & 1u, kWaitLimit)) atomicExch(p.err, 3);
+        if (halo_in) {
+          if (p.save_top) {  // this CTA's feature half of the received rows, back out of shared memory
+#pragma unroll
+            for (int a = half * 2; a < half * 2 + 2; ++a)
+              tma_store_3d(&tmSave, sIn + (H / 64 + a) * B * 128, a * 64, 0, c);
+            bulk_commit();
+          }
+          st_release_sys(p.halo_in_ack + c * 2 + half, p.epoch);
+        }
         tc_fence_after();
         const uint32_t wa = smem_u32(sm + Cfg::OFF_W), ia = smem_u32(sIn);
 #pragma unroll
@@ -214,7 +278,13 @@ grid_sweep_kernel(const __grid_constant__ CUtensorMap tmWa, const __grid_constan
           umma_f16(tmem, adesc, bdesc, idesc, kk > 0 ? 1u : 0u);
         }
         umma_commit(&bar_mma);
+        // the next cell's loads overwrite these rows: the store must have read them by then
+        if (halo_in && p.save_top) bulk_wait_read_all();
       }
+      // a halo wait lasts as long as the other GPU takes to get there (its launch may start late):
+      // hold the CTA here, behind thread 0's bounded spins, rather than in the MMA barrier's
+      // shorter bounded wait
+      if (halo_in || halo_out) __syncthreads();
       __syncwarp();
       if (!mbar_wait(&bar_mma, n_cell & 1u, kWaitLimit)) atomicExch(p.err, 4);
       tc_fence_after();
@@ -243,7 +313,9 @@ grid_sweep_kernel(const __grid_constant__ CUtensorMap tmWa, const __grid_constan
           if (!p.reverse) {
             z += bias_f;
             if (stage_add) z += reinterpret_cast<const float*>(sE)[b * 128 + fl];
-            p.out[o] = __float2bfloat16_rn(tanh_approx(z));
+            const __nv_bfloat16 hb = __float2bfloat16_rn(tanh_approx(z));
+            p.out[o] = hb;
+            if (halo_out) p.halo_out[((int64_t)c * B + b) * H + f] = hb;
           } else {
             const float hv = __bfloat162float(reinterpret_cast<const __nv_bfloat16*>(sE)[b * 128 + fl]);
             const float dhv = __bfloat162float(
@@ -251,18 +323,26 @@ grid_sweep_kernel(const __grid_constant__ CUtensorMap tmWa, const __grid_constan
             const float dz = (z + dhv) * (1.f - hv * hv);
             const __nv_bfloat16 dzb = __float2bfloat16_rn(dz);
             p.out[o] = dzb;
+            if (halo_out) p.halo_out[((int64_t)c * B + b) * H + f] = dzb;
             if (p.out2) p.out2[(((int64_t)b * R + r) * C + c) * H + f] = dzb;
             db_acc += dz;
           }
         }
       }
-      __threadfence();
+      if (halo_out)
+        __threadfence_system();  // the halo stores reach the other GPU before its flag
+      else
+        __threadfence();
       tc_fence_before();
       __syncthreads();
-      if (tid == 0 && cell != p.drop_cell) st_release(p.flags + cell * 2 + half, 1);
+      if (tid == 0 && cell != p.drop_cell) {
+        st_release(p.flags + cell * 2 + half, 1);
+        if (halo_out) st_release_sys(p.halo_out_flags + c * 2 + half, p.epoch);
+      }
     }
   }
   if (p.reverse && db_group >= 0) atomicAdd(p.dbias + (int64_t)db_group * H + f, db_acc);
+  if (tid == 0 && p.save_top && p.halo_in_flags != nullptr) bulk_wait_all();
   tc_fence_before();
   __syncthreads();
   if (warp == 0) tmem_dealloc(tmem, 64);
@@ -368,7 +448,7 @@ int make_ep_map(CUtensorMap* m, const void* X, CUtensorMapDataType dt, int esz, 
 template <int H>
 int launch_sweep(const CUtensorMap& wa, const CUtensorMap& wb, const CUtensorMap& in,
                  const CUtensorMap& top, const CUtensorMap& e1, const CUtensorMap& e2,
-                 const GridParams& p, cudaStream_t s, int* grid_ctas) {
+                 const CUtensorMap& save, const GridParams& p, cudaStream_t s, int* grid_ctas) {
   const int smem = GridCfg<H>::smem(p.B);
   static bool attr = false;
   if (!attr) {
@@ -387,7 +467,7 @@ int launch_sweep(const CUtensorMap& wa, const CUtensorMap& wb, const CUtensorMap
   int workers = std::min<int>(p.R, capacity / NH);
   if (workers < 1) return fail(FLB_ERR_LAUNCH, "grid_sweep: not enough resident CTAs");
   *grid_ctas = workers * NH;
-  grid_sweep_kernel<H><<<workers * NH, 128, smem, s>>>(wa, wb, in, top, e1, e2, p);
+  grid_sweep_kernel<H><<<workers * NH, 128, smem, s>>>(wa, wb, in, top, e1, e2, save, p);
   count_launches(1);
   return check_cuda(cudaGetLastError(), "grid_sweep launch");
 }
@@ -410,7 +490,53 @@ int read_err(const int* err, cudaStream_t s, const char* what) {
   return FLB_OK;
 }
 
+// A rank's receive block for row bands (in its own memory, mapped into its neighbours):
+// [fwd halo C*B*H bf16][bwd halo C*B*H bf16][fwd flags C*2][bwd flags C*2][fwd acks C*2]
+// [bwd acks C*2] (int32), each part 256-byte aligned. The forward halo is written by the band
+// above (its last row), the backward halo by the band below (its first row's dz); acks are
+// written by the band that consumed this rank's outgoing halo.
+struct BandBlock {
+  __nv_bfloat16 *fwd_halo, *bwd_halo;
+  int *fwd_flags, *bwd_flags, *fwd_acks, *bwd_acks;
+  size_t total;
+};
+BandBlock band_block(void* base, int64_t C, int64_t B, int64_t H) {
+  BandBlock k{};
+  uint8_t* p = reinterpret_cast<uint8_t*>(base);
+  size_t o = 0;
+  auto take = [&](size_t n) { uint8_t* q = p ? p + o : nullptr; o += al(n); return q; };
+  k.fwd_halo = (__nv_bfloat16*)take((size_t)(C * B * H) * 2);
+  k.bwd_halo = (__nv_bfloat16*)take((size_t)(C * B * H) * 2);
+  k.fwd_flags = (int*)take((size_t)C * 2 * sizeof(int));
+  k.bwd_flags = (int*)take((size_t)C * 2 * sizeof(int));
+  k.fwd_acks = (int*)take((size_t)C * 2 * sizeof(int));
+  k.bwd_acks = (int*)take((size_t)C * 2 * sizeof(int));
+  k.total = o;
+  return k;
+}
+
+int check_band(const flb_grid_band* band, int64_t R, int64_t C, int64_t B, int64_t H, int64_t G) {
+  if (!band) return check_grid_args(R, C, B, H, G);
+  int st = check_grid_args(R, C, B, H, 1);
+  if (st != FLB_OK) return st;
+  const int64_t T = band->rows_total;
+  if (band->row0 < 0 || R < 1 || band->row0 + R > T || T > (int64_t)1 << 20)
+    return fail(FLB_ERR_SHAPE, "grid band: rows row0 .. row0 + R - 1 must lie in 0 .. rows_total - 1");
+  if (!(G == 1 || G == T)) return fail(FLB_ERR_SHAPE, "grid band: G must be 1 or rows_total");
+  if (!band->own_block) return fail(FLB_ERR_SHAPE, "grid band: null own_block");
+  if ((band->up_block == nullptr) != (band->row0 == 0))
+    return fail(FLB_ERR_SHAPE, "grid band: up_block must be given exactly when row0 > 0");
+  if ((band->down_block == nullptr) != (band->row0 + R == T))
+    return fail(FLB_ERR_SHAPE, "grid band: down_block must be given exactly when rows follow this band");
+  if (band->epoch < 1) return fail(FLB_ERR_SHAPE, "grid band: epoch must be >= 1");
+  return FLB_OK;
+}
+
 }  // namespace
+
+size_t grid_band_block_bytes(int64_t C, int64_t B, int64_t H) {
+  return band_block(nullptr, C, B, H).total;
+}
 
 size_t grid_workspace_bytes(int64_t R, int64_t C, int64_t B, int64_t H, int64_t G, int has_U) {
   return carve(nullptr, R, C, B, H, G, has_U).total;
@@ -419,10 +545,20 @@ size_t grid_workspace_bytes(int64_t R, int64_t C, int64_t B, int64_t H, int64_t 
 int grid_fwd_impl(const void* x, int x_layout, const void* W_l, const void* W_t, const void* U,
                   const float* bias, const void* top, void* h_out, int64_t R, int64_t C,
                   int64_t B, int64_t H, int64_t G, void* ws, size_t ws_bytes, int check_timeout,
-                  cudaStream_t s, int64_t drop_cell, uint32_t spin_limit) {
-  int st = check_grid_args(R, C, B, H, G);
+                  cudaStream_t s, int64_t drop_cell, uint32_t spin_limit,
+                  const flb_grid_band* band, void* saved_top) {
+  int st = check_band(band, R, C, B, H, G);
   if (st != FLB_OK) return st;
   if (!W_l || !W_t || !bias || !h_out || (U && !x)) return fail(FLB_ERR_SHAPE, "grid_fwd: null pointer");
+  const bool from_up = band && band->up_block;
+  if (from_up && (top || !saved_top))
+    return fail(FLB_ERR_SHAPE, "grid band fwd: below the first band, top must be NULL and saved_top given");
+  BandBlock own{}, up{}, down{};
+  if (band) {
+    own = band_block(band->own_block, C, B, H);
+    if (band->up_block) up = band_block(band->up_block, C, B, H);
+    if (band->down_block) down = band_block(band->down_block, C, B, H);
+  }
   GridWs w = carve(ws, R, C, B, H, G, U != nullptr);
   if (!ws || ws_bytes < w.total) return fail(FLB_ERR_WORKSPACE, "grid_fwd: workspace smaller than flb_grid_workspace_bytes()");
   cudaError_t e = cudaMemsetAsync(w.err, 0, 256, s);
@@ -439,11 +575,14 @@ int grid_fwd_impl(const void* x, int x_layout, const void* W_l, const void* W_t,
   if ((st = make_w_map(&mWl, W_l, G, H)) != FLB_OK) return st;
   if ((st = make_w_map(&mWt, W_t, G, H)) != FLB_OK) return st;
   if ((st = make_grid_map(&mIn, h_out, R, C, B, H)) != FLB_OK) return st;
-  if (top) {
-    if ((st = make_top_map(&mTop, top, C, B, H)) != FLB_OK) return st;
+  const void* top_src = from_up ? (const void*)own.fwd_halo : top;
+  if (top_src) {
+    if ((st = make_top_map(&mTop, top_src, C, B, H)) != FLB_OK) return st;
   } else {
     mTop = mIn;
   }
+  CUtensorMap mSave = mIn;
+  if (from_up && (st = make_top_map(&mSave, saved_top, C, B, H)) != FLB_OK) return st;
   CUtensorMap mAdd = mIn;
   if (U && (st = make_ep_map(&mAdd, w.add, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4, x_layout, R, C, B, H)) != FLB_OK)
     return st;
@@ -454,14 +593,28 @@ int grid_fwd_impl(const void* x, int x_layout, const void* W_l, const void* W_t,
   p.out = (__nv_bfloat16*)h_out;
   p.flags = w.flags;
   p.R = (int)R; p.C = (int)C; p.B = (int)B; p.G = (int)G;
-  p.has_top = top != nullptr;
+  p.has_top = top_src != nullptr;
   p.reverse = 0;
   p.err = w.err;
   p.drop_cell = drop_cell;
   p.spin_limit = spin_limit;
+  if (band) {
+    p.row0 = (int)band->row0;
+    p.epoch = band->epoch;
+    if (from_up) {
+      p.halo_in_flags = own.fwd_flags;
+      p.halo_in_ack = up.fwd_acks;
+      p.save_top = 1;
+    }
+    if (band->down_block) {
+      p.halo_out = down.fwd_halo;
+      p.halo_out_flags = down.fwd_flags;
+      p.halo_out_ack = own.fwd_acks;
+    }
+  }
   int ctas = 0;
-  st = H == 256 ? launch_sweep<256>(mWl, mWt, mIn, mTop, mAdd, mAdd, p, s, &ctas)
-                : launch_sweep<128>(mWl, mWt, mIn, mTop, mAdd, mAdd, p, s, &ctas);
+  st = H == 256 ? launch_sweep<256>(mWl, mWt, mIn, mTop, mAdd, mAdd, mSave, p, s, &ctas)
+                : launch_sweep<128>(mWl, mWt, mIn, mTop, mAdd, mAdd, mSave, p, s, &ctas);
   if (st != FLB_OK) return st;
   return check_timeout ? read_err(w.err, s, "grid_fwd") : FLB_OK;
 }
@@ -470,22 +623,45 @@ int grid_fwd(const void* x, int x_layout, const void* W_l, const void* W_t, cons
              const float* bias, const void* top, void* h_out, int64_t R, int64_t C, int64_t B,
              int64_t H, int64_t G, void* ws, size_t ws_bytes, int check_timeout, cudaStream_t s) {
   return grid_fwd_impl(x, x_layout, W_l, W_t, U, bias, top, h_out, R, C, B, H, G, ws, ws_bytes,
-                       check_timeout, s, -1, kFlagSpinLimit);
+                       check_timeout, s, -1, kFlagSpinLimit, nullptr, nullptr);
 }
 
-int grid_bwd(const void* x, int x_layout, const void* W_l, const void* W_t, const void* U,
-             const void* top, const void* h_out, const void* dh, float* dW_l, float* dW_t,
-             float* dU, float* dbias, void* dx, void* dtop, int64_t R, int64_t C, int64_t B,
-             int64_t H, int64_t G, void* ws, size_t ws_bytes, int check_timeout, cudaStream_t s) {
-  int st = check_grid_args(R, C, B, H, G);
+int grid_band_fwd(const void* x, int x_layout, const void* W_l, const void* W_t, const void* U,
+                  const float* bias, const void* top, void* h_out, void* saved_top, int64_t R,
+                  int64_t C, int64_t B, int64_t H, int64_t G, const flb_grid_band* band, void* ws,
+                  size_t ws_bytes, int check_timeout, cudaStream_t s) {
+  if (!band) return fail(FLB_ERR_SHAPE, "grid_band_fwd: null band");
+  return grid_fwd_impl(x, x_layout, W_l, W_t, U, bias, top, h_out, R, C, B, H, G, ws, ws_bytes,
+                       check_timeout, s, -1, kFlagSpinLimit, band, saved_top);
+}
+
+int grid_bwd_impl(const void* x, int x_layout, const void* W_l, const void* W_t, const void* U,
+                  const void* top, const void* h_out, const void* dh, float* dW_l, float* dW_t,
+                  float* dU, float* dbias, void* dx, void* dtop, int64_t R, int64_t C, int64_t B,
+                  int64_t H, int64_t G, void* ws, size_t ws_bytes, int check_timeout,
+                  cudaStream_t s, const flb_grid_band* band) {
+  int st = check_band(band, R, C, B, H, G);
   if (st != FLB_OK) return st;
   if (!W_l || !W_t || !h_out || !dh || !dW_l || !dW_t || !dbias || (U && (!x || !dU)))
     return fail(FLB_ERR_SHAPE, "grid_bwd: null pointer");
+  if (band && band->up_block && dtop)
+    return fail(FLB_ERR_SHAPE, "grid band bwd: dtop exists only for the first band");
+  BandBlock own{}, up{}, down{};
+  if (band) {
+    own = band_block(band->own_block, C, B, H);
+    if (band->up_block) up = band_block(band->up_block, C, B, H);
+    if (band->down_block) down = band_block(band->down_block, C, B, H);
+  }
+  const int64_t row0 = band ? band->row0 : 0;
   GridWs w = carve(ws, R, C, B, H, G, U != nullptr);
   if (!ws || ws_bytes < w.total) return fail(FLB_ERR_WORKSPACE, "grid_bwd: workspace smaller than flb_grid_workspace_bytes()");
   cudaError_t e = cudaMemsetAsync(w.err, 0, 256, s);
   if (e == cudaSuccess) e = cudaMemsetAsync(w.flags, 0, (size_t)R * C * 2 * sizeof(int), s);
   if (e == cudaSuccess) e = cudaMemsetAsync(dbias, 0, (size_t)G * H * sizeof(float), s);
+  if (e == cudaSuccess && G > 1 && G != R) {  // per-row weights of a band: other bands' rows are 0
+    e = cudaMemsetAsync(dW_l, 0, (size_t)G * H * H * sizeof(float), s);
+    if (e == cudaSuccess) e = cudaMemsetAsync(dW_t, 0, (size_t)G * H * H * sizeof(float), s);
+  }
   if (e != cudaSuccess) return check_cuda(e, "grid_bwd memset");
   // transposed weights: A operand rows are input features
   __nv_bfloat16* WlT = w.wt;
@@ -494,10 +670,13 @@ int grid_bwd(const void* x, int x_layout, const void* W_l, const void* W_t, cons
   transpose_weights_kernel<<<tg, tb, 0, s>>>((const __nv_bfloat16*)W_l, WlT, (int)G, (int)H);
   transpose_weights_kernel<<<tg, tb, 0, s>>>((const __nv_bfloat16*)W_t, WtT, (int)G, (int)H);
   count_launches(2);
-  CUtensorMap mWl, mWt, mIn;
+  CUtensorMap mWl, mWt, mIn, mBelow;
   if ((st = make_w_map(&mWl, WlT, G, H)) != FLB_OK) return st;
   if ((st = make_w_map(&mWt, WtT, G, H)) != FLB_OK) return st;
   if ((st = make_grid_map(&mIn, w.dz, R, C, B, H)) != FLB_OK) return st;
+  const bool from_down = band && band->down_block;
+  mBelow = mIn;
+  if (from_down && (st = make_top_map(&mBelow, own.bwd_halo, C, B, H)) != FLB_OK) return st;
   GridParams p{};
   p.out = w.dz;
   p.out2 = (U && x_layout == 0) ? w.dzx : nullptr;
@@ -506,17 +685,30 @@ int grid_bwd(const void* x, int x_layout, const void* W_l, const void* W_t, cons
   p.dbias = dbias;
   p.flags = w.flags;
   p.R = (int)R; p.C = (int)C; p.B = (int)B; p.G = (int)G;
-  p.has_top = 0;
+  p.has_top = from_down ? 1 : 0;  // the last row's row below: the halo from the next band
   p.reverse = 1;
   p.err = w.err;
   p.drop_cell = -1;
   p.spin_limit = kFlagSpinLimit;
+  if (band) {
+    p.row0 = (int)row0;
+    p.epoch = band->epoch;
+    if (from_down) {
+      p.halo_in_flags = own.bwd_flags;
+      p.halo_in_ack = down.bwd_acks;
+    }
+    if (band->up_block) {
+      p.halo_out = up.bwd_halo;
+      p.halo_out_flags = up.bwd_flags;
+      p.halo_out_ack = own.bwd_acks;
+    }
+  }
   int ctas = 0;
   CUtensorMap mH, mDH;
   if ((st = make_ep_map(&mH, h_out, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, 1, R, C, B, H)) != FLB_OK) return st;
   if ((st = make_ep_map(&mDH, dh, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, 1, R, C, B, H)) != FLB_OK) return st;
-  st = H == 256 ? launch_sweep<256>(mWl, mWt, mIn, mIn, mH, mDH, p, s, &ctas)
-                : launch_sweep<128>(mWl, mWt, mIn, mIn, mH, mDH, p, s, &ctas);
+  st = H == 256 ? launch_sweep<256>(mWl, mWt, mIn, mBelow, mH, mDH, mIn, p, s, &ctas)
+                : launch_sweep<128>(mWl, mWt, mIn, mBelow, mH, mDH, mIn, p, s, &ctas);
   if (st != FLB_OK) return st;
 
   cublasHandle_t hb;
@@ -528,7 +720,7 @@ int grid_bwd(const void* x, int x_layout, const void* W_l, const void* W_t, cons
   float* tmp = w.wtmp;
   // dW_l[r] = sum_{c>=1, b} dz[r][c][b][:]^T h[r][c-1][b][:]  (per row, K = (C-1) B)
   if (C > 1) {
-    float* dst = (G > 1) ? dW_l : tmp;
+    float* dst = (G > 1) ? dW_l + row0 * H * H : tmp;
     st = gemm_rm(hb, true, false, Hi, Hi, (int)((C - 1) * B), w.dz + cellHB, Hi, rowHB, hh, Hi,
                  rowHB, dst, Hi, (long long)H * H, (int)R, 0.f);
     if (st != FLB_OK) return st;
@@ -540,9 +732,10 @@ int grid_bwd(const void* x, int x_layout, const void* W_l, const void* W_t, cons
     e = cudaMemsetAsync(dW_l, 0, (size_t)G * H * H * sizeof(float), s);
     if (e != cudaSuccess) return check_cuda(e, "grid_bwd memset dW_l");
   }
-  // dW_t[r] = sum_{c, b} dz[r][c]^T h[r-1][c]  (r >= 1), and dz[0]^T top for r = 0
+  // dW_t[r] = sum_{c, b} dz[r][c]^T h[r-1][c]  (r >= 1), and dz[0]^T top for r = 0 (for a band
+  // below the first, top is the band above's last row as received in the forward)
   {
-    float* dst = (G > 1) ? dW_t : tmp;
+    float* dst = (G > 1) ? dW_t + row0 * H * H : tmp;
     if (R > 1) {
       st = gemm_rm(hb, true, false, Hi, Hi, (int)(C * B), w.dz + rowHB, Hi, rowHB, hh, Hi, rowHB,
                    dst + (long long)H * H, Hi, (long long)H * H, (int)(R - 1), 0.f);
@@ -579,6 +772,81 @@ int grid_bwd(const void* x, int x_layout, const void* W_l, const void* W_t, cons
   }
   return check_timeout ? read_err(w.err, s, "grid_bwd") : FLB_OK;
 }
+
+int grid_bwd(const void* x, int x_layout, const void* W_l, const void* W_t, const void* U,
+             const void* top, const void* h_out, const void* dh, float* dW_l, float* dW_t,
+             float* dU, float* dbias, void* dx, void* dtop, int64_t R, int64_t C, int64_t B,
+             int64_t H, int64_t G, void* ws, size_t ws_bytes, int check_timeout, cudaStream_t s) {
+  return grid_bwd_impl(x, x_layout, W_l, W_t, U, top, h_out, dh, dW_l, dW_t, dU, dbias, dx, dtop,
+                       R, C, B, H, G, ws, ws_bytes, check_timeout, s, nullptr);
+}
+
+int grid_band_bwd(const void* x, int x_layout, const void* W_l, const void* W_t, const void* U,
+                  const void* top, const void* h_out, const void* dh, float* dW_l, float* dW_t,
+                  float* dU, float* dbias, void* dx, void* dtop, int64_t R, int64_t C, int64_t B,
+                  int64_t H, int64_t G, const flb_grid_band* band, void* ws, size_t ws_bytes,
+                  int check_timeout, cudaStream_t s) {
+  if (!band) return fail(FLB_ERR_SHAPE, "grid_band_bwd: null band");
+  return grid_bwd_impl(x, x_layout, W_l, W_t, U, top, h_out, dh, dW_l, dW_t, dU, dbias, dx, dtop,
+                       R, C, B, H, G, ws, ws_bytes, check_timeout, s, band);
+}
+
+// ---- device memory shared with the other ranks of a node (CUDA IPC) ----------------------------
+// The exported handle is CUDA's 64-byte IPC handle followed by the owning GPU's 16-byte UUID.
+constexpr size_t kIpcCudaBytes = sizeof(cudaIpcMemHandle_t);
+static_assert(kIpcCudaBytes + 16 == FLB_IPC_HANDLE_BYTES, "handle layout");
+
+int current_uuid(unsigned char out[16]) {
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  cudaDeviceProp prop{};
+  if (e == cudaSuccess) e = cudaGetDeviceProperties(&prop, dev);
+  if (e != cudaSuccess) return check_cuda(e, "ipc: device properties");
+  memcpy(out, prop.uuid.bytes, 16);
+  return FLB_OK;
+}
+
+int ipc_alloc(size_t bytes, void** dev_ptr, void* handle) {
+  if (!dev_ptr || !handle || bytes == 0) return fail(FLB_ERR_SHAPE, "ipc_alloc: null pointer or zero size");
+  unsigned char* out = static_cast<unsigned char*>(handle);
+  int st = current_uuid(out + kIpcCudaBytes);
+  if (st != FLB_OK) return st;
+  void* p = nullptr;
+  cudaError_t e = cudaMalloc(&p, bytes);
+  if (e != cudaSuccess) return check_cuda(e, "ipc_alloc: cudaMalloc");
+  e = cudaMemset(p, 0, bytes);  // flags and epochs start at 0
+  if (e == cudaSuccess) e = cudaIpcGetMemHandle(reinterpret_cast<cudaIpcMemHandle_t*>(out), p);
+  if (e != cudaSuccess) {
+    cudaFree(p);
+    return check_cuda(e, "ipc_alloc: export");
+  }
+  *dev_ptr = p;
+  return FLB_OK;
+}
+
+int ipc_open(const void* handle, void** dev_ptr) {
+  if (!handle || !dev_ptr) return fail(FLB_ERR_SHAPE, "ipc_open: null pointer");
+  const unsigned char* in = static_cast<const unsigned char*>(handle);
+  // kernels on the two sides wait on each other: they must run on different GPUs
+  unsigned char mine[16];
+  int st = current_uuid(mine);
+  if (st != FLB_OK) return st;
+  if (memcmp(mine, in + kIpcCudaBytes, 16) == 0)
+    return fail(FLB_ERR_UNSUPPORTED, "ipc_open: the allocation lives on this GPU; row bands need one GPU per rank");
+  cudaIpcMemHandle_t h;
+  memcpy(&h, in, sizeof(h));
+  void* p = nullptr;
+  cudaError_t e = cudaIpcOpenMemHandle(&p, h, cudaIpcMemLazyEnablePeerAccess);
+  if (e != cudaSuccess) return check_cuda(e, "ipc_open: cudaIpcOpenMemHandle");
+  *dev_ptr = p;
+  return FLB_OK;
+}
+
+int ipc_close(void* dev_ptr) {
+  return check_cuda(cudaIpcCloseMemHandle(dev_ptr), "ipc_close");
+}
+
+int ipc_free(void* dev_ptr) { return check_cuda(cudaFree(dev_ptr), "ipc_free"); }
 
 // =============================================================================================
 // Allocation-free grid forward.
@@ -656,8 +924,8 @@ int grid_fwd_static(const void* W_l, const void* W_t, const float* bias, const v
   p.drop_cell = -1;
   p.spin_limit = kFlagSpinLimit;
   int ctas = 0;
-  st = H == 256 ? launch_sweep<256>(mWl, mWt, mIn, mTop, mIn, mIn, p, s, &ctas)
-                : launch_sweep<128>(mWl, mWt, mIn, mTop, mIn, mIn, p, s, &ctas);
+  st = H == 256 ? launch_sweep<256>(mWl, mWt, mIn, mTop, mIn, mIn, mIn, p, s, &ctas)
+                : launch_sweep<128>(mWl, mWt, mIn, mTop, mIn, mIn, mIn, p, s, &ctas);
   if (st != FLB_OK) return st;
   return check_timeout ? read_err(err, s, "grid_fwd_static") : FLB_OK;
 }

@@ -64,6 +64,16 @@ PROTOTYPES = {
                                            _vp]),
     "flb_grid_fwd_static": (_i32, [_vp, _vp, _vp, _vp, _vp, _i64, _i64, _i64, _i64, _i64, _i32,
                                    _vp]),
+    "flb_grid_band_block_bytes": (_sz, [_i64, _i64, _i64]),
+    "flb_ipc_alloc": (_i32, [_sz, ctypes.POINTER(ctypes.c_void_p), _vp]),
+    "flb_ipc_open": (_i32, [_vp, ctypes.POINTER(ctypes.c_void_p)]),
+    "flb_ipc_close": (_i32, [_vp]),
+    "flb_ipc_free": (_i32, [_vp]),
+    "flb_grid_band_fwd": (_i32, [_vp, _i32, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _i64, _i64, _i64,
+                                 _i64, _i64, _vp, _vp, _sz, _i32, _vp]),
+    "flb_grid_band_bwd": (_i32, [_vp, _i32, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp,
+                                 _vp, _vp, _i64, _i64, _i64, _i64, _i64, _vp, _vp, _sz, _i32,
+                                 _vp]),
     "flb_microbench": (_i32, [_i32, _vp, _dblp]),
     "flb_selftest_umma": (_i32, [_i32, _i32, _vp, _vp, _vp, _vp, _vp]),
 }
@@ -74,6 +84,16 @@ class BlockWeights(ctypes.Structure):
     _fields_ = [(n, ctypes.c_void_p) for n in (
         "ln_lat_w", "ln_lat_b", "ln_fdbk_w", "ln_fdbk_b", "w_prior_lat", "w_prior_fdbk",
         "w_gate_l", "b_gate_l", "w_gate_x", "b_gate_x", "w_qkv", "w_o", "v_a")]
+
+
+IPC_HANDLE_BYTES = 80  # FLB_IPC_HANDLE_BYTES
+
+
+class GridBand(ctypes.Structure):
+    """flb_grid_band of include/flb_b200.h."""
+    _fields_ = [("row0", ctypes.c_int64), ("rows_total", ctypes.c_int64),
+                ("own_block", ctypes.c_void_p), ("up_block", ctypes.c_void_p),
+                ("down_block", ctypes.c_void_p), ("epoch", ctypes.c_int)]
 
 
 class BlockGrads(ctypes.Structure):

@@ -148,7 +148,7 @@ int flb_wf_index_copy(const void* src, int src_dtype, const int64_t src_strides[
  * ((0,-1),port 1) (wavefront/wavefront_api.py:12-14), evaluated by one persistent kernel with
  * per-cell dependency flags instead of one host tick per anti-diagonal
  * (csrc/wavefront_backend.cpp:16-44).
- * Shapes: R rows, C cols, B batch, H hidden (H in {64,128,256}; B a multiple of 16, <= 64).
+ * Shapes: R rows, C cols, B batch, H hidden (H in {128,256}; B a multiple of 16, <= 64).
  * x: [B, R, C, H] bf16 (row-major, x_layout 0) or [R, C, B, H] (x_layout 1).
  * W_l, W_t: [G, H, H] bf16 (nn.Linear layout [out, in]); U: [H, H] bf16 or NULL; bias: [G, H] f32.
  * top: [C, B, H] bf16 or NULL. h_out: [R, C, B, H] bf16 (engine grid order: cell-major).
@@ -172,6 +172,68 @@ int flb_grid_bwd(const void* x, int x_layout, const void* W_l, const void* W_t, 
                  float* dW_l, float* dW_t, float* dU, float* dbias, void* dx, void* dtop,
                  int64_t R, int64_t C, int64_t B, int64_t H, int64_t G,
                  void* workspace, size_t workspace_bytes, int check_timeout, void* stream);
+
+/* ------------------------------------------------------------------------------------------
+ * Row bands: one grid layer split by rows across the GPUs of a node, one process per GPU.
+ * No counterpart in the reference, which runs on one device (training/trainer.py:31); this is
+ * the row-band partitioning of the grid layer (one exchange step per column).
+ * The band of rows row0 .. row0 + R - 1 (of rows_total) runs its persistent sweep while the
+ * neighbouring bands run theirs on other GPUs; the rows at the band edges exchange [C, B, H]
+ * bf16 halos through NVLink peer memory, column by column, inside the sweep kernels:
+ *   forward:  the last row of the band above stores h[row0 - 1][c] into this rank's receive
+ *             block and releases a per-column flag; this band's row 0 waits for the flag,
+ *             loads the halo from local memory by TMA, keeps a copy in saved_top, and
+ *             acknowledges, so that the next call may overwrite it;
+ *   backward: mirrored, with dz of the first row of the band below, consumed by this band's
+ *             last row through W_t[row0 + R] (all ranks hold all weights).
+ * Each rank allocates its receive block with flb_ipc_alloc(flb_grid_band_block_bytes(C,B,H)),
+ * shares the handle with its neighbours, and maps theirs with flb_ipc_open. Flags carry an
+ * epoch: every rank passes the same epoch to its k-th band forward (1, 2, 3, ...) and, counted
+ * separately, to its k-th band backward. Ranks must issue their band calls in the same order;
+ * a rank that never arrives makes its neighbours' bounded waits give up (FLB_ERR_TIMEOUT when
+ * check_timeout != 0). Weight gradients of a band are partial sums over its rows: all-reduce
+ * them across the ranks (their rows outside the band are zero with per-row weights).
+ * ------------------------------------------------------------------------------------------ */
+typedef struct flb_grid_band {
+  int64_t row0;             /* global index of this band's first row */
+  int64_t rows_total;       /* rows of the whole grid */
+  void* own_block;          /* this rank's receive block (flb_ipc_alloc) */
+  void* up_block;           /* the band above's block mapped here (flb_ipc_open); NULL iff row0 == 0 */
+  void* down_block;         /* the band below's block; NULL iff row0 + R == rows_total */
+  int epoch;                /* >= 1, see above */
+} flb_grid_band;
+
+#define FLB_IPC_HANDLE_BYTES 80
+size_t flb_grid_band_block_bytes(int64_t C, int64_t B, int64_t H);
+/* Device allocation on the current GPU, zero-filled, exportable to other processes: writes the
+ * pointer and a FLB_IPC_HANDLE_BYTES-byte handle (CUDA's IPC handle and the GPU's UUID). */
+int flb_ipc_alloc(size_t bytes, void** dev_ptr, void* handle);
+/* Maps another process's flb_ipc_alloc allocation (by its handle) into this process. Fails with
+ * FLB_ERR_UNSUPPORTED when it lives on the current GPU: band kernels wait on each other and
+ * must run on different GPUs. */
+int flb_ipc_open(const void* handle, void** dev_ptr);
+int flb_ipc_close(void* dev_ptr);
+int flb_ipc_free(void* dev_ptr);
+
+/* Forward of one band. Arguments as for flb_grid_fwd with R = the band's rows, x and h_out the
+ * band's rows, and G in {1, rows_total} (per-row weights indexed by global row). top: the grid's
+ * top row, only for the first band (else NULL). saved_top: [C, B, H] bf16, required below the
+ * first band: receives h[row0 - 1][.] for the backward. Workspace: flb_grid_workspace_bytes(R,
+ * C, B, H, G, has_U). */
+int flb_grid_band_fwd(const void* x, int x_layout, const void* W_l, const void* W_t,
+                      const void* U, const float* bias, const void* top, void* h_out,
+                      void* saved_top, int64_t R, int64_t C, int64_t B, int64_t H, int64_t G,
+                      const flb_grid_band* band, void* workspace, size_t workspace_bytes,
+                      int check_timeout, void* stream);
+/* Backward of one band. As flb_grid_bwd; top: the first band's top (or NULL), below it the
+ * saved_top of the forward; dtop only for the first band. dW_l, dW_t, dU, dbias: this band's
+ * partial sums (all-reduce across the ranks). */
+int flb_grid_band_bwd(const void* x, int x_layout, const void* W_l, const void* W_t,
+                      const void* U, const void* top, const void* h_out, const void* dh,
+                      float* dW_l, float* dW_t, float* dU, float* dbias, void* dx, void* dtop,
+                      int64_t R, int64_t C, int64_t B, int64_t H, int64_t G,
+                      const flb_grid_band* band, void* workspace, size_t workspace_bytes,
+                      int check_timeout, void* stream);
 
 /* Allocation-free form of flb_grid_fwd for callers that cannot allocate device memory when they
  * run the layer (a serving process with its memory carved into a fixed pool up front, code running
