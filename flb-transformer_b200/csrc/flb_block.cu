@@ -151,7 +151,7 @@ __global__ void blk_attn3_kernel(const bf16* __restrict__ qkv, const float* __re
   const int dh = D / H;
   const float* w = v_a + ((int64_t)(l0 + 2 * i) * H + h) * dh;
   const bf16* base = qkv + rb * 3 * (3 * D) + h * dh;  // token r row: base + r * 3D
-  float s[3][3];
+  float s[3][3], vv[4][3];
 #pragma unroll
   for (int a = 0; a < 3; ++a)
 #pragma unroll
@@ -165,6 +165,7 @@ __global__ void blk_attn3_kernel(const bf16* __restrict__ qkv, const float* __re
     for (int r = 0; r < 3; ++r) {
       q[r] = __bfloat162float(base[r * 3 * D + d]);
       k[r] = __bfloat162float(base[r * 3 * D + D + d]);
+      vv[kk][r] = __bfloat162float(base[r * 3 * D + 2 * D + d]);  // V with Q, K: one round trip
     }
     const float wd = w[d];
 #pragma unroll
@@ -196,9 +197,7 @@ __global__ void blk_attn3_kernel(const bf16* __restrict__ qkv, const float* __re
   for (int kk = 0; kk < 4; ++kk) {
     const int d = lane + 32 * kk;
     if (d >= dh) break;
-    float v[3];
-#pragma unroll
-    for (int r = 0; r < 3; ++r) v[r] = __bfloat162float(base[r * 3 * D + 2 * D + d]);
+    const float* v = vv[kk];
 #pragma unroll
     for (int a = 0; a < 3; ++a)
       out[a * D + d] = __float2bfloat16_rn(p[a][0] * v[0] + p[a][1] * v[1] + p[a][2] * v[2]);
@@ -242,6 +241,7 @@ constexpr size_t kBlkBlasWs = 32u << 20;
 struct BlockWs {
   bf16 *ln, *lat, *tok, *z, *qkv, *att, *o;
   void* blas;
+  void* blas_side;
 };
 
 size_t block_ws_layout(int64_t nmax, int64_t B, int64_t D, BlockWs* w, void* base) {
@@ -255,7 +255,7 @@ size_t block_ws_layout(int64_t nmax, int64_t B, int64_t D, BlockWs* w, void* bas
   };
   const size_t o_ln = take(2 * rowb), o_lat = take(rowb), o_tok = take(3 * rowb), o_z = take(rowb),
                o_qkv = take(9 * rowb), o_att = take(3 * rowb), o_o = take(3 * rowb),
-               o_blas = take(kBlkBlasWs);
+               o_blas = take(kBlkBlasWs), o_blas_side = take(kBlkBlasWs);
   if (w && base) {
     uint8_t* p = reinterpret_cast<uint8_t*>(base);
     w->ln = (bf16*)(p + o_ln);
@@ -266,6 +266,7 @@ size_t block_ws_layout(int64_t nmax, int64_t B, int64_t D, BlockWs* w, void* bas
     w->att = (bf16*)(p + o_att);
     w->o = (bf16*)(p + o_o);
     w->blas = p + o_blas;
+    w->blas_side = p + o_blas_side;
   }
   return off;
 }
@@ -283,6 +284,39 @@ size_t block_grid_workspace_bytes(int64_t L, int64_t S, int64_t B, int64_t D) {
 
 namespace {
 
+// A per-device side stream and fork/join events: GEMMs that are off a tick's critical chain
+// (the lateral prior of the forward, the weight-gradient GEMMs of the backward) run on it while
+// the chain continues on the caller's stream. Created on the first call on a device and kept
+// until exit.
+struct SideStream {
+  cudaStream_t s = nullptr;
+  cudaEvent_t fork[5] = {}, join = nullptr, fwd_fork = nullptr, fwd_join = nullptr;
+};
+
+int side_stream(SideStream** out) {
+  static std::mutex mu;
+  static SideStream per_dev[64];
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (dev < 0 || dev >= 64) return fail(FLB_ERR_UNSUPPORTED, "block_grid: device index >= 64");
+  std::lock_guard<std::mutex> lock(mu);
+  SideStream& ss = per_dev[dev];
+  if (ss.s == nullptr) {
+    cudaError_t e = cudaStreamCreateWithFlags(&ss.s, cudaStreamNonBlocking);
+    for (int i = 0; e == cudaSuccess && i < 5; ++i)
+      e = cudaEventCreateWithFlags(&ss.fork[i], cudaEventDisableTiming);
+    if (e == cudaSuccess) e = cudaEventCreateWithFlags(&ss.join, cudaEventDisableTiming);
+    if (e == cudaSuccess) e = cudaEventCreateWithFlags(&ss.fwd_fork, cudaEventDisableTiming);
+    if (e == cudaSuccess) e = cudaEventCreateWithFlags(&ss.fwd_join, cudaEventDisableTiming);
+    if (e != cudaSuccess) {
+      ss.s = nullptr;
+      return check_cuda(e, "block_grid side stream");
+    }
+  }
+  *out = &ss;
+  return FLB_OK;
+}
+
 // Forward buffers of one tick (bf16): LayerNorm outputs [2][n][B][D], lat_prior [n][B][D],
 // tokens [n][B][3][D] (x', lat', fdbk_prior), gate pre-activations [n][B][D] (the forward reuses
 // one buffer for both), q|k|v [n][3B][3D], attention output [n][3B][D].
@@ -291,23 +325,35 @@ struct TickBufs {
 };
 
 // stages 1-6 of a tick (everything up to the attention output)
-int tick_forward(cublasHandle_t hb, const flb_block_weights* W, const bf16* xb, const bf16* g,
-                 int64_t port_stride, const TickBufs& b, int T, int l0, int n, int L, int S, int B,
-                 int D, int H, float eps, cudaStream_t s) {
+// the side stream and its cuBLAS handle for GEMMs off the critical chain of a tick
+struct Side {
+  SideStream* ss;
+  cublasHandle_t h;
+};
+
+int tick_forward(cublasHandle_t hb, const Side& side, const flb_block_weights* W, const bf16* xb,
+                 const bf16* g, int64_t port_stride, const TickBufs& b, int T, int l0, int n,
+                 int L, int S, int B, int D, int H, float eps, cudaStream_t s) {
   const long long DD = (long long)D * D, BD = (long long)B * D;
   int st;
   blk_ln_kernel<<<(2 * n * B + 7) / 8, 256, 0, s>>>(g + port_stride, g + 2 * port_stride,
                                                     W->ln_lat_w, W->ln_lat_b, W->ln_fdbk_w,
                                                     W->ln_fdbk_b, b.ln, T, l0, n, L, S, B, D, eps);
+  cudaError_t e = cudaEventRecord(side.ss->fwd_fork, s);
+  if (e == cudaSuccess) e = cudaStreamWaitEvent(side.ss->s, side.ss->fwd_fork, 0);
+  if (e != cudaSuccess) return check_cuda(e, "block_grid tick fork");
   const bf16* Wpl = reinterpret_cast<const bf16*>(W->w_prior_lat) + (int64_t)l0 * DD;
   const bf16* Wpf = reinterpret_cast<const bf16*>(W->w_prior_fdbk) + (int64_t)l0 * DD;
   const bf16* Wgl = reinterpret_cast<const bf16*>(W->w_gate_l) + (int64_t)l0 * DD;
   const bf16* Wgx = reinterpret_cast<const bf16*>(W->w_gate_x) + (int64_t)l0 * DD;
   const bf16* Wqkv = reinterpret_cast<const bf16*>(W->w_qkv) + (int64_t)l0 * 3 * DD;
-  // priors: lat_prior -> b.lat; fdbk_prior -> token slot 2 (row pitch 3D)
-  if ((st = gemm_rm(hb, false, true, B, D, D, b.ln, D, BD, Wpl, D, 2 * DD, b.lat, D, BD, n, 0.f,
+  // priors: lat_prior -> b.lat (side stream: first needed by the lateral gate kernel);
+  // fdbk_prior -> token slot 2 (row pitch 3D)
+  if ((st = gemm_rm(side.h, false, true, B, D, D, b.ln, D, BD, Wpl, D, 2 * DD, b.lat, D, BD, n, 0.f,
                     CUDA_R_16BF)) != FLB_OK)
     return st;
+  e = cudaEventRecord(side.ss->fwd_join, side.ss->s);
+  if (e != cudaSuccess) return check_cuda(e, "block_grid tick join");
   if ((st = gemm_rm(hb, false, true, B, D, D, b.ln + n * BD, D, BD, Wpf, D, 2 * DD, b.tok + 2 * D,
                     3 * D, 3 * BD, n, 0.f, CUDA_R_16BF)) != FLB_OK)
     return st;
@@ -315,6 +361,8 @@ int tick_forward(cublasHandle_t hb, const flb_block_weights* W, const bf16* xb, 
   if ((st = gemm_rm(hb, false, true, B, D, D, b.tok + 2 * D, 3 * D, 3 * BD, Wgl, D, 2 * DD, b.zl, D,
                     BD, n, 0.f, CUDA_R_16BF)) != FLB_OK)
     return st;
+  e = cudaStreamWaitEvent(s, side.ss->fwd_join, 0);
+  if (e != cudaSuccess) return check_cuda(e, "block_grid tick join");
   const dim3 ew_grid((unsigned)((D / 2 + 127) / 128), (unsigned)(n * B));
   blk_gate_kernel<<<ew_grid, 128, 0, s>>>(b.zl, W->b_gate_l, b.lat, g, xb, 0, b.tok + D, T, l0, S,
                                           B, D);
@@ -342,6 +390,9 @@ int block_grid_fwd(const flb_block_weights* W, const void* x, void* grids, int64
   cublasHandle_t hb;
   int st = blas(s, w.blas, kBlkBlasWs, &hb);
   if (st != FLB_OK) return st;
+  Side side{};
+  if ((st = side_stream(&side.ss)) != FLB_OK) return st;
+  if ((st = blas(side.ss->s, w.blas_side, kBlkBlasWs, &side.h, 1)) != FLB_OK) return st;
   const bf16* xb = reinterpret_cast<const bf16*>(x);
   bf16* g = reinterpret_cast<bf16*>(grids);
   const int64_t port_stride = (L * S + L) * B * D;  // the engine's grids keep L dock rows
@@ -354,8 +405,8 @@ int block_grid_fwd(const flb_block_weights* W, const void* x, void* grids, int64
     const Tick tk = tick_of(T, Li, Si);
     const int n = tk.n, l0 = tk.l0;
     if (n == 0) continue;
-    if ((st = tick_forward(hb, W, xb, g, port_stride, tb, T, l0, n, Li, Si, Bi, Di, Hi, eps, s)) !=
-        FLB_OK)
+    if ((st = tick_forward(hb, side, W, xb, g, port_stride, tb, T, l0, n, Li, Si, Bi, Di, Hi, eps,
+                           s)) != FLB_OK)
       return st;
     const bf16* Wo = reinterpret_cast<const bf16*>(W->w_o) + (int64_t)l0 * DD;
     if ((st = gemm_rm(hb, false, true, 3 * Bi, Di, Di, w.att, Di, 3 * BD, Wo, Di, 2 * DD, w.o, Di,
@@ -715,36 +766,6 @@ struct BlockBwdWs {
   void* blas_side;
 };
 
-// A per-device side stream and fork/join events of the backward: the weight-gradient GEMMs of
-// a tick run on it while the input-gradient chain continues on the caller's stream. Created on
-// the first backward call on a device and kept until exit.
-struct SideStream {
-  cudaStream_t s = nullptr;
-  cudaEvent_t fork[5] = {}, join = nullptr;
-};
-
-int side_stream(SideStream** out) {
-  static std::mutex mu;
-  static SideStream per_dev[64];
-  int dev = 0;
-  cudaGetDevice(&dev);
-  if (dev < 0 || dev >= 64) return fail(FLB_ERR_UNSUPPORTED, "block_grid_bwd: device index >= 64");
-  std::lock_guard<std::mutex> lock(mu);
-  SideStream& ss = per_dev[dev];
-  if (ss.s == nullptr) {
-    cudaError_t e = cudaStreamCreateWithFlags(&ss.s, cudaStreamNonBlocking);
-    for (int i = 0; e == cudaSuccess && i < 5; ++i)
-      e = cudaEventCreateWithFlags(&ss.fork[i], cudaEventDisableTiming);
-    if (e == cudaSuccess) e = cudaEventCreateWithFlags(&ss.join, cudaEventDisableTiming);
-    if (e != cudaSuccess) {
-      ss.s = nullptr;
-      return check_cuda(e, "block_grid_bwd side stream");
-    }
-  }
-  *out = &ss;
-  return FLB_OK;
-}
-
 size_t block_bwd_ws_layout(int64_t L, int64_t S, int64_t B, int64_t D, BlockBwdWs* w, void* base) {
   const int64_t nmax = max_cells_per_tick(L, S);
   auto al = [](size_t x) { return (x + 255) & ~(size_t)255; };
@@ -833,8 +854,8 @@ int block_grid_bwd(const flb_block_weights* W, const void* x, const void* grids,
     const Tick tk = tick_of(T, Li, Si);
     const int n = tk.n, l0 = tk.l0;
     if (n == 0) continue;
-    if ((st = tick_forward(hb, W, xb, g, port_stride, w.f, T, l0, n, Li, Si, Bi, Di, Hi, eps, s)) !=
-        FLB_OK)
+    if ((st = tick_forward(hb, Side{side, hs}, W, xb, g, port_stride, w.f, T, l0, n, Li, Si, Bi,
+                           Di, Hi, eps, s)) != FLB_OK)
       return st;
     const dim3 ew_grid((unsigned)((D / 2 + 127) / 128), (unsigned)(n * Bi));
     const dim3 cell_grid((unsigned)((D / 2 + 127) / 128), (unsigned)n);
