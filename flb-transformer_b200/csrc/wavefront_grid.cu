@@ -9,16 +9,19 @@
 // here a single launch advances the whole grid:
 //   * one CTA per (grid row, 128 output features); rows are co-resident (grid <= the device's
 //     resident-CTA capacity) and a CTA walks its row left to right;
-//   * a cell starts when per-cell dependency flags in global memory say that both 128-feature
-//     halves of its left and top neighbours are stored (ld.acquire.gpu spin with an iteration
-//     bound; on expiry an error word is set and the kernel carries on, so it never hangs);
+//   * per-cell dependency flags in global memory say when both 128-feature halves of a cell are
+//     stored; one thread polls the left and top neighbours' flags together (ld.acquire.gpu, with
+//     an iteration bound: on expiry an error word is set and the kernel carries on, so it never
+//     hangs) and starts each neighbour's load the moment its flags are set;
 //   * the neighbours' h ([batch x hidden] bf16 each) arrive by TMA straight from the output grid;
 //     coordinates outside the grid (c-1 < 0, r-1 < 0) are zero-filled by the TMA unit, which is
 //     exactly the zero boundary;
 //   * the cell GEMM, z^T[128 x B] = [W_l | W_t][128 x 2H] . [h_left ; h_top][2H x B], runs on
-//     tcgen05 with the CTA's weight slice resident in shared memory and the accumulator in TMEM;
-//   * the epilogue adds bias and the hoisted x U^T, applies tanh, stores h (bf16) into the output
-//     grid, fences, and releases the cell's flag.
+//     tcgen05 with the CTA's weight slice resident in shared memory and the accumulator in TMEM,
+//     the W_l half as soon as h_left has landed;
+//   * the epilogue adds bias and the hoisted x U^T (prefetched one cell ahead), applies tanh and
+//     stores h (bf16) into the output grid; after a CTA barrier one thread releases the cell's
+//     flag (st.release, which is cumulative over the stores the barrier ordered before it).
 // The backward is the mirrored reverse sweep producing dz = dh_total * (1 - h^2) with
 // dh_total = dh_ext + W_l^T dz[r][c+1] + W_t^T dz[r+1][c]; weight gradients are then plain
 // cuBLAS GEMMs over dz and the saved h (and x), and db is reduced inside the sweep.
@@ -47,14 +50,6 @@ __device__ __forceinline__ int ld_acquire(const int* p) {
 }
 __device__ __forceinline__ void st_release(int* p, int v) {
   asm volatile("st.release.gpu.global.b32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
-}
-// Bounded spin until *p == want. Returns false if it gave up.
-__device__ __forceinline__ bool wait_flag(const int* p, int want, uint32_t limit) {
-  for (uint32_t i = 0; i < limit; ++i) {
-    if (ld_acquire(p) == want) return true;
-    if (i > 64) __nanosleep(64);
-  }
-  return false;
 }
 // System scope: flags written by another GPU over NVLink, or written into another GPU's memory.
 __device__ __forceinline__ int ld_acquire_sys(const int* p) {
@@ -103,12 +98,19 @@ struct GridCfg {
   static constexpr int OFF_IN = KATOMS * W_ATOM;      // B operand atoms follow
   // epilogue operands of a cell, staged by TMA: [B][128] fp32 (add) or 2 x [B][128] bf16 (h, dh)
   __host__ __device__ static int off_ep(int B) { return OFF_IN + KATOMS * B * 128; }
-  __host__ __device__ static int smem(int B) { return off_ep(B) + B * 128 * 4 + 1024; }
+  // one epilogue stage: [B][128] fp32, or [B][128] bf16 h and dh
+  __host__ __device__ static int ep_bytes(int B) { return B * 128 * 4; }
+  __host__ __device__ static int smem(int B, int stages) {
+    return off_ep(B) + stages * ep_bytes(B) + 1024;
+  }
+  static constexpr int kMaxDynSmem = 226 * 1024;  // under the 227 KB per-block limit with static
+  // two stages (the next cell's operands prefetched during this cell) when they fit
+  static int ep_stages(int B) { return smem(B, 2) <= kMaxDynSmem ? 2 : 1; }
 };
 
 struct GridParams {
-  const float* add;      // hoisted x U^T (fp32) or null
-  int add_layout;        // 0: [B, R, C, H] rows, 1: [R, C, B, H] rows
+  const float* add;      // hoisted x U^T (fp32, [R, C, B, H]) or null
+  int ep_stages;         // epilogue operand stages in shared memory (1 or 2)
   const float* bias;     // [G, H] (forward) ; unused in backward
   __nv_bfloat16* out;    // forward: h grid [R, C, B, H]; backward: dz grid [R, C, B, H]
   __nv_bfloat16* out2;   // backward: dz in x layout [B, R, C, H] or null
@@ -150,7 +152,7 @@ grid_sweep_kernel(const __grid_constant__ CUtensorMap tmWa, const __grid_constan
   constexpr int NH = H / 128;  // feature halves (CTAs per row)
   extern __shared__ uint8_t smem_raw[];
   uint8_t* sm = (uint8_t*)(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
-  __shared__ __align__(8) uint64_t bar_w, bar_in, bar_mma, bar_ep;
+  __shared__ __align__(8) uint64_t bar_w, bar_l, bar_t, bar_mma, bar_ep[2];
   __shared__ uint32_t tmem_slot;
 
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
@@ -162,9 +164,11 @@ grid_sweep_kernel(const __grid_constant__ CUtensorMap tmWa, const __grid_constan
 
   if (tid == 0) {
     mbar_init(&bar_w, 1);
-    mbar_init(&bar_in, 1);
+    mbar_init(&bar_l, 1);  // same-row input landed
+    mbar_init(&bar_t, 1);  // other-row input landed
     mbar_init(&bar_mma, 1);
-    mbar_init(&bar_ep, 1);
+    mbar_init(&bar_ep[0], 1);
+    mbar_init(&bar_ep[1], 1);
     fence_mbar_init();
     tma_prefetch_desc(&tmWa);
     tma_prefetch_desc(&tmWb);
@@ -181,7 +185,9 @@ grid_sweep_kernel(const __grid_constant__ CUtensorMap tmWa, const __grid_constan
   const uint32_t tmem = tmem_slot;
   const uint32_t idesc = make_idesc_f16(128, B, 1, 0, 0);
   const int f = half * 128 + warp * 32 + lane;  // this thread's output feature
-  uint32_t n_wload = 0, n_cell = 0, n_ep = 0;
+  uint32_t n_wload = 0, n_cell = 0;
+  uint32_t ep_issued = 0, ep_used = 0;  // epilogue operand tiles issued / consumed (stage = k % S)
+  const int S = p.ep_stages;
   float db_acc = 0.f;
   int db_group = -1;
 
@@ -218,64 +224,113 @@ grid_sweep_kernel(const __grid_constant__ CUtensorMap tmWa, const __grid_constan
       const int r_nb = p.reverse ? r + 1 : r - 1;   // other-row neighbour
       const bool stage_add = !p.reverse && p.add != nullptr;
       if (tid == 0 && (p.reverse || stage_add)) {
-        // epilogue operands do not depend on the recurrence: fetch them before waiting on it
-        uint8_t* sE = sm + Cfg::off_ep(B);
-        if (p.reverse) {
-          mbar_arrive_expect_tx(&bar_ep, 2 * B * 128 * 2);
-          tma_load_4d(sE, &tmE1, &bar_ep, half * 128, 0, c, r);                 // h
-          tma_load_4d(sE + B * 128 * 2, &tmE2, &bar_ep, half * 128, 0, c, r);   // dh
-        } else {
-          mbar_arrive_expect_tx(&bar_ep, B * 128 * 4);
-          if (p.add_layout == 0)
-            tma_load_4d(sE, &tmE1, &bar_ep, half * 128, c, r, 0);  // add rows (b, r, c)
-          else
-            tma_load_4d(sE, &tmE1, &bar_ep, half * 128, 0, c, r);  // add rows (r, c, b)
-        }
+        // Epilogue operands do not depend on the recurrence: fetch them before waiting on it,
+        // with two stages one cell ahead (a row's first cell fetches its own too).
+        auto issue_ep = [&](int cj) {
+          const int cc = p.reverse ? (C - 1 - cj) : cj;
+          const int st = (int)(ep_issued % (uint32_t)S);
+          uint8_t* sE = sm + Cfg::off_ep(B) + st * Cfg::ep_bytes(B);
+          if (p.reverse) {
+            mbar_arrive_expect_tx(&bar_ep[st], 2 * B * 128 * 2);
+            tma_load_4d(sE, &tmE1, &bar_ep[st], half * 128, 0, cc, r);                 // h
+            tma_load_4d(sE + B * 128 * 2, &tmE2, &bar_ep[st], half * 128, 0, cc, r);   // dh
+          } else {
+            mbar_arrive_expect_tx(&bar_ep[st], B * 128 * 4);
+            tma_load_4d(sE, &tmE1, &bar_ep[st], half * 128, 0, cc, r);  // add rows (r, c, b)
+          }
+          ++ep_issued;
+        };
+        if (S == 1 || ci == 0) issue_ep(ci);
+        if (S == 2 && ci + 1 < C) issue_ep(ci + 1);
       }
       if (tid == 0) {
-        bool ok = true;
-        if (c_nb >= 0 && c_nb < C)
-          for (int hh = 0; hh < NH; ++hh) ok &= wait_flag(p.flags + ((int64_t)r * C + c_nb) * 2 + hh, 1, p.spin_limit);
-        if (r_nb >= 0 && r_nb < R)
-          for (int hh = 0; hh < NH; ++hh) ok &= wait_flag(p.flags + ((int64_t)r_nb * C + c) * 2 + hh, 1, p.spin_limit);
-        if (!ok) atomicExch(p.err, 2);
-        bool ok_halo = true;
-        if (halo_in)  // the neighbour band's edge row, both feature halves, this epoch
-          for (int hh = 0; hh < NH; ++hh)
-            ok_halo &= wait_flag_sys(p.halo_in_flags + c * 2 + hh, p.epoch, p.spin_limit);
-        if (halo_out)  // the neighbour has loaded the previous epoch's column c: it may be rewritten
-          for (int hh = 0; hh < NH; ++hh)
-            ok_halo &= wait_flag_sys(p.halo_out_ack + c * 2 + hh, p.epoch - 1, p.spin_limit);
-        if (!ok_halo) atomicExch(p.err, 6);
-        fence_async_global();  // order the acquired generic stores before the TMA reads
         uint8_t* sIn = sm + Cfg::OFF_IN;
-        mbar_arrive_expect_tx(&bar_in, Cfg::KATOMS * B * 128);
+        constexpr int kAtoms = H / 64;
+        const uint32_t part = (uint32_t)kAtoms * B * 128;  // bytes of one input tile
+        // Each input is loaded as soon as its producer's flags (both feature halves) are set;
+        // out-of-grid neighbours are zero-filled by TMA (the zero boundary) without a wait.
+        auto issue_left = [&]() {
+          fence_async_global();  // order the acquired generic stores before the TMA reads
+          mbar_arrive_expect_tx(&bar_l, part);
 #pragma unroll
-        for (int a = 0; a < H / 64; ++a) {
-          // out-of-grid coordinates are zero-filled: the zero boundary
-          tma_load_4d(sIn + a * B * 128, &tmIn, &bar_in, a * 64, 0, c_nb, r);
-          if (in_edge && p.has_top)
-            tma_load_3d(sIn + (H / 64 + a) * B * 128, &tmTop, &bar_in, a * 64, 0, c);
-          else
-            tma_load_4d(sIn + (H / 64 + a) * B * 128, &tmIn, &bar_in, a * 64, 0, c, r_nb);
+          for (int a = 0; a < kAtoms; ++a)
+            tma_load_4d(sIn + a * B * 128, &tmIn, &bar_l, a * 64, 0, c_nb, r);
+        };
+        auto issue_top = [&]() {
+          fence_async_global();
+          mbar_arrive_expect_tx(&bar_t, part);
+#pragma unroll
+          for (int a = 0; a < kAtoms; ++a) {
+            if (in_edge && p.has_top)
+              tma_load_3d(sIn + (kAtoms + a) * B * 128, &tmTop, &bar_t, a * 64, 0, c);
+            else
+              tma_load_4d(sIn + (kAtoms + a) * B * 128, &tmIn, &bar_t, a * 64, 0, c, r_nb);
+          }
+        };
+        const bool left_dep = c_nb >= 0 && c_nb < C;
+        const bool top_dep = r_nb >= 0 && r_nb < R;
+        const int* lflag = p.flags + ((int64_t)r * C + (left_dep ? c_nb : 0)) * 2;
+        const int* tflag = p.flags + ((int64_t)(top_dep ? r_nb : 0) * C + c) * 2;
+        // the other-row input of a band's edge row is the halo of the neighbouring band
+        const int* hflag = halo_in ? p.halo_in_flags + c * 2 : nullptr;
+        bool lready = !left_dep, tready = !top_dep && !halo_in;
+        if (lready) issue_left();
+        if (tready) issue_top();
+        for (uint32_t i = 0; !(lready && tready) && i < p.spin_limit; ++i) {
+          if (!lready) {
+            bool set = true;
+            for (int hh = 0; hh < NH; ++hh) set &= ld_acquire(lflag + hh) == 1;
+            if (set) {
+              lready = true;
+              issue_left();
+            }
+          }
+          if (!tready) {
+            bool set = true;
+            for (int hh = 0; hh < NH; ++hh)
+              set &= halo_in ? ld_acquire_sys(hflag + hh) == p.epoch : ld_acquire(tflag + hh) == 1;
+            if (set) {
+              tready = true;
+              issue_top();
+            }
+          }
+          if (i > 64) __nanosleep(64);
         }
-        if (!mbar_wait(&bar_in, n_cell & 1u, kWaitLimit)) atomicExch(p.err, 3);
+        if (!(lready && tready)) {  // gave up: record it, keep the barrier phases in step
+          atomicExch(p.err, halo_in && !tready ? 6 : 2);
+          if (!lready) issue_left();
+          if (!tready) issue_top();
+        }
+        const uint32_t wa = smem_u32(sm + Cfg::OFF_W), ia = smem_u32(sIn);
+        auto mma_range = [&](int k0, int k1) {
+#pragma unroll
+          for (int kk = k0; kk < k1; ++kk) {
+            const uint64_t adesc = make_smem_desc(wa + (kk >> 2) * Cfg::W_ATOM + (kk & 3) * 32, 16, 1024, kSwizzle128B);
+            const uint64_t bdesc = make_smem_desc(ia + (kk >> 2) * B * 128 + (kk & 3) * 32, 16, 1024, kSwizzle128B);
+            umma_f16(tmem, adesc, bdesc, idesc, kk > 0 ? 1u : 0u);
+          }
+        };
+        // same-row half of K first: it runs while the other-row tile may still be in flight
+        if (!mbar_wait(&bar_l, n_cell & 1u, kWaitLimit)) atomicExch(p.err, 3);
+        tc_fence_after();
+        mma_range(0, H / 16);
+        if (!mbar_wait(&bar_t, n_cell & 1u, kWaitLimit)) atomicExch(p.err, 3);
         if (halo_in) {
           if (p.save_top) {  // this CTA's feature half of the received rows, back out of shared memory
 #pragma unroll
             for (int a = half * 2; a < half * 2 + 2; ++a)
-              tma_store_3d(&tmSave, sIn + (H / 64 + a) * B * 128, a * 64, 0, c);
+              tma_store_3d(&tmSave, sIn + (kAtoms + a) * B * 128, a * 64, 0, c);
             bulk_commit();
           }
           st_release_sys(p.halo_in_ack + c * 2 + half, p.epoch);
         }
         tc_fence_after();
-        const uint32_t wa = smem_u32(sm + Cfg::OFF_W), ia = smem_u32(sIn);
-#pragma unroll
-        for (int kk = 0; kk < 2 * H / 16; ++kk) {
-          const uint64_t adesc = make_smem_desc(wa + (kk >> 2) * Cfg::W_ATOM + (kk & 3) * 32, 16, 1024, kSwizzle128B);
-          const uint64_t bdesc = make_smem_desc(ia + (kk >> 2) * B * 128 + (kk & 3) * 32, 16, 1024, kSwizzle128B);
-          umma_f16(tmem, adesc, bdesc, idesc, kk > 0 ? 1u : 0u);
+        mma_range(H / 16, 2 * H / 16);
+        if (halo_out) {  // the neighbour has loaded the previous epoch's column c: it may be rewritten
+          bool ok_ack = true;
+          for (int hh = 0; hh < NH; ++hh)
+            ok_ack &= wait_flag_sys(p.halo_out_ack + c * 2 + hh, p.epoch - 1, p.spin_limit);
+          if (!ok_ack) atomicExch(p.err, 6);
         }
         umma_commit(&bar_mma);
         // the next cell's loads overwrite these rows: the store must have read them by then
@@ -292,11 +347,12 @@ grid_sweep_kernel(const __grid_constant__ CUtensorMap tmWa, const __grid_constan
 
       // ---- epilogue: this thread owns feature f for every batch element --------------------
       const int64_t cell = (int64_t)r * C + c;
-      const uint8_t* sE = sm + Cfg::off_ep(B);
+      const uint8_t* sE = sm + Cfg::off_ep(B) + (int)(ep_used % (uint32_t)S) * Cfg::ep_bytes(B);
       const int fl = warp * 32 + lane;  // feature within this CTA's half
       if (p.reverse || stage_add) {
-        if (!mbar_wait(&bar_ep, n_ep & 1u, kWaitLimit)) atomicExch(p.err, 5);
-        ++n_ep;
+        if (!mbar_wait(&bar_ep[ep_used % (uint32_t)S], (ep_used / (uint32_t)S) & 1u, kWaitLimit))
+          atomicExch(p.err, 5);
+        ++ep_used;
       }
       const float bias_f = p.reverse ? 0.f : p.bias[(int64_t)g * H + f];
       for (int cb = 0; cb < B; cb += 32) {
@@ -329,15 +385,16 @@ grid_sweep_kernel(const __grid_constant__ CUtensorMap tmWa, const __grid_constan
           }
         }
       }
-      if (halo_out)
-        __threadfence_system();  // the halo stores reach the other GPU before its flag
-      else
-        __threadfence();
       tc_fence_before();
       __syncthreads();
+      // The barrier orders every thread's stores of this cell before thread 0's release, and a
+      // release is cumulative: consumers that acquire the flag see all of them.
       if (tid == 0 && cell != p.drop_cell) {
         st_release(p.flags + cell * 2 + half, 1);
-        if (halo_out) st_release_sys(p.halo_out_flags + c * 2 + half, p.epoch);
+        if (halo_out) {  // the halo stores reach the other GPU before its flag
+          __threadfence_system();
+          st_release_sys(p.halo_out_flags + c * 2 + half, p.epoch);
+        }
       }
     }
   }
@@ -429,19 +486,12 @@ int make_top_map(CUtensorMap* m, const void* T, int64_t C, int64_t B, int64_t H)
                    CU_TENSOR_MAP_SWIZZLE_128B);
 }
 
-// Epilogue staging maps: a cell's [B x 128] slice of a [R, C, B, H] grid (bf16 or fp32), or of a
-// [B, R, C, H] array (x layout 0, fp32).
-int make_ep_map(CUtensorMap* m, const void* X, CUtensorMapDataType dt, int esz, int layout,
-                int64_t R, int64_t C, int64_t B, int64_t H) {
-  if (layout == 1) {
-    const uint64_t dims[4] = {(uint64_t)H, (uint64_t)B, (uint64_t)C, (uint64_t)R};
-    const uint64_t strides[3] = {(uint64_t)H * esz, (uint64_t)(B * H * esz), (uint64_t)(C * B * H * esz)};
-    const uint32_t box[4] = {128, (uint32_t)B, 1, 1};
-    return make_tmap(m, X, dt, 4, dims, strides, box, CU_TENSOR_MAP_SWIZZLE_NONE);
-  }
-  const uint64_t dims[4] = {(uint64_t)H, (uint64_t)C, (uint64_t)R, (uint64_t)B};
-  const uint64_t strides[3] = {(uint64_t)H * esz, (uint64_t)(C * H * esz), (uint64_t)(R * C * H * esz)};
-  const uint32_t box[4] = {128, 1, 1, (uint32_t)B};
+// Epilogue staging maps: a cell's [B x 128] slice of a [R, C, B, H] grid (bf16 or fp32).
+int make_ep_map(CUtensorMap* m, const void* X, CUtensorMapDataType dt, int esz, int64_t R,
+                int64_t C, int64_t B, int64_t H) {
+  const uint64_t dims[4] = {(uint64_t)H, (uint64_t)B, (uint64_t)C, (uint64_t)R};
+  const uint64_t strides[3] = {(uint64_t)H * esz, (uint64_t)(B * H * esz), (uint64_t)(C * B * H * esz)};
+  const uint32_t box[4] = {128, (uint32_t)B, 1, 1};
   return make_tmap(m, X, dt, 4, dims, strides, box, CU_TENSOR_MAP_SWIZZLE_NONE);
 }
 
@@ -449,12 +499,12 @@ template <int H>
 int launch_sweep(const CUtensorMap& wa, const CUtensorMap& wb, const CUtensorMap& in,
                  const CUtensorMap& top, const CUtensorMap& e1, const CUtensorMap& e2,
                  const CUtensorMap& save, const GridParams& p, cudaStream_t s, int* grid_ctas) {
-  const int smem = GridCfg<H>::smem(p.B);
+  const int smem = GridCfg<H>::smem(p.B, p.ep_stages);
   static bool attr = false;
   if (!attr) {
     cudaError_t e = cudaFuncSetAttribute(grid_sweep_kernel<H>,
                                          cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                         GridCfg<H>::smem(64));
+                                         GridCfg<H>::kMaxDynSmem);
     if (e != cudaSuccess) return check_cuda(e, "grid_sweep smem attribute");
     attr = true;
   }
@@ -564,11 +614,15 @@ int grid_fwd_impl(const void* x, int x_layout, const void* W_l, const void* W_t,
   cudaError_t e = cudaMemsetAsync(w.err, 0, 256, s);
   if (e == cudaSuccess) e = cudaMemsetAsync(w.flags, 0, (size_t)R * C * 2 * sizeof(int), s);
   if (e != cudaSuccess) return check_cuda(e, "grid_fwd memset");
-  if (U) {  // add = x U^T  (rows of x in its own layout)
+  if (U) {  // add = x U^T, always in the grid's [R, C, B, H] order (a cell's rows contiguous)
     cublasHandle_t h;
     if ((st = blas(s, w.blas, kBlasWs, &h)) != FLB_OK) return st;
-    st = gemm_rm(h, false, true, (int)(R * C * B), (int)H, (int)H, x, (int)H, 0, U, (int)H, 0,
-                 w.add, (int)H, 0, 1, 0.f);
+    if (x_layout == 1)
+      st = gemm_rm(h, false, true, (int)(R * C * B), (int)H, (int)H, x, (int)H, 0, U, (int)H, 0,
+                   w.add, (int)H, 0, 1, 0.f);
+    else  // x [B, R, C, H]: one batch per b, its R*C rows written with a pitch of B rows
+      st = gemm_rm(h, false, true, (int)(R * C), (int)H, (int)H, x, (int)H, (long long)(R * C * H),
+                   U, (int)H, 0, w.add, (int)(B * H), (long long)H, (int)B, 0.f);
     if (st != FLB_OK) return st;
   }
   CUtensorMap mWl, mWt, mIn, mTop;
@@ -584,11 +638,11 @@ int grid_fwd_impl(const void* x, int x_layout, const void* W_l, const void* W_t,
   CUtensorMap mSave = mIn;
   if (from_up && (st = make_top_map(&mSave, saved_top, C, B, H)) != FLB_OK) return st;
   CUtensorMap mAdd = mIn;
-  if (U && (st = make_ep_map(&mAdd, w.add, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4, x_layout, R, C, B, H)) != FLB_OK)
+  if (U && (st = make_ep_map(&mAdd, w.add, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4, R, C, B, H)) != FLB_OK)
     return st;
   GridParams p{};
   p.add = U ? w.add : nullptr;
-  p.add_layout = x_layout;
+  p.ep_stages = H == 256 ? GridCfg<256>::ep_stages((int)B) : GridCfg<128>::ep_stages((int)B);
   p.bias = bias;
   p.out = (__nv_bfloat16*)h_out;
   p.flags = w.flags;
@@ -687,6 +741,7 @@ int grid_bwd_impl(const void* x, int x_layout, const void* W_l, const void* W_t,
   p.R = (int)R; p.C = (int)C; p.B = (int)B; p.G = (int)G;
   p.has_top = from_down ? 1 : 0;  // the last row's row below: the halo from the next band
   p.reverse = 1;
+  p.ep_stages = H == 256 ? GridCfg<256>::ep_stages((int)B) : GridCfg<128>::ep_stages((int)B);
   p.err = w.err;
   p.drop_cell = -1;
   p.spin_limit = kFlagSpinLimit;
@@ -705,8 +760,8 @@ int grid_bwd_impl(const void* x, int x_layout, const void* W_l, const void* W_t,
   }
   int ctas = 0;
   CUtensorMap mH, mDH;
-  if ((st = make_ep_map(&mH, h_out, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, 1, R, C, B, H)) != FLB_OK) return st;
-  if ((st = make_ep_map(&mDH, dh, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, 1, R, C, B, H)) != FLB_OK) return st;
+  if ((st = make_ep_map(&mH, h_out, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, R, C, B, H)) != FLB_OK) return st;
+  if ((st = make_ep_map(&mDH, dh, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, R, C, B, H)) != FLB_OK) return st;
   st = H == 256 ? launch_sweep<256>(mWl, mWt, mIn, mBelow, mH, mDH, mIn, p, s, &ctas)
                 : launch_sweep<128>(mWl, mWt, mIn, mBelow, mH, mDH, mIn, p, s, &ctas);
   if (st != FLB_OK) return st;
@@ -913,7 +968,7 @@ int grid_fwd_static(const void* W_l, const void* W_t, const float* bias, const v
   }
   GridParams p{};
   p.add = nullptr;
-  p.add_layout = 1;
+  p.ep_stages = 1;
   p.bias = bias;
   p.out = (__nv_bfloat16*)h_out;
   p.flags = flags;
