@@ -513,6 +513,13 @@ int attn_fwd_fast(const void* q, const void* k, const void* v, const float* w, c
 
 namespace {
 
+// dst[0..3] += {a, b, c, d} as one vector reduction (dst 16-byte aligned)
+__device__ __forceinline__ void red_add_v4(float* dst, float a, float b, float c, float d) {
+  asm volatile("red.global.add.v4.f32 [%0], {%1, %2, %3, %4};" ::"l"(dst), "f"(a), "f"(b), "f"(c),
+               "f"(d)
+               : "memory");
+}
+
 struct BwdCfg {
   static constexpr int D = 64, BM = 128, BN = 128;
   static constexpr int TILE = BM * D * 2;                  // 16 KB (a q or dO tile, bf16/fp16)
@@ -902,11 +909,16 @@ attn_bwd_tc_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constan
     {
       const int rows = min(C::BM, N - q0);
       float* dst = dq_acc + ((int64_t)bh * N + q0) * D;
-      for (int e = tid; e < rows * D; e += NT) {
+      // four consecutive head dims per thread, one vector reduction each: dims d, d+2 sit at
+      // [d/2, d/2+1] of the even half of the row's partials, d+1, d+3 in the odd half
+      for (int e = 4 * tid; e < rows * D; e += 4 * NT) {
         const int rr = e / D, d = e % D;
-        float* src = &sDQ[rr * D + (d & 1) * 32 + (d >> 1)];
-        atomicAdd(dst + e, *src * ds_unscale);
-        *src = 0.f;
+        float2* ev = reinterpret_cast<float2*>(&sDQ[rr * D + (d >> 1)]);
+        float2* od = reinterpret_cast<float2*>(&sDQ[rr * D + 32 + (d >> 1)]);
+        const float2 a = *ev, b = *od;
+        red_add_v4(dst + e, a.x * ds_unscale, b.x * ds_unscale, a.y * ds_unscale, b.y * ds_unscale);
+        *ev = make_float2(0.f, 0.f);
+        *od = make_float2(0.f, 0.f);
       }
       if (tid == 0) s_amax = 0u;
     }
