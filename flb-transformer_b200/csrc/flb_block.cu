@@ -34,6 +34,31 @@ namespace {
 
 using bf16 = __nv_bfloat16;
 
+// Programmatic dependent launch: a kernel launched with launch_pdl may be scheduled while its
+// predecessor in the stream is still draining (its launch latency hides behind the predecessor's
+// tail); it waits in pdl_wait, before touching the predecessor's outputs, until that grid has
+// completed and its memory is visible. Without the launch attribute pdl_wait returns at once.
+__device__ __forceinline__ void pdl_wait() {
+  asm volatile("griddepcontrol.wait;" ::: "memory");
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+}
+
+template <typename... KArgs, typename... Args>
+cudaError_t launch_pdl(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem,
+                       cudaStream_t s, Args... args) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = s;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, kernel, static_cast<KArgs>(args)...);
+}
+
 struct Tick {
   int T, l0, n;  // tick, first layer, cells
 };
@@ -58,6 +83,7 @@ __global__ void blk_ln_kernel(const bf16* __restrict__ g_left, const bf16* __res
                               const float* __restrict__ lw1, const float* __restrict__ lb1,
                               bf16* __restrict__ out, int T, int l0, int n, int L, int S, int B,
                               int D, float eps) {
+  pdl_wait();
   const int warps = blockDim.x >> 5, lane = threadIdx.x & 31;
   const int row = blockIdx.x * warps + (threadIdx.x >> 5);
   if (row >= 2 * n * B) return;
@@ -122,6 +148,7 @@ __global__ void blk_gate_kernel(const bf16* __restrict__ z, const float* __restr
                                 const bf16* __restrict__ m, const bf16* __restrict__ g0,
                                 const bf16* __restrict__ x, int mode, bf16* __restrict__ dst,
                                 int T, int l0, int S, int B, int D) {
+  pdl_wait();
   const int j = blockIdx.x * blockDim.x + threadIdx.x;
   if (j >= D / 2) return;
   const int rb = blockIdx.y;  // i * B + b
@@ -142,6 +169,7 @@ __global__ void blk_gate_kernel(const bf16* __restrict__ z, const float* __restr
 //    heads side by side (the reference's transpose(1, 2).view(B, 3, D)).
 __global__ void blk_attn3_kernel(const bf16* __restrict__ qkv, const float* __restrict__ v_a,
                                  bf16* __restrict__ att, int l0, int n, int B, int D, int H) {
+  pdl_wait();
   const int warps = blockDim.x >> 5, lane = threadIdx.x & 31;
   const int task = blockIdx.x * warps + (threadIdx.x >> 5);
   if (task >= n * B * H) return;
@@ -210,6 +238,7 @@ __global__ void blk_out_kernel(const bf16* __restrict__ o, const bf16* __restric
                                const bf16* __restrict__ tok, const bf16* __restrict__ x,
                                bf16* __restrict__ grids, int64_t port_stride, int T, int l0,
                                int S, int B, int D) {
+  pdl_wait();
   const int j = blockIdx.x * blockDim.x + threadIdx.x;
   if (j >= D / 2) return;
   const int rb = blockIdx.y;
@@ -336,10 +365,11 @@ int tick_forward(cublasHandle_t hb, const Side& side, const flb_block_weights* W
                  int L, int S, int B, int D, int H, float eps, cudaStream_t s) {
   const long long DD = (long long)D * D, BD = (long long)B * D;
   int st;
-  blk_ln_kernel<<<(2 * n * B + 7) / 8, 256, 0, s>>>(g + port_stride, g + 2 * port_stride,
-                                                    W->ln_lat_w, W->ln_lat_b, W->ln_fdbk_w,
-                                                    W->ln_fdbk_b, b.ln, T, l0, n, L, S, B, D, eps);
-  cudaError_t e = cudaEventRecord(side.ss->fwd_fork, s);
+  cudaError_t e = launch_pdl(blk_ln_kernel, dim3((2 * n * B + 7) / 8), dim3(256), 0, s,
+                             g + port_stride, g + 2 * port_stride, W->ln_lat_w, W->ln_lat_b,
+                             W->ln_fdbk_w, W->ln_fdbk_b, b.ln, T, l0, n, L, S, B, D, eps);
+  if (e != cudaSuccess) return check_cuda(e, "block_grid LayerNorm launch");
+  e = cudaEventRecord(side.ss->fwd_fork, s);
   if (e == cudaSuccess) e = cudaStreamWaitEvent(side.ss->s, side.ss->fwd_fork, 0);
   if (e != cudaSuccess) return check_cuda(e, "block_grid tick fork");
   const bf16* Wpl = reinterpret_cast<const bf16*>(W->w_prior_lat) + (int64_t)l0 * DD;
@@ -364,20 +394,23 @@ int tick_forward(cublasHandle_t hb, const Side& side, const flb_block_weights* W
   e = cudaStreamWaitEvent(s, side.ss->fwd_join, 0);
   if (e != cudaSuccess) return check_cuda(e, "block_grid tick join");
   const dim3 ew_grid((unsigned)((D / 2 + 127) / 128), (unsigned)(n * B));
-  blk_gate_kernel<<<ew_grid, 128, 0, s>>>(b.zl, W->b_gate_l, b.lat, g, xb, 0, b.tok + D, T, l0, S,
-                                          B, D);
+  e = launch_pdl(blk_gate_kernel, ew_grid, dim3(128), 0, s, b.zl, W->b_gate_l, b.lat, g, xb, 0,
+                 b.tok + D, T, l0, S, B, D);
+  if (e != cudaSuccess) return check_cuda(e, "block_grid gate launch");
   // sensory gate
   if ((st = gemm_rm(hb, false, true, B, D, D, b.tok + D, 3 * D, 3 * BD, Wgx, D, 2 * DD, b.zx, D, BD,
                     n, 0.f, CUDA_R_16BF)) != FLB_OK)
     return st;
-  blk_gate_kernel<<<ew_grid, 128, 0, s>>>(b.zx, W->b_gate_x, nullptr, g, xb, 1, b.tok, T, l0, S, B,
-                                          D);
+  e = launch_pdl(blk_gate_kernel, ew_grid, dim3(128), 0, s, b.zx, W->b_gate_x,
+                 static_cast<const bf16*>(nullptr), g, xb, 1, b.tok, T, l0, S, B, D);
+  if (e != cudaSuccess) return check_cuda(e, "block_grid gate launch");
   // q | k | v of the 3 tokens: [n, 3B, D] x [3D, D]^T
   if ((st = gemm_rm(hb, false, true, 3 * B, 3 * D, D, b.tok, D, 3 * BD, Wqkv, D, 6 * DD, b.qkv,
                     3 * D, 9 * BD, n, 0.f, CUDA_R_16BF)) != FLB_OK)
     return st;
-  blk_attn3_kernel<<<(n * B * H + 7) / 8, 256, 0, s>>>(b.qkv, W->v_a, b.att, l0, n, B, D, H);
-  return FLB_OK;
+  e = launch_pdl(blk_attn3_kernel, dim3((n * B * H + 7) / 8), dim3(256), 0, s, b.qkv, W->v_a,
+                 b.att, l0, n, B, D, H);
+  return check_cuda(e, "block_grid attention launch");
 }
 
 }  // namespace
@@ -413,8 +446,9 @@ int block_grid_fwd(const flb_block_weights* W, const void* x, void* grids, int64
                       3 * BD, n, 0.f, CUDA_R_16BF)) != FLB_OK)
       return st;
     const dim3 ew_grid((unsigned)((D / 2 + 127) / 128), (unsigned)(n * Bi));
-    blk_out_kernel<<<ew_grid, 128, 0, s>>>(w.o, w.lat, w.tok, xb, g, port_stride, T, l0, Si, Bi,
-                                           Di);
+    cudaError_t e = launch_pdl(blk_out_kernel, ew_grid, dim3(128), 0, s, w.o, w.lat, w.tok, xb,
+                               g, port_stride, T, l0, Si, Bi, Di);
+    if (e != cudaSuccess) return check_cuda(e, "block_grid output launch");
     launches += 6;  // own kernels (the GEMMs are cuBLAS's)
   }
   count_launches(launches);
