@@ -480,6 +480,7 @@ __device__ __forceinline__ float sigm(float z) { return 1.f / (1.f + __expf(-z))
 __global__ void blk_dg_init_kernel(const bf16* __restrict__ g0, const bf16* __restrict__ g1,
                                    const bf16* __restrict__ g2, float* __restrict__ dG,
                                    int64_t per_port) {
+  pdl_wait();
   for (int64_t e = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; e < 3 * per_port;
        e += (int64_t)gridDim.x * blockDim.x) {
     const int p = (int)(e / per_port);
@@ -496,6 +497,7 @@ __global__ void blk_bwd_out_kernel(const float* __restrict__ dG, int64_t per_por
                                    const bf16* __restrict__ tok, bf16* __restrict__ d_o,
                                    float* __restrict__ d_top, float* __restrict__ d_lp,
                                    float* __restrict__ d_fp, int T, int l0, int S, int B, int D) {
+  pdl_wait();
   const int j = blockIdx.x * blockDim.x + threadIdx.x;
   if (j >= D / 2) return;
   const int rb = blockIdx.y;
@@ -527,6 +529,7 @@ __global__ void blk_bwd_out_kernel(const float* __restrict__ dG, int64_t per_por
 __global__ void blk_attn3_bwd_kernel(const bf16* __restrict__ qkv, const float* __restrict__ v_a,
                                      const bf16* __restrict__ d_att, bf16* __restrict__ d_qkv,
                                      float* __restrict__ d_va, int l0, int n, int B, int D, int H) {
+  pdl_wait();
   const int warps = blockDim.x >> 5, lane = threadIdx.x & 31;
   const int task = blockIdx.x * warps + (threadIdx.x >> 5);
   if (task >= n * B * H) return;
@@ -626,6 +629,7 @@ __global__ void blk_gx_bwd_kernel(const float* __restrict__ dT, const bf16* __re
                                   bf16* __restrict__ d_zx, float* __restrict__ d_lr,
                                   float* __restrict__ d_fp, float* __restrict__ db_gx, int T,
                                   int l0, int S, int B, int D) {
+  pdl_wait();
   const int j = blockIdx.x * blockDim.x + threadIdx.x;
   if (j >= D / 2) return;
   const int i = blockIdx.y;
@@ -670,6 +674,7 @@ __global__ void blk_gl_bwd_kernel(const float* __restrict__ d_lr, const bf16* __
                                   float* __restrict__ d_lp, bf16* __restrict__ d_lp_h,
                                   bf16* __restrict__ d_zl, float* __restrict__ db_gl, int l0,
                                   int B, int D) {
+  pdl_wait();
   const int j = blockIdx.x * blockDim.x + threadIdx.x;
   if (j >= D / 2) return;
   const int i = blockIdx.y;
@@ -697,6 +702,7 @@ __global__ void blk_gl_bwd_kernel(const float* __restrict__ d_lr, const bf16* __
 
 __global__ void blk_cast_kernel(const float* __restrict__ src, bf16* __restrict__ dst,
                                 int64_t pairs) {
+  pdl_wait();
   for (int64_t e = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; e < pairs;
        e += (int64_t)gridDim.x * blockDim.x) {
     const float2 v = reinterpret_cast<const float2*>(src)[e];
@@ -714,6 +720,7 @@ __global__ void blk_ln_bwd_kernel(const bf16* __restrict__ grids, int64_t port_s
                                   float* __restrict__ db0, float* __restrict__ dw1,
                                   float* __restrict__ db1, int T, int l0, int n, int L, int S,
                                   int B, int D, float eps) {
+  pdl_wait();
   extern __shared__ float red[];  // [2][D]: dgamma, dbeta partials of this block
   const int which = blockIdx.x / n, i = blockIdx.x % n;
   const int l = l0 + 2 * i, t = (T - l) / 2;
@@ -878,9 +885,11 @@ int block_grid_bwd(const flb_block_weights* W, const void* x, const void* grids,
   const int Li = (int)L, Si = (int)S, Bi = (int)B, Di = (int)D, Hi = (int)H;
   const int ticks = (int)(L + 2 * S - 2);
   const int ew = 4 * num_sms();
-  blk_dg_init_kernel<<<ew, 256, 0, s>>>((const bf16*)dgrids[0], (const bf16*)dgrids[1],
-                                        (const bf16*)dgrids[2], w.dG, per_port);
-  cudaError_t ce = cudaMemsetAsync(dx, 0, (size_t)B * S * D * 4, s);
+  cudaError_t ce = launch_pdl(blk_dg_init_kernel, dim3(ew), dim3(256), 0, s,
+                              (const bf16*)dgrids[0], (const bf16*)dgrids[1],
+                              (const bf16*)dgrids[2], w.dG, per_port);
+  if (ce != cudaSuccess) return check_cuda(ce, "block_grid_bwd launch");
+  ce = cudaMemsetAsync(dx, 0, (size_t)B * S * D * 4, s);
   if (ce != cudaSuccess) return check_cuda(ce, "block_grid_bwd dx reset");
   const bf16* ext3 = (const bf16*)dgrids[3];
   int launches = 1;
@@ -893,9 +902,10 @@ int block_grid_bwd(const flb_block_weights* W, const void* x, const void* grids,
       return st;
     const dim3 ew_grid((unsigned)((D / 2 + 127) / 128), (unsigned)(n * Bi));
     const dim3 cell_grid((unsigned)((D / 2 + 127) / 128), (unsigned)n);
-    blk_bwd_out_kernel<<<ew_grid, 128, 0, s>>>(w.dG, per_port, ext3, g, port_stride, w.f.lat,
-                                               w.f.tok, w.d_o, w.d_top, w.d_lp, w.d_fp, T, l0, Si,
-                                               Bi, Di);
+    if ((ce = launch_pdl(blk_bwd_out_kernel, ew_grid, dim3(128), 0, s, w.dG, per_port, ext3, g,
+                         port_stride, w.f.lat, w.f.tok, w.d_o, w.d_top, w.d_lp, w.d_fp, T, l0,
+                         Si, Bi, Di)) != cudaSuccess)
+      return check_cuda(ce, "block_grid_bwd launch");
     const bf16* Wo = reinterpret_cast<const bf16*>(W->w_o) + (int64_t)l0 * DD;
     const bf16* Wqkv = reinterpret_cast<const bf16*>(W->w_qkv) + (int64_t)l0 * 3 * DD;
     const bf16* Wgx = reinterpret_cast<const bf16*>(W->w_gate_x) + (int64_t)l0 * DD;
@@ -910,8 +920,10 @@ int block_grid_bwd(const flb_block_weights* W, const void* x, const void* grids,
     if ((st = gemm_rm(hs, true, false, Di, Di, 3 * Bi, w.d_o, Di, 3 * BD, w.f.att, Di, 3 * BD,
                       G->w_o + (int64_t)l0 * DD, Di, 2 * DD, n, 1.f)) != FLB_OK)
       return st;
-    blk_attn3_bwd_kernel<<<(n * Bi * Hi + 7) / 8, 256, 0, s>>>(w.f.qkv, W->v_a, w.d_att, w.d_qkv,
-                                                               G->v_a, l0, n, Bi, Di, Hi);
+    if ((ce = launch_pdl(blk_attn3_bwd_kernel, dim3((n * Bi * Hi + 7) / 8), dim3(256), 0, s,
+                         w.f.qkv, W->v_a, w.d_att, w.d_qkv, G->v_a, l0, n, Bi, Di, Hi)) !=
+        cudaSuccess)
+      return check_cuda(ce, "block_grid_bwd launch");
     // q | k | v projections
     if ((st = gemm_rm(hb, false, false, 3 * Bi, Di, 3 * Di, w.d_qkv, 3 * Di, 9 * BD, Wqkv, Di,
                       6 * DD, w.dT, Di, 3 * BD, n, 0.f)) != FLB_OK)
@@ -921,9 +933,10 @@ int block_grid_bwd(const flb_block_weights* W, const void* x, const void* grids,
                       3 * BD, G->w_qkv + (int64_t)l0 * 3 * DD, Di, 6 * DD, n, 1.f)) != FLB_OK)
       return st;
     // sensory gate
-    blk_gx_bwd_kernel<<<cell_grid, 128, 0, s>>>(w.dT, w.f.zx, W->b_gate_x, g, xb, w.d_top, w.dG,
-                                                dx, w.d_zx, w.d_lr, w.d_fp, G->b_gate_x, T, l0, Si,
-                                                Bi, Di);
+    if ((ce = launch_pdl(blk_gx_bwd_kernel, cell_grid, dim3(128), 0, s, w.dT, w.f.zx, W->b_gate_x,
+                         g, xb, w.d_top, w.dG, dx, w.d_zx, w.d_lr, w.d_fp, G->b_gate_x, T, l0, Si,
+                         Bi, Di)) != cudaSuccess)
+      return check_cuda(ce, "block_grid_bwd launch");
     if ((st = gemm_rm(hb, false, false, Bi, Di, Di, w.d_zx, Di, BD, Wgx, Di, 2 * DD, w.d_lr, Di, BD,
                       n, 1.f)) != FLB_OK)
       return st;
@@ -932,8 +945,10 @@ int block_grid_bwd(const flb_block_weights* W, const void* x, const void* grids,
                       G->w_gate_x + (int64_t)l0 * DD, Di, 2 * DD, n, 1.f)) != FLB_OK)
       return st;
     // lateral gate
-    blk_gl_bwd_kernel<<<cell_grid, 128, 0, s>>>(w.d_lr, w.f.zl, W->b_gate_l, w.f.lat, w.d_lp,
-                                                w.d_lp_h, w.d_zl, G->b_gate_l, l0, Bi, Di);
+    if ((ce = launch_pdl(blk_gl_bwd_kernel, cell_grid, dim3(128), 0, s, w.d_lr, w.f.zl,
+                         W->b_gate_l, w.f.lat, w.d_lp, w.d_lp_h, w.d_zl, G->b_gate_l, l0, Bi,
+                         Di)) != cudaSuccess)
+      return check_cuda(ce, "block_grid_bwd launch");
     if ((st = gemm_rm(hb, false, false, Bi, Di, Di, w.d_zl, Di, BD, Wgl, Di, 2 * DD, w.d_fp, Di, BD,
                       n, 1.f)) != FLB_OK)
       return st;
@@ -941,8 +956,11 @@ int block_grid_bwd(const flb_block_weights* W, const void* x, const void* grids,
     if ((st = gemm_rm(hs, true, false, Di, Di, Bi, w.d_zl, Di, BD, w.f.tok + 2 * D, 3 * Di, 3 * BD,
                       G->w_gate_l + (int64_t)l0 * DD, Di, 2 * DD, n, 1.f)) != FLB_OK)
       return st;
-    blk_cast_kernel<<<(unsigned)std::min<int64_t>((n * BD / 2 + 255) / 256, ew), 256, 0, s>>>(
-        w.d_fp, w.d_fp_h, n * BD / 2);
+    if ((ce = launch_pdl(blk_cast_kernel,
+                         dim3((unsigned)std::min<int64_t>((n * BD / 2 + 255) / 256, ew)),
+                         dim3(256), 0, s, w.d_fp, w.d_fp_h, (int64_t)(n * BD / 2))) !=
+        cudaSuccess)
+      return check_cuda(ce, "block_grid_bwd launch");
     // priors
     if ((st = gemm_rm(hb, false, false, Bi, Di, Di, w.d_lp_h, Di, BD, Wpl, Di, 2 * DD, w.dA, Di, BD,
                       n, 0.f)) != FLB_OK)
@@ -957,9 +975,11 @@ int block_grid_bwd(const flb_block_weights* W, const void* x, const void* grids,
     if ((st = gemm_rm(hs, true, false, Di, Di, Bi, w.d_fp_h, Di, BD, w.f.ln + n * BD, Di, BD,
                       G->w_prior_fdbk + (int64_t)l0 * DD, Di, 2 * DD, n, 1.f)) != FLB_OK)
       return st;
-    blk_ln_bwd_kernel<<<2 * n, 512, 2 * D * sizeof(float), s>>>(
-        g, port_stride, w.dA, W->ln_lat_w, W->ln_fdbk_w, w.dG, per_port, G->ln_lat_w,
-        G->ln_lat_b, G->ln_fdbk_w, G->ln_fdbk_b, T, l0, n, Li, Si, Bi, Di, eps);
+    if ((ce = launch_pdl(blk_ln_bwd_kernel, dim3(2 * n), dim3(512), 2 * D * sizeof(float), s, g,
+                         port_stride, w.dA, W->ln_lat_w, W->ln_fdbk_w, w.dG, per_port,
+                         G->ln_lat_w, G->ln_lat_b, G->ln_fdbk_w, G->ln_fdbk_b, T, l0, n, Li, Si,
+                         Bi, Di, eps)) != cudaSuccess)
+      return check_cuda(ce, "block_grid_bwd launch");
     if ((st = join()) != FLB_OK) return st;
     launches += 10;  // own kernels (4 recompute + 6 backward)
   }
