@@ -31,7 +31,6 @@ CU_SOURCES = [
     "attention_generic.cu",
     "attention_fast.cu",
     "wavefront_prims.cu",
-    "cell_gemm.cu",
     "wavefront_grid.cu",
     "flb_block.cu",
     "microbench.cu",

@@ -90,9 +90,6 @@ int grid_fwd_static(const void* W_l, const void* W_t, const float* bias, const v
                     void* h_out, int64_t R, int64_t C, int64_t B, int64_t H, int64_t G,
                     int check_timeout, cudaStream_t s);
 int microbench(int kind, void* scratch, double* ops_per_s);
-int cell_gemm(const void* W, int64_t w_rows_total, int w_row0, int w_cell_rows, const void* X,
-              int64_t ldx, int64_t stride_x, int n_cells, int M, int N, int K, void* Y,
-              int64_t ldy, int64_t stride_y, int* err, cudaStream_t s);
 int umma_selftest(int variant, int n, const void* A, const void* B, float* D, int* err,
                   cudaStream_t s);
 
@@ -359,20 +356,6 @@ int flb_grid_fwd_static(const void* W_l, const void* W_t, const float* bias, con
                         int check_timeout, void* stream) {
   return grid_fwd_static(W_l, W_t, bias, top, h_out, R, C, B, H, G, check_timeout,
                          as_stream(stream));
-}
-
-int flb_cell_gemm(const void* W, int64_t w_rows_total, int64_t w_row0, int64_t w_cell_rows,
-                  const void* X, int64_t ldx, int64_t stride_x, int64_t n_cells, int64_t M,
-                  int64_t N, int64_t K, void* Y, int64_t ldy, int64_t stride_y, int* err,
-                  void* stream) {
-  if (!W || !X || !Y) return fail(FLB_ERR_SHAPE, "cell_gemm: null pointer");
-  if (n_cells < 0 || n_cells > 65535 || M < 0 || N < 0 || K < 0 || w_row0 < 0 || w_cell_rows < 0 ||
-      w_rows_total > INT32_MAX || ldx < K || ldy < N || stride_x < 0 || stride_y < 0)
-    return fail(FLB_ERR_SHAPE, "cell_gemm: bad sizes");
-  if (n_cells > 0 && w_row0 + (n_cells - 1) * w_cell_rows + N > w_rows_total)
-    return fail(FLB_ERR_SHAPE, "cell_gemm: weight rows out of range");
-  return cell_gemm(W, w_rows_total, (int)w_row0, (int)w_cell_rows, X, ldx, stride_x, (int)n_cells,
-                   (int)M, (int)N, (int)K, Y, ldy, stride_y, err, as_stream(stream));
 }
 
 int flb_microbench(int kind, void* scratch, double* ops_per_s) {

@@ -75,8 +75,6 @@ PROTOTYPES = {
                                  _vp, _vp, _i64, _i64, _i64, _i64, _i64, _vp, _vp, _sz, _i32,
                                  _vp]),
     "flb_microbench": (_i32, [_i32, _vp, _dblp]),
-    "flb_cell_gemm": (_i32, [_vp, _i64, _i64, _i64, _vp, _i64, _i64, _i64, _i64, _i64, _i64, _vp,
-                             _i64, _i64, _vp, _vp]),
     "flb_selftest_umma": (_i32, [_i32, _i32, _vp, _vp, _vp, _vp, _vp]),
 }
 

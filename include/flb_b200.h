@@ -351,19 +351,6 @@ int flb_microbench(int kind, void* scratch, double* ops_per_s);
 int flb_selftest_umma(int variant, int n, const void* A, const void* B, float* D, int* err,
                       void* stream);
 
-/* Direct call of the tcgen05 projection GEMM of the FLB block cells (no reference counterpart: it
- * replaces the per-tick nn.Linear calls of models/FLB_Model.py:32-96 inside flb_block_grid_fwd and
- * the backward's recompute; exposed for its parity test). For cells i < n_cells:
- *   Y[i*stride_y + m*ldy + j] = sum_k X[i*stride_x + m*ldx + k] * W[(w_row0 + i*w_cell_rows + j)*K + k]
- * with m < M, j < N, k < K; bf16 in and out, fp32 accumulation. W holds w_rows_total rows of K.
- * Supported: M in {16, 32, 48, 64}, N a multiple of 128, K a multiple of 64, 16-byte aligned
- * W and X with ldx and stride_x multiples of 8 (else FLB_ERR_UNSUPPORTED). *err (device int,
- * caller-zeroed, may be NULL) becomes non-zero if a bounded wait gave up. */
-int flb_cell_gemm(const void* W, int64_t w_rows_total, int64_t w_row0, int64_t w_cell_rows,
-                  const void* X, int64_t ldx, int64_t stride_x, int64_t n_cells, int64_t M,
-                  int64_t N, int64_t K, void* Y, int64_t ldy, int64_t stride_y, int* err,
-                  void* stream);
-
 #ifdef __cplusplus
 }
 #endif
