@@ -630,42 +630,56 @@ __global__ void blk_gx_bwd_kernel(const float* __restrict__ dT, const bf16* __re
                                   float* __restrict__ d_fp, float* __restrict__ db_gx, int T,
                                   int l0, int S, int B, int D) {
   pdl_wait();
-  const int j = blockIdx.x * blockDim.x + threadIdx.x;
-  if (j >= D / 2) return;
+  // block: 32 feature pairs (x) by up to 16 batch rows (y); the bias gradient is summed over
+  // the rows in a fixed order (deterministic)
+  __shared__ float2 part[16][32];
+  const int j = blockIdx.x * 32 + threadIdx.x;
+  const bool live = j < D / 2;
   const int i = blockIdx.y;
   const int l = l0 + 2 * i, t = (T - l) / 2;
-  const float2 bias = reinterpret_cast<const float2*>(b_gx + (int64_t)l * D)[j];
   float2 acc = make_float2(0.f, 0.f);
-  for (int b = 0; b < B; ++b) {
-    const int64_t rb = (int64_t)i * B + b;
-    const float2 dxr = reinterpret_cast<const float2*>(dT + (rb * 3) * D)[j];
-    const float2 z = __bfloat1622float2(reinterpret_cast<const __nv_bfloat162*>(zx + rb * D)[j]);
-    const float2 top = __bfloat1622float2(
-        reinterpret_cast<const __nv_bfloat162*>(top_row(grids, x, l, t, b, S, B, D))[j]);
-    const float s0 = sigm(z.x + bias.x), s1 = sigm(z.y + bias.y);
-    const float2 dt0 = reinterpret_cast<const float2*>(d_top + rb * D)[j];
-    const float2 dtop = make_float2(dt0.x + dxr.x * s0, dt0.y + dxr.y * s1);
-    if (l > 0) {
-      float2* dst = reinterpret_cast<float2*>(dG0 + (cell_row(l - 1, t, S) * B + b) * D) + j;
-      const float2 o = *dst;
-      *dst = make_float2(o.x + dtop.x, o.y + dtop.y);
-    } else {
-      reinterpret_cast<float2*>(dx + ((int64_t)b * S + t) * D)[j] = dtop;
+  if (live) {
+    const float2 bias = reinterpret_cast<const float2*>(b_gx + (int64_t)l * D)[j];
+    for (int b = threadIdx.y; b < B; b += blockDim.y) {
+      const int64_t rb = (int64_t)i * B + b;
+      const float2 dxr = reinterpret_cast<const float2*>(dT + (rb * 3) * D)[j];
+      const float2 z = __bfloat1622float2(reinterpret_cast<const __nv_bfloat162*>(zx + rb * D)[j]);
+      const float2 top = __bfloat1622float2(
+          reinterpret_cast<const __nv_bfloat162*>(top_row(grids, x, l, t, b, S, B, D))[j]);
+      const float s0 = sigm(z.x + bias.x), s1 = sigm(z.y + bias.y);
+      const float2 dt0 = reinterpret_cast<const float2*>(d_top + rb * D)[j];
+      const float2 dtop = make_float2(dt0.x + dxr.x * s0, dt0.y + dxr.y * s1);
+      if (l > 0) {
+        float2* dst = reinterpret_cast<float2*>(dG0 + (cell_row(l - 1, t, S) * B + b) * D) + j;
+        const float2 o = *dst;
+        *dst = make_float2(o.x + dtop.x, o.y + dtop.y);
+      } else {
+        reinterpret_cast<float2*>(dx + ((int64_t)b * S + t) * D)[j] = dtop;
+      }
+      const float dz0 = dxr.x * top.x * s0 * (1.f - s0), dz1 = dxr.y * top.y * s1 * (1.f - s1);
+      reinterpret_cast<__nv_bfloat162*>(d_zx + rb * D)[j] = __floats2bfloat162_rn(dz0, dz1);
+      acc.x += dz0;
+      acc.y += dz1;
+      reinterpret_cast<float2*>(d_lr + rb * D)[j] =
+          reinterpret_cast<const float2*>(dT + (rb * 3 + 1) * D)[j];
+      const float2 dtf = reinterpret_cast<const float2*>(dT + (rb * 3 + 2) * D)[j];
+      float2* fp = reinterpret_cast<float2*>(d_fp + rb * D) + j;
+      const float2 o = *fp;
+      *fp = make_float2(o.x + dtf.x, o.y + dtf.y);
     }
-    const float dz0 = dxr.x * top.x * s0 * (1.f - s0), dz1 = dxr.y * top.y * s1 * (1.f - s1);
-    reinterpret_cast<__nv_bfloat162*>(d_zx + rb * D)[j] = __floats2bfloat162_rn(dz0, dz1);
-    acc.x += dz0;
-    acc.y += dz1;
-    reinterpret_cast<float2*>(d_lr + rb * D)[j] =
-        reinterpret_cast<const float2*>(dT + (rb * 3 + 1) * D)[j];
-    const float2 dtf = reinterpret_cast<const float2*>(dT + (rb * 3 + 2) * D)[j];
-    float2* fp = reinterpret_cast<float2*>(d_fp + rb * D) + j;
-    const float2 o = *fp;
-    *fp = make_float2(o.x + dtf.x, o.y + dtf.y);
   }
-  float2* db = reinterpret_cast<float2*>(db_gx + (int64_t)l * D) + j;
-  const float2 o = *db;
-  *db = make_float2(o.x + acc.x, o.y + acc.y);
+  part[threadIdx.y][threadIdx.x] = acc;
+  __syncthreads();
+  if (live && threadIdx.y == 0) {
+    float2 sum = part[0][threadIdx.x];
+    for (int y = 1; y < (int)blockDim.y; ++y) {
+      sum.x += part[y][threadIdx.x].x;
+      sum.y += part[y][threadIdx.x].y;
+    }
+    float2* db = reinterpret_cast<float2*>(db_gx + (int64_t)l * D) + j;
+    const float2 o = *db;
+    *db = make_float2(o.x + sum.x, o.y + sum.y);
+  }
 }
 
 // lateral gate backward: grid (pairs, cells), loop over the batch rows; finishes d_lat_prior
@@ -675,29 +689,41 @@ __global__ void blk_gl_bwd_kernel(const float* __restrict__ d_lr, const bf16* __
                                   bf16* __restrict__ d_zl, float* __restrict__ db_gl, int l0,
                                   int B, int D) {
   pdl_wait();
-  const int j = blockIdx.x * blockDim.x + threadIdx.x;
-  if (j >= D / 2) return;
+  __shared__ float2 part[16][32];  // as blk_gx_bwd_kernel: 32 pairs by up to 16 rows
+  const int j = blockIdx.x * 32 + threadIdx.x;
+  const bool live = j < D / 2;
   const int i = blockIdx.y;
   const int l = l0 + 2 * i;
-  const float2 bias = reinterpret_cast<const float2*>(b_gl + (int64_t)l * D)[j];
   float2 acc = make_float2(0.f, 0.f);
-  for (int b = 0; b < B; ++b) {
-    const int64_t rb = (int64_t)i * B + b;
-    const float2 dl = reinterpret_cast<const float2*>(d_lr + rb * D)[j];
-    const float2 z = __bfloat1622float2(reinterpret_cast<const __nv_bfloat162*>(zl + rb * D)[j]);
-    const float2 lp = __bfloat1622float2(reinterpret_cast<const __nv_bfloat162*>(lat + rb * D)[j]);
-    const float s0 = sigm(z.x + bias.x), s1 = sigm(z.y + bias.y);
-    const float2 o = reinterpret_cast<const float2*>(d_lp + rb * D)[j];
-    const float2 dlp = make_float2(o.x + dl.x * s0, o.y + dl.y * s1);
-    reinterpret_cast<__nv_bfloat162*>(d_lp_h + rb * D)[j] = __floats2bfloat162_rn(dlp.x, dlp.y);
-    const float dz0 = dl.x * lp.x * s0 * (1.f - s0), dz1 = dl.y * lp.y * s1 * (1.f - s1);
-    reinterpret_cast<__nv_bfloat162*>(d_zl + rb * D)[j] = __floats2bfloat162_rn(dz0, dz1);
-    acc.x += dz0;
-    acc.y += dz1;
+  if (live) {
+    const float2 bias = reinterpret_cast<const float2*>(b_gl + (int64_t)l * D)[j];
+    for (int b = threadIdx.y; b < B; b += blockDim.y) {
+      const int64_t rb = (int64_t)i * B + b;
+      const float2 dl = reinterpret_cast<const float2*>(d_lr + rb * D)[j];
+      const float2 z = __bfloat1622float2(reinterpret_cast<const __nv_bfloat162*>(zl + rb * D)[j]);
+      const float2 lp = __bfloat1622float2(reinterpret_cast<const __nv_bfloat162*>(lat + rb * D)[j]);
+      const float s0 = sigm(z.x + bias.x), s1 = sigm(z.y + bias.y);
+      const float2 o = reinterpret_cast<const float2*>(d_lp + rb * D)[j];
+      const float2 dlp = make_float2(o.x + dl.x * s0, o.y + dl.y * s1);
+      reinterpret_cast<__nv_bfloat162*>(d_lp_h + rb * D)[j] = __floats2bfloat162_rn(dlp.x, dlp.y);
+      const float dz0 = dl.x * lp.x * s0 * (1.f - s0), dz1 = dl.y * lp.y * s1 * (1.f - s1);
+      reinterpret_cast<__nv_bfloat162*>(d_zl + rb * D)[j] = __floats2bfloat162_rn(dz0, dz1);
+      acc.x += dz0;
+      acc.y += dz1;
+    }
   }
-  float2* db = reinterpret_cast<float2*>(db_gl + (int64_t)l * D) + j;
-  const float2 o = *db;
-  *db = make_float2(o.x + acc.x, o.y + acc.y);
+  part[threadIdx.y][threadIdx.x] = acc;
+  __syncthreads();
+  if (live && threadIdx.y == 0) {
+    float2 sum = part[0][threadIdx.x];
+    for (int y = 1; y < (int)blockDim.y; ++y) {
+      sum.x += part[y][threadIdx.x].x;
+      sum.y += part[y][threadIdx.x].y;
+    }
+    float2* db = reinterpret_cast<float2*>(db_gl + (int64_t)l * D) + j;
+    const float2 o = *db;
+    *db = make_float2(o.x + sum.x, o.y + sum.y);
+  }
 }
 
 __global__ void blk_cast_kernel(const float* __restrict__ src, bf16* __restrict__ dst,
@@ -710,9 +736,11 @@ __global__ void blk_cast_kernel(const float* __restrict__ src, bf16* __restrict_
   }
 }
 
-// LayerNorm backward: one block per (which, cell), its warps over the batch rows. Routes the
-// input gradient to the producer's port gradient (left -> port 1 of (l, t-1), bottom-left ->
-// port 2 of (l+1, t-1)) and accumulates dgamma / dbeta of the cell's layer.
+// LayerNorm backward: one block per (which, cell). Phase 1, a warp per batch row: the row's
+// mean, 1/std and the two reductions of the input gradient (c1 = mean of g*gamma, c2 = mean of
+// g*gamma*xhat). Phase 2, threads over feature pairs looping over the rows (coalesced, no
+// atomics): dgamma / dbeta of the cell's layer, and the input gradient routed to the producer's
+// port gradient (left -> port 1 of (l, t-1), bottom-left -> port 2 of (l+1, t-1)).
 __global__ void blk_ln_bwd_kernel(const bf16* __restrict__ grids, int64_t port_stride,
                                   const float* __restrict__ dA, const float* __restrict__ lw0,
                                   const float* __restrict__ lw1, float* __restrict__ dG,
@@ -721,27 +749,25 @@ __global__ void blk_ln_bwd_kernel(const bf16* __restrict__ grids, int64_t port_s
                                   float* __restrict__ db1, int T, int l0, int n, int L, int S,
                                   int B, int D, float eps) {
   pdl_wait();
-  extern __shared__ float red[];  // [2][D]: dgamma, dbeta partials of this block
+  extern __shared__ float stat[];  // [B][4]: mean, rstd, c1, c2
   const int which = blockIdx.x / n, i = blockIdx.x % n;
   const int l = l0 + 2 * i, t = (T - l) / 2;
   const int warps = blockDim.x >> 5, warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  for (int e = threadIdx.x; e < 2 * D; e += blockDim.x) red[e] = 0.f;
-  __syncthreads();
   const float* gamma = (which ? lw1 : lw0) + (int64_t)l * D;
   const bool has_src = t > 0 && (which == 0 || l + 1 < L);
   const int64_t src_cell = which == 0 ? cell_row(l, t - 1, S) : cell_row(l + 1, t - 1, S);
-  const bf16* src_port = grids + (which ? 2 : 1) * port_stride;
-  float* dst_port = dG + (which ? 2 : 1) * per_port;
+  const bf16* src = grids + (which ? 2 : 1) * port_stride + src_cell * B * D;
+  float* dst = dG + (which ? 2 : 1) * per_port + src_cell * B * D;
+  const float* da = dA + (int64_t)(which * n + i) * B * D;
   const int nch = D / 8;
   for (int b = warp; b < B; b += warps) {
-    const float* da = dA + ((int64_t)(which * n + i) * B + b) * D;
     float xv[kMaxChunks][8];
     float s = 0.f, ss = 0.f;
 #pragma unroll
     for (int k = 0; k < kMaxChunks; ++k) {
       const int c = lane + 32 * k;
       uint4 raw = make_uint4(0, 0, 0, 0);
-      if (has_src && c < nch) raw = reinterpret_cast<const uint4*>(src_port + (src_cell * B + b) * D)[c];
+      if (has_src && c < nch) raw = reinterpret_cast<const uint4*>(src + (int64_t)b * D)[c];
       const uint32_t* r = reinterpret_cast<const uint32_t*>(&raw);
 #pragma unroll
       for (int e = 0; e < 4; ++e) {
@@ -761,41 +787,57 @@ __global__ void blk_ln_bwd_kernel(const bf16* __restrict__ grids, int64_t port_s
     for (int k = 0; k < kMaxChunks; ++k) {
       const int c = lane + 32 * k;
       if (c >= nch) break;
+      const float4* g4 = reinterpret_cast<const float4*>(da + (int64_t)b * D + 8 * c);
+      const float4* w4 = reinterpret_cast<const float4*>(gamma + 8 * c);
+      const float4 ga = g4[0], gb = g4[1], wa = w4[0], wb = w4[1];
+      const float g[8] = {ga.x, ga.y, ga.z, ga.w, gb.x, gb.y, gb.z, gb.w};
+      const float w[8] = {wa.x, wa.y, wa.z, wa.w, wb.x, wb.y, wb.z, wb.w};
 #pragma unroll
       for (int e = 0; e < 8; ++e) {
-        const int d = 8 * c + e;
-        const float xh = (xv[k][e] - mean) * rstd;
-        const float g = da[d];
-        const float dxh = g * gamma[d];
+        const float dxh = g[e] * w[e];
         c1 += dxh;
-        c2 += dxh * xh;
-        atomicAdd(&red[d], g * xh);
-        atomicAdd(&red[D + d], g);
-        xv[k][e] = xh;
+        c2 += dxh * (xv[k][e] - mean) * rstd;
       }
     }
     c1 = warp_sum(c1) / D;
     c2 = warp_sum(c2) / D;
-    if (has_src) {
-      float* dst = dst_port + (src_cell * B + b) * D;
-#pragma unroll
-      for (int k = 0; k < kMaxChunks; ++k) {
-        const int c = lane + 32 * k;
-        if (c >= nch) break;
-#pragma unroll
-        for (int e = 0; e < 8; ++e) {
-          const int d = 8 * c + e;
-          dst[d] += rstd * (da[d] * gamma[d] - c1 - xv[k][e] * c2);
-        }
-      }
+    if (lane == 0) {
+      stat[4 * b] = mean;
+      stat[4 * b + 1] = rstd;
+      stat[4 * b + 2] = c1;
+      stat[4 * b + 3] = c2;
     }
   }
   __syncthreads();
   float* dw = (which ? dw1 : dw0) + (int64_t)l * D;
   float* db = (which ? db1 : db0) + (int64_t)l * D;
-  for (int d = threadIdx.x; d < D; d += blockDim.x) {
-    dw[d] += red[d];
-    db[d] += red[D + d];
+  for (int jp = threadIdx.x; jp < D / 2; jp += blockDim.x) {
+    const float2 gm = reinterpret_cast<const float2*>(gamma)[jp];
+    float2 dgam = make_float2(0.f, 0.f), dbet = make_float2(0.f, 0.f);
+    for (int b = 0; b < B; ++b) {
+      const float mean = stat[4 * b], rstd = stat[4 * b + 1], c1 = stat[4 * b + 2],
+                  c2 = stat[4 * b + 3];
+      const float2 xx = has_src ? __bfloat1622float2(
+                                      reinterpret_cast<const __nv_bfloat162*>(src + (int64_t)b * D)[jp])
+                                : make_float2(0.f, 0.f);
+      const float2 g = reinterpret_cast<const float2*>(da + (int64_t)b * D)[jp];
+      const float xh0 = (xx.x - mean) * rstd, xh1 = (xx.y - mean) * rstd;
+      dgam.x += g.x * xh0;
+      dgam.y += g.y * xh1;
+      dbet.x += g.x;
+      dbet.y += g.y;
+      if (has_src) {
+        float2* o = reinterpret_cast<float2*>(dst + (int64_t)b * D) + jp;
+        const float2 v = *o;
+        *o = make_float2(v.x + rstd * (g.x * gm.x - c1 - xh0 * c2),
+                         v.y + rstd * (g.y * gm.y - c1 - xh1 * c2));
+      }
+    }
+    float2* pw = reinterpret_cast<float2*>(dw) + jp;
+    float2* pb = reinterpret_cast<float2*>(db) + jp;
+    const float2 ow = *pw, ob = *pb;
+    *pw = make_float2(ow.x + dgam.x, ow.y + dgam.y);
+    *pb = make_float2(ob.x + dbet.x, ob.y + dbet.y);
   }
 }
 
@@ -901,7 +943,9 @@ int block_grid_bwd(const flb_block_weights* W, const void* x, const void* grids,
                            Di, Hi, eps, s)) != FLB_OK)
       return st;
     const dim3 ew_grid((unsigned)((D / 2 + 127) / 128), (unsigned)(n * Bi));
-    const dim3 cell_grid((unsigned)((D / 2 + 127) / 128), (unsigned)n);
+    // gate backward blocks: 32 feature pairs by up to 16 batch rows, one grid row per cell
+    const dim3 pair_grid((unsigned)((D / 2 + 31) / 32), (unsigned)n);
+    const dim3 pair_block(32, (unsigned)std::min<int64_t>(B, 16));
     if ((ce = launch_pdl(blk_bwd_out_kernel, ew_grid, dim3(128), 0, s, w.dG, per_port, ext3, g,
                          port_stride, w.f.lat, w.f.tok, w.d_o, w.d_top, w.d_lp, w.d_fp, T, l0,
                          Si, Bi, Di)) != cudaSuccess)
@@ -933,7 +977,7 @@ int block_grid_bwd(const flb_block_weights* W, const void* x, const void* grids,
                       3 * BD, G->w_qkv + (int64_t)l0 * 3 * DD, Di, 6 * DD, n, 1.f)) != FLB_OK)
       return st;
     // sensory gate
-    if ((ce = launch_pdl(blk_gx_bwd_kernel, cell_grid, dim3(128), 0, s, w.dT, w.f.zx, W->b_gate_x,
+    if ((ce = launch_pdl(blk_gx_bwd_kernel, pair_grid, pair_block, 0, s, w.dT, w.f.zx, W->b_gate_x,
                          g, xb, w.d_top, w.dG, dx, w.d_zx, w.d_lr, w.d_fp, G->b_gate_x, T, l0, Si,
                          Bi, Di)) != cudaSuccess)
       return check_cuda(ce, "block_grid_bwd launch");
@@ -945,7 +989,7 @@ int block_grid_bwd(const flb_block_weights* W, const void* x, const void* grids,
                       G->w_gate_x + (int64_t)l0 * DD, Di, 2 * DD, n, 1.f)) != FLB_OK)
       return st;
     // lateral gate
-    if ((ce = launch_pdl(blk_gl_bwd_kernel, cell_grid, dim3(128), 0, s, w.d_lr, w.f.zl,
+    if ((ce = launch_pdl(blk_gl_bwd_kernel, pair_grid, pair_block, 0, s, w.d_lr, w.f.zl,
                          W->b_gate_l, w.f.lat, w.d_lp, w.d_lp_h, w.d_zl, G->b_gate_l, l0, Bi,
                          Di)) != cudaSuccess)
       return check_cuda(ce, "block_grid_bwd launch");
@@ -975,7 +1019,7 @@ int block_grid_bwd(const flb_block_weights* W, const void* x, const void* grids,
     if ((st = gemm_rm(hs, true, false, Di, Di, Bi, w.d_fp_h, Di, BD, w.f.ln + n * BD, Di, BD,
                       G->w_prior_fdbk + (int64_t)l0 * DD, Di, 2 * DD, n, 1.f)) != FLB_OK)
       return st;
-    if ((ce = launch_pdl(blk_ln_bwd_kernel, dim3(2 * n), dim3(512), 2 * D * sizeof(float), s, g,
+    if ((ce = launch_pdl(blk_ln_bwd_kernel, dim3(2 * n), dim3(512), 4 * B * sizeof(float), s, g,
                          port_stride, w.dA, W->ln_lat_w, W->ln_fdbk_w, w.dG, per_port,
                          G->ln_lat_w, G->ln_lat_b, G->ln_fdbk_w, G->ln_fdbk_b, T, l0, n, Li, Si,
                          Bi, Di, eps)) != cudaSuccess)
