@@ -544,7 +544,8 @@ def run_profile_case(case: str):
     """A short, fixed workload for ncu: one warm-up step and one profiled step, no timing.
     attn: A2 attention forward (saving scores) + backward. grid: W4 grid layer forward +
     backward (64x64, batch 32, hidden 256). flb: the FLB model (12 layers, d768, batch 16) at
-    seq 64, bf16 inference forward through the native FLB cells."""
+    seq 64, bf16 inference forward through the native FLB cells. flb_train: the same model's
+    training step (forward, cross-entropy + aux, backward through the native FLB cells)."""
     device = torch.device("cuda", 0)
     if case == "attn":
         from kernels.additive_attention import attention_forward, attention_backward
@@ -552,7 +553,7 @@ def run_profile_case(case: str):
         for _ in range(2):
             out, lse, table, idx, sc = attention_forward(q, k, v, w, True, save_scores=True)
             attention_backward(q, k, v, w, out, lse, do, table, idx, True, scores=sc)
-    elif case == "flb":
+    elif case in ("flb", "flb_train"):
         from flb_model import FLBTransformer
         torch.manual_seed(0)
         m = FLBTransformer(32000, hidden_dim=768, num_layers=12, seq_len=64, batch_size=16)
@@ -560,11 +561,22 @@ def run_profile_case(case: str):
             for name, p in m.named_parameters():
                 if p.dim() >= 2 or name.endswith("v_a"):
                     p.normal_(0.0, 0.02)
-        m = m.to(device).eval()
         tok = torch.randint(0, 32000, (16, 64), device=device)
-        with torch.no_grad(), torch.autocast("cuda", dtype=torch.bfloat16):
+        if case == "flb":
+            m = m.to(device).eval()
+            with torch.no_grad(), torch.autocast("cuda", dtype=torch.bfloat16):
+                for _ in range(2):
+                    m(tok)
+        else:
+            m = m.to(device).train()
+            tgt = torch.randint(0, 32000, (16, 64), device=device)
             for _ in range(2):
-                m(tok)
+                m.zero_grad(set_to_none=True)
+                with torch.autocast("cuda", dtype=torch.bfloat16):
+                    logits, aux, _ = m(tok)
+                loss = torch.nn.functional.cross_entropy(logits.float().reshape(-1, 32000),
+                                                         tgt.reshape(-1)) + aux
+                loss.backward()
     else:
         from wavefront.grid_layer import wavefront_grid_layer, grid_inputs
         x, Wl, Wt, U, b, dh = grid_inputs(32, 64, 64, 256, device, seed=3)
@@ -583,7 +595,7 @@ def main():
     ap.add_argument("--impl", choices=["flb", "reference"], default="flb")
     ap.add_argument("--no-extras", action="store_true")
     ap.add_argument("--no-cpu-baseline", action="store_true")
-    ap.add_argument("--profile", choices=["attn", "grid", "flb"], default=None,
+    ap.add_argument("--profile", choices=["attn", "grid", "flb", "flb_train"], default=None,
                     help="run one fixed warm-up + profiled step for ncu and exit")
     args = ap.parse_args()
     if args.profile:
