@@ -269,11 +269,12 @@ constexpr size_t kBlkBlasWs = 32u << 20;
 
 struct BlockWs {
   bf16 *ln, *lat, *tok, *z, *qkv, *att, *o;
+  bf16* glpf;  // [L, D, D] folded lateral-gate weights G_L P_fb
   void* blas;
   void* blas_side;
 };
 
-size_t block_ws_layout(int64_t nmax, int64_t B, int64_t D, BlockWs* w, void* base) {
+size_t block_ws_layout(int64_t nmax, int64_t L, int64_t B, int64_t D, BlockWs* w, void* base) {
   auto al = [](size_t x) { return (x + 255) & ~(size_t)255; };
   const size_t rowb = (size_t)nmax * B * D * sizeof(bf16);
   size_t off = 0;
@@ -284,7 +285,8 @@ size_t block_ws_layout(int64_t nmax, int64_t B, int64_t D, BlockWs* w, void* bas
   };
   const size_t o_ln = take(2 * rowb), o_lat = take(rowb), o_tok = take(3 * rowb), o_z = take(rowb),
                o_qkv = take(9 * rowb), o_att = take(3 * rowb), o_o = take(3 * rowb),
-               o_blas = take(kBlkBlasWs), o_blas_side = take(kBlkBlasWs);
+               o_blas = take(kBlkBlasWs), o_blas_side = take(kBlkBlasWs),
+               o_glpf = take((size_t)L * D * D * sizeof(bf16));
   if (w && base) {
     uint8_t* p = reinterpret_cast<uint8_t*>(base);
     w->ln = (bf16*)(p + o_ln);
@@ -296,6 +298,7 @@ size_t block_ws_layout(int64_t nmax, int64_t B, int64_t D, BlockWs* w, void* bas
     w->o = (bf16*)(p + o_o);
     w->blas = p + o_blas;
     w->blas_side = p + o_blas_side;
+    w->glpf = (bf16*)(p + o_glpf);
   }
   return off;
 }
@@ -308,7 +311,7 @@ int64_t max_cells_per_tick(int64_t L, int64_t S) {
 }  // namespace
 
 size_t block_grid_workspace_bytes(int64_t L, int64_t S, int64_t B, int64_t D) {
-  return block_ws_layout(max_cells_per_tick(L, S), B, D, nullptr, nullptr);
+  return block_ws_layout(max_cells_per_tick(L, S), L, B, D, nullptr, nullptr);
 }
 
 namespace {
@@ -319,7 +322,8 @@ namespace {
 // until exit.
 struct SideStream {
   cudaStream_t s = nullptr;
-  cudaEvent_t fork[5] = {}, join = nullptr, fwd_fork = nullptr, fwd_join = nullptr;
+  cudaEvent_t fork[5] = {}, join = nullptr, fwd_fork = nullptr, fwd_join = nullptr,
+              fwd_join2 = nullptr;
 };
 
 int side_stream(SideStream** out) {
@@ -337,6 +341,7 @@ int side_stream(SideStream** out) {
     if (e == cudaSuccess) e = cudaEventCreateWithFlags(&ss.join, cudaEventDisableTiming);
     if (e == cudaSuccess) e = cudaEventCreateWithFlags(&ss.fwd_fork, cudaEventDisableTiming);
     if (e == cudaSuccess) e = cudaEventCreateWithFlags(&ss.fwd_join, cudaEventDisableTiming);
+    if (e == cudaSuccess) e = cudaEventCreateWithFlags(&ss.fwd_join2, cudaEventDisableTiming);
     if (e != cudaSuccess) {
       ss.s = nullptr;
       return check_cuda(e, "block_grid side stream");
@@ -360,9 +365,13 @@ struct Side {
   cublasHandle_t h;
 };
 
+// w_glpf: the per-layer products G_L P_fb [L, D, D] (inference), or null. With them the lateral
+// gate's pre-activation comes straight from the LayerNorm output, z_l = LN(diag) (G_L P_fb)^T,
+// and both priors run on the side stream next to it.
 int tick_forward(cublasHandle_t hb, const Side& side, const flb_block_weights* W, const bf16* xb,
                  const bf16* g, int64_t port_stride, const TickBufs& b, int T, int l0, int n,
-                 int L, int S, int B, int D, int H, float eps, cudaStream_t s) {
+                 int L, int S, int B, int D, int H, float eps, cudaStream_t s,
+                 const bf16* w_glpf = nullptr) {
   const long long DD = (long long)D * D, BD = (long long)B * D;
   int st;
   cudaError_t e = launch_pdl(blk_ln_kernel, dim3((2 * n * B + 7) / 8), dim3(256), 0, s,
@@ -384,13 +393,25 @@ int tick_forward(cublasHandle_t hb, const Side& side, const flb_block_weights* W
     return st;
   e = cudaEventRecord(side.ss->fwd_join, side.ss->s);
   if (e != cudaSuccess) return check_cuda(e, "block_grid tick join");
-  if ((st = gemm_rm(hb, false, true, B, D, D, b.ln + n * BD, D, BD, Wpf, D, 2 * DD, b.tok + 2 * D,
-                    3 * D, 3 * BD, n, 0.f, CUDA_R_16BF)) != FLB_OK)
-    return st;
-  // lateral gate
-  if ((st = gemm_rm(hb, false, true, B, D, D, b.tok + 2 * D, 3 * D, 3 * BD, Wgl, D, 2 * DD, b.zl, D,
-                    BD, n, 0.f, CUDA_R_16BF)) != FLB_OK)
-    return st;
+  if (w_glpf) {
+    // fdbk_prior on the side stream (first needed by the q|k|v GEMM); z_l from the folded weights
+    if ((st = gemm_rm(side.h, false, true, B, D, D, b.ln + n * BD, D, BD, Wpf, D, 2 * DD,
+                      b.tok + 2 * D, 3 * D, 3 * BD, n, 0.f, CUDA_R_16BF)) != FLB_OK)
+      return st;
+    e = cudaEventRecord(side.ss->fwd_join2, side.ss->s);
+    if (e != cudaSuccess) return check_cuda(e, "block_grid tick join");
+    if ((st = gemm_rm(hb, false, true, B, D, D, b.ln + n * BD, D, BD, w_glpf + (int64_t)l0 * DD, D,
+                      2 * DD, b.zl, D, BD, n, 0.f, CUDA_R_16BF)) != FLB_OK)
+      return st;
+  } else {
+    if ((st = gemm_rm(hb, false, true, B, D, D, b.ln + n * BD, D, BD, Wpf, D, 2 * DD, b.tok + 2 * D,
+                      3 * D, 3 * BD, n, 0.f, CUDA_R_16BF)) != FLB_OK)
+      return st;
+    // lateral gate
+    if ((st = gemm_rm(hb, false, true, B, D, D, b.tok + 2 * D, 3 * D, 3 * BD, Wgl, D, 2 * DD, b.zl,
+                      D, BD, n, 0.f, CUDA_R_16BF)) != FLB_OK)
+      return st;
+  }
   e = cudaStreamWaitEvent(s, side.ss->fwd_join, 0);
   if (e != cudaSuccess) return check_cuda(e, "block_grid tick join");
   const dim3 ew_grid((unsigned)((D / 2 + 127) / 128), (unsigned)(n * B));
@@ -404,6 +425,10 @@ int tick_forward(cublasHandle_t hb, const Side& side, const flb_block_weights* W
   e = launch_pdl(blk_gate_kernel, ew_grid, dim3(128), 0, s, b.zx, W->b_gate_x,
                  static_cast<const bf16*>(nullptr), g, xb, 1, b.tok, T, l0, S, B, D);
   if (e != cudaSuccess) return check_cuda(e, "block_grid gate launch");
+  if (w_glpf) {
+    e = cudaStreamWaitEvent(s, side.ss->fwd_join2, 0);
+    if (e != cudaSuccess) return check_cuda(e, "block_grid tick join");
+  }
   // q | k | v of the 3 tokens: [n, 3B, D] x [3D, D]^T
   if ((st = gemm_rm(hb, false, true, 3 * B, 3 * D, D, b.tok, D, 3 * BD, Wqkv, D, 6 * DD, b.qkv,
                     3 * D, 9 * BD, n, 0.f, CUDA_R_16BF)) != FLB_OK)
@@ -419,7 +444,7 @@ int block_grid_fwd(const flb_block_weights* W, const void* x, void* grids, int64
                    int64_t B, int64_t D, int64_t H, float eps, void* ws, size_t ws_bytes,
                    cudaStream_t s) {
   BlockWs w;
-  block_ws_layout(max_cells_per_tick(L, S), B, D, &w, ws);
+  block_ws_layout(max_cells_per_tick(L, S), L, B, D, &w, ws);
   cublasHandle_t hb;
   int st = blas(s, w.blas, kBlkBlasWs, &hb);
   if (st != FLB_OK) return st;
@@ -433,13 +458,17 @@ int block_grid_fwd(const flb_block_weights* W, const void* x, void* grids, int64
   const int Li = (int)L, Si = (int)S, Bi = (int)B, Di = (int)D, Hi = (int)H;
   const int ticks = (int)(L + 2 * S - 2);
   const TickBufs tb{w.ln, w.lat, w.tok, w.z, w.z, w.qkv, w.att};
+  // inference: fold the lateral gate onto the feedback prior once per call, G_L P_fb per layer
+  if ((st = gemm_rm(hb, false, false, Di, Di, Di, W->w_gate_l, Di, DD, W->w_prior_fdbk, Di, DD,
+                    w.glpf, Di, DD, Li, 0.f, CUDA_R_16BF)) != FLB_OK)
+    return st;
   int launches = 0;
   for (int T = 0; T < ticks; ++T) {
     const Tick tk = tick_of(T, Li, Si);
     const int n = tk.n, l0 = tk.l0;
     if (n == 0) continue;
     if ((st = tick_forward(hb, side, W, xb, g, port_stride, tb, T, l0, n, Li, Si, Bi, Di, Hi, eps,
-                           s)) != FLB_OK)
+                           s, w.glpf)) != FLB_OK)
       return st;
     const bf16* Wo = reinterpret_cast<const bf16*>(W->w_o) + (int64_t)l0 * DD;
     if ((st = gemm_rm(hb, false, true, 3 * Bi, Di, Di, w.att, Di, 3 * BD, Wo, Di, 2 * DD, w.o, Di,
