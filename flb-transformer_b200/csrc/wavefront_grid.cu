@@ -285,7 +285,9 @@ grid_sweep_kernel(const __grid_constant__ CUtensorMap tmWa, const __grid_constan
               issue_left();
             }
           }
-          if (!tready) {
+          // a band's halo flags are polled at system scope, which costs far more per load:
+          // only once the same-row input is in
+          if (!tready && !(halo_in && !lready)) {
             bool set = true;
             for (int hh = 0; hh < NH; ++hh)
               set &= halo_in ? ld_acquire_sys(hflag + hh) == p.epoch : ld_acquire(tflag + hh) == 1;
