@@ -1,7 +1,7 @@
 """Benchmark of the FLB hot paths on B200.
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl flb|reference]
-                    [--workload attn_a2|attn_a3|grid_w4] [--no-extras]
+                    [--no-extras] [--no-cpu-baseline] [--profile attn|grid|flb|flb_train]
 
 Headline workload (attn_a2): fused additive attention forward + backward, bf16 inputs with fp32
 accumulation, causal, B=8 H=16 N=2048 D=64 per GPU; Q,K,V ~ N(0,1), w ~ N(0,1/D), dO ~ N(0,1),
@@ -248,6 +248,25 @@ class HostPipeline:
             fn()
 
 
+def profile_traffic(summary: str):
+    """dram__bytes_read.sum + dram__bytes_write.sum (bytes) from a committed ncu summary table
+    under profiles/, or None when the summary lacks them."""
+    units = {"B": 1.0, "KB": 1e3, "MB": 1e6, "GB": 1e9, "byte": 1.0, "Kbyte": 1e3,
+             "Mbyte": 1e6, "Gbyte": 1e9}
+    total, seen = 0.0, 0
+    try:
+        with open(os.path.join(REPO, "profiles", summary)) as f:
+            for line in f:
+                cells = [c.strip() for c in line.strip().strip("|").split("|")]
+                if len(cells) >= 2 and cells[0] in ("dram__bytes_read.sum", "dram__bytes_write.sum"):
+                    num, unit = cells[1].split()[:2]
+                    total += float(num) * units[unit]
+                    seen += 1
+    except (OSError, ValueError, KeyError):
+        return None
+    return total if seen == 2 else None
+
+
 def time_steps(fn, steps, world):
     barrier(world)
     torch.cuda.synchronize()
@@ -292,6 +311,32 @@ def extra_long_context(device, steps=3, warmup=1):
     p = pairs_of(A3)
     return {"workload": "attn fwd B4 H8 N8192 D128 bf16 causal", "ms": round(ms, 3),
             "pairs_per_s": p / (ms * 1e-3), "tanh_per_s": p * A3["D"] / (ms * 1e-3)}
+
+
+def a3_sharded(world, rank, device, steps=3, warmup=2):
+    """The long-context configuration (B4 H8 N8192 D128 bf16 causal, forward) split over the
+    ranks by (batch, head) units: 32 units -> 32/world per rank, no collective on the data path
+    (strong scaling: total work fixed). Every rank draws the same seeded inputs and keeps its
+    own units; time = max over ranks (CUDA events, barrier + synchronize on both sides)."""
+    from kernels.additive_attention import attention_forward
+    from kernels.sharding import shard_batch_heads, head_index_of_units
+    B, H, N, D = A3["B"], A3["H"], A3["N"], A3["D"]
+    g = torch.Generator().manual_seed(11)
+    q, k, v = (torch.randn(B, H, N, D, generator=g).to(torch.bfloat16) for _ in range(3))
+    w = (torch.randn(H, 1, D, generator=g) / math.sqrt(D)).to(torch.bfloat16)
+    qs, ks, vs = (shard_batch_heads(t, rank, world).contiguous().to(device) for t in (q, k, v))
+    ws = w[head_index_of_units(B, H, rank, world)].reshape(-1, 1, 1, D).to(device)
+    del q, k, v
+
+    def fwd():
+        attention_forward(qs, ks, vs, ws, True)
+    for _ in range(warmup):
+        fwd()
+    ms = time_steps(fwd, steps, world) / steps
+    return {"workload": "attn fwd B4 H8 N8192 D128 bf16 causal, (batch,head) units split over "
+                        f"{world} GPU(s)", "units_per_rank": int(qs.shape[0]),
+            "ms": round(ms, 3), "pairs_per_s": pairs_of(A3) / (ms * 1e-3),
+            "scaling": "strong"}
 
 
 def extra_grid(device, steps=3, warmup=1, with_cpu=True):
@@ -354,38 +399,155 @@ def extra_engine(device, steps=2, warmup=1):
     tick = nn.ModuleList([TickCell(H) for _ in range(R)]).to(device)
     tick.load_state_dict(fast.state_dict())
     x = torch.randn(B, C, H, device=device).bfloat16()
-    res = {}
+    res, fast_out = {}, None
     for name, layers, n in (("persistent", fast, steps), ("per_diagonal", tick, 1),
                             ("per_diagonal_graphed", tick, steps)):
         eng = WavefrontEngine(cfg, layers).to(device)
         run = eng.graphed(x) if name == "per_diagonal_graphed" else eng
 
         def step():
+            layers.zero_grad(set_to_none=True)
             xx = x.detach().requires_grad_(True)
             g = run(xx)
             (g[0].float().sum() + g[1][-1].float().sum()).backward()
+            return g[0].detach(), xx.grad
         for _ in range(warmup):
             step()
         res[name] = time_steps(step, n, 1) / n
-    return {"workload": "WavefrontEngine 64x64 per-row tanh cells, batch32 hidden256 bf16 fwd+bwd",
-            "persistent_ms": round(res["persistent"], 3),
-            "per_diagonal_ms": round(res["per_diagonal"], 3),
-            "per_diagonal_graphed_ms": round(res["per_diagonal_graphed"], 3),
-            "speedup": res["per_diagonal"] / res["persistent"],
-            "graph_speedup": res["per_diagonal"] / res["per_diagonal_graphed"],
-            "cells_per_s": R * C / (res["persistent"] * 1e-3)}
+        if name == "persistent":
+            h, gx = step()
+            fast_out = {"h": h.float().cpu(), "x_grad": gx.float().cpu(),
+                        "grads": {k: p.grad.float().cpu() for k, p in layers.named_parameters()}}
+    out = {"workload": "WavefrontEngine 64x64 per-row tanh cells, batch32 hidden256 bf16 fwd+bwd",
+           "persistent_ms": round(res["persistent"], 3),
+           "per_diagonal_ms": round(res["per_diagonal"], 3),
+           "per_diagonal_graphed_ms": round(res["per_diagonal_graphed"], 3),
+           "speedup": res["per_diagonal"] / res["persistent"],
+           "graph_speedup": res["per_diagonal"] / res["per_diagonal_graphed"],
+           "cells_per_s": R * C / (res["persistent"] * 1e-3)}
+    ref = reference_engine_timing(cfg, fast, x, fast_out, device)
+    out["reference_engine"] = ref
+    if "ms" in ref:
+        out["reference_per_diagonal_ms"] = ref["ms"]
+        out["speedup_vs_reference_engine"] = ref["ms"] / res["persistent"]
+    return out
 
 
-def extra_flb_e2e(device, steps=3, decode_steps=8):
-    """The FLB model end to end: 12 layers, d_model 768 (8 heads of additive attention per
-    cell, as FLB_Block fixes), vocab 32000, weights ~ N(0, 0.02), a 16 x 1024 prompt of uniform
+REF_DIR = os.path.join(REPO, "baseline", "_ref")
+
+
+def reference_engine_timing(cfg, layers, x, fast_out, device, steps=2, warmup=1):
+    """The reference's own engine (baseline/_ref: its WavefrontEngine with the Triton gather,
+    the vmapped cell, its C++ tick loop built from its csrc/) on the same grid, weights and
+    input, timed in a child process (its packages share names with this one's). Returns its
+    fwd+bwd time per step (CUDA events) and how its outputs compare with the persistent
+    kernel's (h: max-abs excess over 2e-2 + half a bf16 ulp; gradients: max-abs error relative
+    to the tensor's largest magnitude)."""
+    import tempfile
+    if not os.path.isdir(os.path.join(REF_DIR, "wavefront")):
+        return {"unavailable": "reference not installed under baseline/_ref"}
+    with tempfile.TemporaryDirectory() as tmp:
+        fin, fout = os.path.join(tmp, "in.pt"), os.path.join(tmp, "out.pt")
+        torch.save({"grid": list(cfg.grid_shape), "batch": cfg.batch_size, "dim": cfg.dim,
+                    "state": {k: v.cpu() for k, v in layers.state_dict().items()},
+                    "x": x.cpu()}, fin)
+        env = dict(os.environ)
+        env["CUDA_VISIBLE_DEVICES"] = env.get("CUDA_VISIBLE_DEVICES", str(device.index or 0))
+        cmd = [sys.executable, os.path.abspath(__file__), "--ref-engine", fin, fout,
+               "--steps", str(steps), "--warmup", str(warmup)]
+        try:
+            r = subprocess.run(cmd, stdout=subprocess.PIPE, stderr=subprocess.STDOUT, text=True,
+                               timeout=900, env=env)
+        except subprocess.TimeoutExpired:
+            return {"unavailable": "reference engine run exceeded 900 s"}
+        if r.returncode != 0 or not os.path.exists(fout):
+            tail = " | ".join(r.stdout.strip().splitlines()[-3:])
+            return {"unavailable": f"reference engine run failed (rc {r.returncode}): {tail}"}
+        got = torch.load(fout, weights_only=False)
+    res = {"ms": round(got["ms"], 3), "mode": got["mode"], "steps": steps}
+    if fast_out is not None:
+        h, hr = fast_out["h"].double(), got["h"].double()
+        res["h_excess"] = ((h - hr).abs() - (2e-2 + 2.0 ** -8 * hr.abs())).max().item()
+        rel = lambda a, b: ((a.double() - b.double()).abs().max()
+                            / max(1.0, b.double().abs().max().item())).item()
+        res["x_grad_rel"] = rel(fast_out["x_grad"], got["x_grad"])
+        res["param_grad_rel"] = {k: rel(v, got["grads"][k]) for k, v in fast_out["grads"].items()}
+        res["within_tolerance"] = bool(res["h_excess"] <= 0 and res["x_grad_rel"] < 2e-2 and
+                                       all(v < 2e-2 for v in res["param_grad_rel"].values()))
+    return res
+
+
+def run_ref_engine(fin, fout, steps, warmup):
+    """Child process of reference_engine_timing: imports the reference's packages from
+    baseline/_ref (none of this package's modules), builds its WavefrontEngine on the given
+    configuration with a per-row tanh cell of the same parameters, and times forward + backward
+    through its public module API and stock code path."""
+    sys.path[:] = [p for p in sys.path if os.path.abspath(p) != os.path.abspath(PKG)]
+    sys.path.insert(0, REF_DIR)
+    import torch.nn as nn
+    import wavefront.wavefront_engine as wfe
+    from wavefront.wavefront_api import WavefrontConfig
+    assert os.path.abspath(wfe.__file__).startswith(os.path.abspath(REF_DIR)), wfe.__file__
+    inp = torch.load(fin, weights_only=False)
+    R, C = inp["grid"]
+    H = inp["dim"]
+
+    class RefTanhCell(nn.Module):  # the cell equation of the benchmark grid, reference form
+        def __init__(self, dim):
+            super().__init__()
+            self.W_l = nn.Parameter(torch.empty(dim, dim))
+            self.W_t = nn.Parameter(torch.empty(dim, dim))
+            self.b = nn.Parameter(torch.empty(dim))
+
+        def forward(self, top, left):
+            h = torch.tanh(left @ self.W_l.T + top @ self.W_t.T + self.b)
+            return h, h
+
+    device = torch.device("cuda", 0)
+    layers = nn.ModuleList([RefTanhCell(H) for _ in range(R)])
+    layers.load_state_dict(inp["state"])
+    layers = layers.to(device)
+    x = inp["x"].to(device)
+    cfg = WavefrontConfig(grid_shape=(R, C), batch_size=inp["batch"], dim=H)
+    eng = wfe.WavefrontEngine(cfg, layers).to(device)
+
+    def step():
+        layers.zero_grad(set_to_none=True)
+        xx = x.detach().requires_grad_(True)
+        g = eng(xx)
+        (g[0].float().sum() + g[1][-1].float().sum()).backward()
+        return g[0].detach(), xx.grad
+
+    mode = "stock"
+    try:
+        step()
+    except Exception as e:  # noqa: BLE001
+        # its compiled vjp (torch.compile, aot_eager) can fail to trace on some torch versions;
+        # force_eager runs the same eager ATen ops without tracing
+        print(f"stock backward failed ({type(e).__name__}: {e}); retrying with force_eager",
+              file=sys.stderr)
+        torch.compiler.set_stance("force_eager")
+        mode = "force_eager"
+        eng = wfe.WavefrontEngine(cfg, layers).to(device)
+        step()
+    for _ in range(max(0, warmup - 1)):
+        step()
+    ms = time_steps(step, steps, 1) / steps
+    h, gx = step()
+    torch.save({"ms": ms, "mode": mode, "h": h.float().cpu(), "x_grad": gx.float().cpu(),
+                "grads": {k: p.grad.float().cpu() for k, p in layers.named_parameters()}}, fout)
+
+
+def extra_flb_e2e(device, steps=3, decode_steps=256):
+    """The FLB model end to end: 12 layers, d_model 768, 12 heads of additive attention per
+    cell (head dim 64), vocab 32000, weights ~ N(0, 0.02), a 16 x 1024 prompt of uniform
     token ids; bf16 autocast. The grid runs as the native FLB cells replayed as CUDA graphs:
     the inference forward, greedy decode steps (each re-runs the sliding 1024-token window: the
     model carries no usable context) and a training step (cross-entropy + aux, backward)."""
     from flb_model import FLBTransformer, greedy_decode
     V, D, L, S, B = 32000, 768, 12, 1024, 16
     torch.manual_seed(0)
-    m = FLBTransformer(V, hidden_dim=D, num_layers=L, seq_len=S, batch_size=B)
+    m = FLBTransformer(V, hidden_dim=D, num_layers=L, seq_len=S, batch_size=B, num_heads=12)
     with torch.no_grad():
         for name, p in m.named_parameters():
             if p.dim() >= 2 or name.endswith("v_a"):
@@ -421,7 +583,8 @@ def extra_flb_e2e(device, steps=3, decode_steps=8):
         loss.backward()
     train_step()
     train_ms = time_steps(train_step, steps, 1) / steps
-    return {"workload": "FLB model 12 layers d768 vocab32000, prompt 16x1024, bf16",
+    return {"workload": "FLB model 12 layers d768 12 heads vocab32000, prompt 16x1024, "
+                        f"{decode_steps} greedy decode steps, bf16",
             "native_cells": bool(gt.native_flb), "capture_s": round(capture_s, 2),
             "forward_ms": round(fwd_ms, 2), "cells_per_s": L * S / (fwd_ms * 1e-3),
             "prompt_tokens_per_s": B * S / (fwd_ms * 1e-3),
@@ -461,12 +624,16 @@ def run_flb(args):
     torch.cuda.synchronize()
     d2h = pipe.d2h_bytes
     ms_e2e = time_steps(pipe.step_fn(args.steps), args.steps, world) / args.steps
+    del pipe
+    # the long-context configuration split over the ranks (every rank takes part)
+    a3 = a3_sharded(world, rank, device)
 
     # roofline: dominant launch against the measured MUFU tanh rate
     tanh_peak = nat.microbench(0, device)
-    # DRAM bytes per launch (dram__bytes_read.sum + dram__bytes_write.sum) from an ncu capture of
-    # `bench.py --profile attn` on B200; the launches of this workload move the same bytes.
-    traffic = {"forward": 485.8e6 + 1071.1e6, "backward": 2121.4e6 + 500.8e6}
+    # DRAM bytes per launch (dram__bytes_read.sum + dram__bytes_write.sum) from the committed ncu
+    # summaries of `bench.py --profile attn` (the same launches as this workload)
+    traffic = {"forward": profile_traffic("attn_fwd_tc_a2.md"),
+               "backward": profile_traffic("attn_bwd_tc_a2.md")}
     tanh_work = pairs_of(cfg) * cfg["D"]
     dom = "backward" if bwd_ms >= fwd_ms else "forward"
     dom_ms = max(bwd_ms, fwd_ms)
@@ -492,6 +659,7 @@ def run_flb(args):
                      "traffic": traffic[dom],
                      "algorithmic_tanh_per_launch": tanh_work},
         "clocks": clk.summary(),
+        "a3_sharded": a3,
     }
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         cps, sample, threads = cpu_attention_sample(cfg)
@@ -597,8 +765,12 @@ def main():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--profile", choices=["attn", "grid", "flb", "flb_train"], default=None,
                     help="run one fixed warm-up + profiled step for ncu and exit")
+    ap.add_argument("--ref-engine", nargs=2, metavar=("IN", "OUT"), default=None,
+                    help=argparse.SUPPRESS)  # child process of reference_engine_timing
     args = ap.parse_args()
-    if args.profile:
+    if args.ref_engine:
+        run_ref_engine(args.ref_engine[0], args.ref_engine[1], args.steps, args.warmup)
+    elif args.profile:
         run_profile_case(args.profile)
     elif args.impl == "reference":
         run_reference(args)

@@ -441,13 +441,8 @@ int launch_fwd_tc(const void* q, const void* k, const void* v, const float* w, c
   if (st != FLB_OK) return st;
   st = make_tmap(&tmV, v, dt, 3, dims, strides, boxV, CU_TENSOR_MAP_SWIZZLE_128B);
   if (st != FLB_OK) return st;
-  static bool attr_set = false;
-  if (!attr_set) {
-    cudaError_t e = cudaFuncSetAttribute(attn_fwd_tc_kernel<D, T>,
-                                         cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM);
-    if (e != cudaSuccess) return check_cuda(e, "attn_fwd_tc smem attribute");
-    attr_set = true;
-  }
+  st = ensure_dyn_smem((const void*)attn_fwd_tc_kernel<D, T>, C::SMEM, "attn_fwd_tc smem attribute");
+  if (st != FLB_OK) return st;
   const unsigned grid = (unsigned)(((N + C::BM - 1) / C::BM) * BH);
   // vector score stores (8 / TPR floats) need an aligned base (rows are padded to 16 bytes)
   const int kpt = 8 / C::TPR;
@@ -1010,13 +1005,8 @@ int launch_bwd_tc(const void* q, const void* k, const void* v, const float* w, c
   const int64_t rows = BH * N;
   bwd_prep_kernel<T><<<(unsigned)((rows + 7) / 8), 256, 0, s>>>((const T*)o, (const T*)dout, delta,
                                                                 dq_acc, rows);
-  static bool attr_set = false;
-  if (!attr_set) {
-    e = cudaFuncSetAttribute(attn_bwd_tc_kernel<T>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                             C::SMEM);
-    if (e != cudaSuccess) return check_cuda(e, "attn_bwd_tc smem attribute");
-    attr_set = true;
-  }
+  st = ensure_dyn_smem((const void*)attn_bwd_tc_kernel<T>, C::SMEM, "attn_bwd_tc smem attribute");
+  if (st != FLB_OK) return st;
   const unsigned grid = (unsigned)(((N + C::BN - 1) / C::BN) * BH);
   attn_bwd_tc_kernel<T><<<grid, 512, C::SMEM, s>>>(tmQ, tmDO, tmV, tmSC, (const T*)k, w, wi, lse,
                                                    delta, dq_acc, (T*)dk, (T*)dv, dw, N, causal,

@@ -1,6 +1,8 @@
 // extern "C" boundary of libflb_b200.so: argument validation, dispatch to the kernels, status
 // codes and the thread-local error message.
 #include <atomic>
+#include <map>
+#include <mutex>
 #include <string>
 #include "common.cuh"
 
@@ -20,6 +22,21 @@ int check_cuda(cudaError_t e, const char* what) {
   if (e == cudaSuccess) return FLB_OK;
   g_last_error = std::string(what) + ": " + cudaGetErrorString(e);
   return FLB_ERR_CUDA;
+}
+
+int ensure_dyn_smem(const void* kernel, int bytes, const char* what) {
+  static std::mutex mu;
+  static std::map<std::pair<int, const void*>, int> done;  // (device, kernel) -> bytes set
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return check_cuda(e, what);
+  std::lock_guard<std::mutex> lock(mu);
+  auto it = done.find({dev, kernel});
+  if (it != done.end() && it->second >= bytes) return FLB_OK;
+  e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);
+  if (e != cudaSuccess) return check_cuda(e, what);
+  done[{dev, kernel}] = bytes;
+  return FLB_OK;
 }
 
 // kernels (defined in the other translation units)

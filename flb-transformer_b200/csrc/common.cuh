@@ -17,6 +17,11 @@ int check_cuda(cudaError_t e, const char* what);
 
 inline cudaStream_t as_stream(void* s) { return reinterpret_cast<cudaStream_t>(s); }
 
+// Raises a kernel's dynamic shared-memory limit to `bytes` on the CURRENT device. The attribute
+// belongs to the device's context, so it is set once per (device, kernel) and remembered under a
+// lock (host threads may launch on different devices at once).
+int ensure_dyn_smem(const void* kernel, int bytes, const char* what);
+
 inline int dtype_size(int dtype) {
   switch (dtype) {
     case FLB_F32: return 4;
@@ -30,15 +35,13 @@ inline int dtype_size(int dtype) {
 // stride alignment TMA needs.
 __host__ __device__ inline int64_t attn_scores_ld(int64_t N) { return (N + 3) & ~(int64_t)3; }
 
+// SM count of the current device (a cheap attribute query, so no cache that could go stale when a
+// process drives several devices)
 inline int num_sms() {
-  static int n = 0;
-  if (n == 0) {
-    int dev = 0;
-    cudaGetDevice(&dev);
-    cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev);
-    if (n <= 0) n = 148;
-  }
-  return n;
+  int dev = 0, n = 0;
+  cudaGetDevice(&dev);
+  cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev);
+  return n > 0 ? n : 148;
 }
 
 // ---- device-side dtype access ------------------------------------------------------------

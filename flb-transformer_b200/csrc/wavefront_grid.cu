@@ -299,7 +299,9 @@ grid_sweep_kernel(const __grid_constant__ CUtensorMap tmWa, const __grid_constan
           if (i > 64) __nanosleep(64);
         }
         if (!(lready && tready)) {  // gave up: record it, keep the barrier phases in step
-          atomicExch(p.err, halo_in && !tready ? 6 : 2);
+          // 2: a same-grid flag never came (an edge row polls its halo only once the same-row
+          // input is in, so a same-row timeout must not be reported as a halo timeout); 6: halo
+          atomicExch(p.err, (!lready || !halo_in) ? 2 : 6);
           if (!lready) issue_left();
           if (!tready) issue_top();
         }
@@ -502,14 +504,9 @@ int launch_sweep(const CUtensorMap& wa, const CUtensorMap& wb, const CUtensorMap
                  const CUtensorMap& top, const CUtensorMap& e1, const CUtensorMap& e2,
                  const CUtensorMap& save, const GridParams& p, cudaStream_t s, int* grid_ctas) {
   const int smem = GridCfg<H>::smem(p.B, p.ep_stages);
-  static bool attr = false;
-  if (!attr) {
-    cudaError_t e = cudaFuncSetAttribute(grid_sweep_kernel<H>,
-                                         cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                         GridCfg<H>::kMaxDynSmem);
-    if (e != cudaSuccess) return check_cuda(e, "grid_sweep smem attribute");
-    attr = true;
-  }
+  int st = ensure_dyn_smem((const void*)grid_sweep_kernel<H>, GridCfg<H>::kMaxDynSmem,
+                           "grid_sweep smem attribute");
+  if (st != FLB_OK) return st;
   int per_sm = 0;
   cudaError_t e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, grid_sweep_kernel<H>, 128, smem);
   if (e != cudaSuccess || per_sm < 1) return fail(FLB_ERR_LAUNCH, "grid_sweep: kernel does not fit on an SM");

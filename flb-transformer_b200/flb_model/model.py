@@ -62,13 +62,16 @@ class FLBAttentionLayer(nn.Module):
 
 
 class FLBBlock(nn.Module):
-    def __init__(self, hidden_dim: int, dropout: float = 0.1):
+    """FLB_Block (models/FLB_Model.py:64-96). The reference fixes 8 attention heads (:73);
+    num_heads (default 8) makes the head count a constructor argument."""
+
+    def __init__(self, hidden_dim: int, dropout: float = 0.1, num_heads: int = 8):
         super().__init__()
         self.norm_lat = nn.LayerNorm(hidden_dim)
         self.norm_fdbk = nn.LayerNorm(hidden_dim)
         self.proj_lateral = nn.Linear(hidden_dim, hidden_dim, bias=False)
         self.proj_feedback = nn.Linear(hidden_dim, hidden_dim, bias=False)
-        self.flb_attention = FLBAttentionLayer(hidden_dim, num_heads=8, dropout=dropout)
+        self.flb_attention = FLBAttentionLayer(hidden_dim, num_heads=num_heads, dropout=dropout)
 
     def forward(self, x_input, prev_lat, prev_fdbk):
         b, cells, dim = x_input.shape
@@ -87,7 +90,7 @@ FLB_DEPENDENCIES = [((-1, 0), 0), ((0, -1), 1), ((1, -1), 2)]
 class FLBTransformer(nn.Module):
     def __init__(self, vocab_size: int, hidden_dim: int = 256, num_layers: int = 6,
                  seq_len: int = 128, batch_size: int = 32, dropout: float = 0.1,
-                 aux_weight: float = 0.05):
+                 aux_weight: float = 0.05, num_heads: int = 8):
         super().__init__()
         self.aux_weight = aux_weight
         self.embedding = nn.Embedding(vocab_size, hidden_dim)
@@ -95,7 +98,8 @@ class FLBTransformer(nn.Module):
         self.out_dropout = nn.Dropout(dropout)
         self.config = WavefrontConfig(grid_shape=(num_layers, seq_len), batch_size=batch_size,
                                       dim=hidden_dim, dependencies=FLB_DEPENDENCIES, num_ports=4)
-        self.layers = nn.ModuleList([FLBBlock(hidden_dim, dropout) for _ in range(num_layers)])
+        self.layers = nn.ModuleList([FLBBlock(hidden_dim, dropout, num_heads)
+                                     for _ in range(num_layers)])
         self.engine = WavefrontEngine(self.config, self.layers)
         self.head = nn.Linear(hidden_dim, vocab_size)
 

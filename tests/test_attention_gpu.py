@@ -104,24 +104,97 @@ def test_half_precision(cuda, dtype, N, D, causal):
         assert excess_half(a, b) <= 0
 
 
-def test_a2_config_sampled_heads(cuda):
-    """B8 H16 N2048 D64 bf16 causal, forward + backward on the GPU; parity checked on sampled
-    (batch, head) slices against the oracle (the full tensor grid does not fit the oracle)."""
+A2_SLICES = ((0, 0), (3, 9), (7, 15))
+
+
+@pytest.fixture(scope="module")
+def a2_run(cuda):
+    """B8 H16 N2048 D64 bf16 causal: one forward + backward of the whole configuration on the
+    GPU (the launch the benchmark times), kept for the parity checks below."""
     B, H, N, D = 8, 16, 2048, 64
     q, k, v, w, g = oa.make_inputs(B, H, N, D, seed=0, with_grad_out=True, dtype=torch.bfloat16)
     out, grads = run(*(t.to(cuda) for t in (q, k, v, w)), dout=g.to(cuda), causal=True)
+    return (q, k, v, w, g), out.cpu(), [t.cpu() for t in grads]
+
+
+def test_a2_config_sampled_heads(a2_run):
+    """Forward output and every input gradient of the full A2 launch, checked on three sampled
+    (batch, head) slices (first, middle, last) against the oracle (the full tensors do not fit
+    the oracle's memory; the slices are whole: every query row and key of the unit)."""
+    (q, k, v, w, g), out, grads = a2_run
     assert torch.isfinite(out.float()).all()
-    for b, h in ((0, 0), (7, 15)):
+    for b, h in A2_SLICES:
         sl = lambda t: t[b:b + 1, h:h + 1]
         ref = oa.attention_forward(sl(q), sl(k), sl(v), w[h:h + 1], causal=True, row_chunk=256)[0]
-        assert excess_half(sl(out), ref) <= 0
-    b, h = 3, 9
-    sl = lambda t: t[b:b + 1, h:h + 1]
-    rq, rk, rv, _ = oa.attention_backward(sl(q), sl(k), sl(v), w[h:h + 1], sl(g), causal=True,
-                                          dtype=torch.float32)
-    for a, r in zip(grads[:3], (rq, rk, rv)):
-        assert excess_half(sl(a), r) <= 0
-    assert torch.isfinite(grads[3]).all()
+        assert excess_half(sl(out), ref) <= 0, (b, h)
+        rq, rk, rv, _ = oa.attention_backward(sl(q), sl(k), sl(v), w[h:h + 1], sl(g),
+                                              causal=True, dtype=torch.float32, row_chunk=64)
+        for name, a, r in zip(("dq", "dk", "dv"), grads[:3], (rq, rk, rv)):
+            assert excess_half(sl(a), r) <= 0, (name, b, h)
+
+
+def test_a2_dv_a_all_units(a2_run):
+    """dv_a is the one reduction across (batch, head) units: each head's row of the gradient
+    sums the contributions of all 8 batch elements (atomics from every key block of every unit
+    in the kernel). Checked against the oracle's grad_va evaluated on the host in float32 for
+    all 128 units; bf16 output, so the bound is 2e-2 plus half a bf16 ulp of the value."""
+    (q, k, v, w, g), _, grads = a2_run
+    B, H = q.shape[:2]
+    ref = torch.zeros(H, 1, q.shape[-1], dtype=torch.float64)
+    for b in range(B):
+        for h in range(H):
+            sl = lambda t: t[b:b + 1, h:h + 1]
+            ref[h] += oa.attention_backward(sl(q), sl(k), sl(v), w[h:h + 1], sl(g), causal=True,
+                                            dtype=torch.float32, row_chunk=64)[3][0].double()
+    dva = grads[3]
+    assert dva.shape == w.shape and dva.dtype == w.dtype
+    assert excess_half(dva, ref) <= 0
+    # the quantity is not trivially small: a wrong reduction would show
+    assert ref.abs().max().item() > 0.1
+
+
+A3_RESCALE_HEAD = 5
+A3_SLICES = ((0, 0), (3, 7), (1, A3_RESCALE_HEAD))
+A3_ROWS = ((0, 128), (4032, 4160), (8064, 8192))
+
+
+def test_a3_config_sampled_rows(cuda):
+    """Long-context configuration B4 H8 N8192 D128 bf16 causal, forward, the whole launch on the
+    GPU; output and lse checked against the oracle on the first, a middle and the last 128 query
+    rows of three (batch, head) slices (each softmax row is independent, so sampled rows are
+    exact checks). Head 5's score vector is scaled to w_std = 3.5 (sum|w|/sqrt(D) ~ 33, scores
+    ~ 8 log2 units apart within a row) so that later keys exceed a row's first-group maximum by
+    more than the kernel's rescale threshold: that slice runs the accumulator-rescale path, and
+    the test asserts on the oracle's scores that its sampled rows do. Bound: 2e-2 plus half a
+    bf16 ulp; for the scaled head 5e-2 (score errors grow with sum|w|, as in
+    test_large_weights_stable at the same sum|w|/sqrt(D)). lse: 1e-2 absolute."""
+    from kernels.additive_attention import attention_forward
+    B, H, N, D = 4, 8, 8192, 128
+    q, k, v, w = oa.make_inputs(B, H, N, D, seed=7, dtype=torch.bfloat16)
+    w = w.clone()
+    gw = torch.Generator().manual_seed(70)
+    w[A3_RESCALE_HEAD] = (torch.randn(1, D, generator=gw) * 3.5).bfloat16()
+    out, lse, _, _, _ = attention_forward(*(t.to(cuda) for t in (q, k, v, w)), True)
+    out, lse = out.cpu(), lse.view(B, H, N).cpu()
+    assert torch.isfinite(out.float()).all()
+    rescaled_rows = 0
+    for b, h in A3_SLICES:
+        sl = lambda t: t[b:b + 1, h:h + 1]
+        tol = 5e-2 if h == A3_RESCALE_HEAD else TOL_HALF
+        for r0, r1 in A3_ROWS:
+            ref_o, ref_l = oa.attention_forward(sl(q), sl(k), sl(v), w[h:h + 1], causal=True,
+                                                row_range=(r0, r1), row_chunk=32)
+            got = out[b, h, r0:r1].double()
+            excess = ((got - ref_o[0, 0]).abs() - (tol + 2.0 ** -8 * ref_o[0, 0].abs())).max()
+            assert excess.item() <= 0, (b, h, r0)
+            assert maxdiff(lse[b, h, r0:r1], ref_l[0, 0]) < 1e-2, (b, h, r0)
+            if h == A3_RESCALE_HEAD:
+                s2 = oa.attention_scores(sl(q), sl(k), w[h:h + 1], causal=True,
+                                         row_range=(r0, r1), dtype=torch.float32)[0, 0]
+                s2 = s2 * 1.4426950408889634  # log2 units, as the kernel compares
+                first = s2[:, :8].max(dim=-1).values
+                rescaled_rows += int((s2.max(dim=-1).values > first + 8.0).sum())
+    assert rescaled_rows > 0, "the rescale path was not exercised"
 
 
 def test_v_a_broadcast_shapes(cuda):

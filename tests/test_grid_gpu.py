@@ -143,7 +143,11 @@ def test_bounded_wait_reports_timeout(cuda):
                                              R, C, B, H, 1, ws.data_ptr(), ws_bytes, 1, 1, 20000,
                                              nat.stream_of(h))
     assert st == 4  # FLB_ERR_TIMEOUT
-    assert "gave up" in nat.lib.flb_last_error().decode()
+    msg = nat.lib.flb_last_error().decode()
+    assert "gave up" in msg
+    # cells (1, 2) and (2, 1) wait on the withheld flag of (1, 1) through the same grid's flags:
+    # code 2 (a halo timeout would be code 6)
+    assert "(code 2)" in msg
     h2 = wavefront_grid_layer(x, Wl, Wt, U, b)  # the device is still healthy
     torch.cuda.synchronize()
     assert torch.isfinite(h2.float()).all()
