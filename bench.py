@@ -395,7 +395,16 @@ def extra_engine(device, steps=2, warmup=1):
     R = C = 64
     B, H = 32, 256
     cfg = WavefrontConfig(grid_shape=(R, C), batch_size=B, dim=H)
-    fast = nn.ModuleList([TanhGridCell(H) for _ in range(R)]).to(device)
+    fast = nn.ModuleList([TanhGridCell(H) for _ in range(R)])
+    # b ~ N(0, 1): with W ~ N(0, 1/H) and no bias the recurrence amplifies any rounding
+    # difference about 1000x over 64 rows (the oracle's own float32 and float64 evaluations
+    # differ by 1.4e-3 at the last row), so outputs of implementations that round differently
+    # cannot be compared; with the bias the grid is well conditioned (float32 vs float64 ~2e-6
+    # at every row, mean |h| ~0.66). Timing does not depend on the values.
+    with torch.no_grad():
+        for l in fast:
+            l.b.normal_(0.0, 1.0)
+    fast = fast.to(device)
     tick = nn.ModuleList([TickCell(H) for _ in range(R)]).to(device)
     tick.load_state_dict(fast.state_dict())
     x = torch.randn(B, C, H, device=device).bfloat16()
@@ -418,7 +427,8 @@ def extra_engine(device, steps=2, warmup=1):
             h, gx = step()
             fast_out = {"h": h.float().cpu(), "x_grad": gx.float().cpu(),
                         "grads": {k: p.grad.float().cpu() for k, p in layers.named_parameters()}}
-    out = {"workload": "WavefrontEngine 64x64 per-row tanh cells, batch32 hidden256 bf16 fwd+bwd",
+    out = {"workload": "WavefrontEngine 64x64 per-row tanh cells, batch32 hidden256 bf16 fwd+bwd "
+                       "(W ~ N(0,1/H), b ~ N(0,1))",
            "persistent_ms": round(res["persistent"], 3),
            "per_diagonal_ms": round(res["per_diagonal"], 3),
            "per_diagonal_graphed_ms": round(res["per_diagonal_graphed"], 3),

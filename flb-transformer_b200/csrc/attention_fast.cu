@@ -487,20 +487,26 @@ int attn_fwd_fast(const void* q, const void* k, const void* v, const float* w, c
 // =============================================================================================
 // Backward (bf16/fp16, D = 64), consuming the scores saved by the forward.
 //
-// One CTA per (128-key block, batch*head), 8 warps, looping over 128-query tiles (causal: only
-// tiles at or below the key block). Per query tile:
+// One CTA per (128-key block, batch*head), 32 warps (1024 threads, at most 64 registers each, one
+// CTA per SM), looping over 128-query tiles (causal: only tiles at or below the key block). Per
+// query tile:
 //   1. dP = dO . V^T on the tensor core (A = dO tile, K-major; B = the CTA's V block, K-major;
 //      M = N = 128, K = 64) into TMEM columns [0, 128).
-//   2. Threads (TMEM lane = query row, warps 0-3 / 4-7 take the two 64-key halves) form
-//      P = exp(s - lse) from the saved scores and dS = P * (dP - Delta); P goes to shared memory
-//      as the MN-major A operand of step 3, dS (fp32) to a shared tile.
+//   2. Phase A (TMEM lane = query row; the 8 warps of a lane quarter take 16 keys each): P =
+//      exp(s - lse) from the saved scores, dS = P * (dP - Delta); P goes to shared memory as the
+//      MN-major A operand of step 3, dS (fp16, scaled per tile by a power of two) to a shared tile.
 //   3. dV += P^T . dO on the tensor core: P is read MN-major (M = keys), and the same swizzled dO
 //      tile serves as an MN-major B operand (N = d); accumulator in TMEM columns [128, 192).
-//   4. The tanh grid (the MUFU-bound part): warp w owns keys 16w..16w+15, lane l owns head dims
-//      2l, 2l+1. For every query row: t = tanh(q + k), u = dS t, g = dS - u t; dK and dw
-//      accumulate in registers over the whole key block, dQ over the warp's 16 keys and then
-//      into a shared fp32 tile with shared-memory atomics, flushed to a global fp32 accumulator
-//      once per tile (one red.add per element per CTA and tile).
+//   4. Phase B, the tanh grid (the MUFU-bound part): warp w owns keys 16 (w % 8) .. +15 for query
+//      rows 32 (w / 8) .. +31, lane l head dims 2l, 2l+1, in packed f16x2. For every row:
+//      t = tanh(q + k), s = 1 - t^2; dK accumulates dS s per key (f16 over the tile's rows, then
+//      fp32 in TMEM columns [256, 512)), dw accumulates dS t, dQ's per-row sum over the warp's
+//      keys goes into a shared fp32 tile with shared-memory reductions, flushed to a global fp32
+//      accumulator once per tile (one vector red.add per four elements per CTA and tile).
+// 32 warps (8 per scheduler) are what keep both the MUFU and the FMA pipe busy through each
+// row's dependency chains; keeping the dK partials in TMEM instead of registers is what lets
+// that many warps fit the register file, and 16 keys per warp halve the per-row loads and
+// reductions per key against 8.
 // A prep kernel computes Delta = rowsum(dO * O) and clears the dQ accumulator; a finish kernel
 // scales dQ by w' and casts it. dQ[i,d] = w'[d] sum_j dS (1 - t^2), dK[j,d] = w'[d] sum_i dS
 // (1 - t^2), dw[d] = sum dS t / sqrt(D), w' = w / sqrt(D) (kernels/additive_attention.py:91-130).
@@ -517,6 +523,7 @@ __device__ __forceinline__ void red_add_v4(float* dst, float a, float b, float c
 
 struct BwdCfg {
   static constexpr int D = 64, BM = 128, BN = 128;
+  static constexpr int NT = 1024;                          // 32 warps, <= 64 registers each
   static constexpr int TILE = BM * D * 2;                  // 16 KB (a q or dO tile, bf16/fp16)
   static constexpr int SC_BOX = BM * 32 * 4;               // 16 KB: scores of 128 rows x 32 keys
   static constexpr int OFF_V = 0;                          // V block [128 keys x 64] swizzled
@@ -532,7 +539,11 @@ struct BwdCfg {
   static constexpr int OFF_DS = OFF_SC + 2 * SC_BOX;             // fp16 [129 x DS_LD]
   static constexpr int OFF_DQ = OFF_DS + (BM + 1) * DS_LD * 2;   // fp32 [129 x 64]
   static constexpr int SMEM = OFF_DQ + (BM + 1) * D * 4 + 1024;
-  static constexpr int TMEM_COLS = 256;                    // dP: [0,128), dV: [128,192)
+  // TMEM columns: dP [0,128), dV [128,192), and from 256 the fp32 dK partials of phase B: warp
+  // (16-key group kg, 32-row quarter rq) owns 32 columns at 256 + 32 (kg / 4 + 2 rq) of lane
+  // quarter kg % 4 (column 2 j + c: key j of the group, head dim 2 lane + c)
+  static constexpr int TMEM_COLS = 512;
+  static constexpr int DK_COL0 = 256;
   static_assert(OFF_P % 1024 == 0 && OFF_SC % 1024 == 0, "swizzled boxes need 1 KB alignment");
 };
 
@@ -571,7 +582,7 @@ __global__ void bwd_finish_kernel(const float* __restrict__ dq_acc, const float*
 }
 
 template <typename T>
-__global__ void __launch_bounds__(512, 1)
+__global__ void __launch_bounds__(BwdCfg::NT, 1)
 attn_bwd_tc_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmDO,
                    const __grid_constant__ CUtensorMap tmV, const __grid_constant__ CUtensorMap tmSC,
                    const T* __restrict__ k, const float* __restrict__ w,
@@ -583,12 +594,14 @@ attn_bwd_tc_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constan
   using C = BwdCfg;
   using U = Unpack<T>;
   constexpr int D = C::D;
-  constexpr int NT = 512;  // 16 warps
+  constexpr int NT = C::NT;  // 32 warps
   extern __shared__ uint8_t smem_raw[];
   uint8_t* sm = (uint8_t*)(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
   __shared__ __align__(8) uint64_t full_bar[2];
   __shared__ __align__(8) uint64_t dp_bar, dv_bar, sc_bar;
   __shared__ uint32_t tmem_slot;
+  __shared__ unsigned s_amax;  // max |dS| of the current tile (float bits; non-negative floats order as ints)
+  __shared__ float s_dw[D];    // the CTA's dw partial, one global atomic per head dim at the end
 
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   // 1-D grid over (key block, head); key blocks ascend = most query tiles first, so every head's
@@ -610,7 +623,9 @@ attn_bwd_tc_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constan
     mbar_init(&dv_bar, 1);
     mbar_init(&sc_bar, 1);
     fence_mbar_init();
+    s_amax = 0u;
   }
+  if (tid < D) s_dw[tid] = 0.f;
   if (warp == 0) {
     tmem_alloc(&tmem_slot, C::TMEM_COLS);
     tmem_relinquish();
@@ -619,20 +634,31 @@ attn_bwd_tc_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constan
   for (int i = tid; i < (C::BM + 1) * D; i += NT) sDQ[i] = 0.f;
   if (tid < C::DS_LD)
     reinterpret_cast<__half*>(sm + C::OFF_DS)[C::BM * C::DS_LD + tid] = __float2half(0.f);
-  // phase B ownership: warp w holds keys 8w..8w+7 of the block, lane l holds head dims 2l, 2l+1
-  __half2 kr[8];
+  // phase B ownership: warp w holds keys 16 (w % 8) .. +15 of the block for query rows
+  // 32 (w / 8) .. +31 of every tile; lane l holds head dims 2l, 2l+1
+  const int kg = warp & 7, rq = warp >> 3;
+  __half2 kr[16];
 #pragma unroll
-  for (int j = 0; j < 8; ++j) {
-    const int key = kb0 + warp * 8 + j;
+  for (int j = 0; j < 16; ++j) {
+    const int key = kb0 + kg * 16 + j;
     kr[j] = key < N ? to_h2<T>(reinterpret_cast<const uint32_t*>(kbh + (int64_t)key * D)[lane])
                     : __floats2half2_rn(0.f, 0.f);
   }
-  __shared__ unsigned s_amax;  // max |dS| of the current tile (float bits; non-negative floats order as ints)
-  if (tid == 0) s_amax = 0u;
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = tmem_slot;
+  // this warp's dK accumulator columns (its lane quarter = its key group's, lane = head dim pair)
+  const uint32_t dk_taddr =
+      tmem + ((uint32_t)(32 * (warp & 3)) << 16) + C::DK_COL0 + 32 * ((kg >> 2) + 2 * rq);
+  {
+    uint32_t z[16];
+#pragma unroll
+    for (int i = 0; i < 16; ++i) z[i] = 0u;
+    tmem_st16(dk_taddr, z);
+    tmem_st16(dk_taddr + 16, z);
+    tmem_wait_st();
+  }
 
   auto issue_tile = [&](int t) {  // t: 0-based tile counter
     const int st = t & 1;
@@ -681,11 +707,14 @@ attn_bwd_tc_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constan
   }
   __syncwarp();
 
-  // phase A ownership: TMEM lane quarter (warp & 3) = query rows, key group (warp >> 2) of 32
+  // phase A ownership: TMEM lane quarter (warp & 3) = query rows, 16-key group (warp >> 2) of 8;
+  // the group's scores are half of one 32-key box (four of its 16-byte chunks)
   const int arow = 32 * (warp & 3) + lane;
   const int agrp = warp >> 2;
-  const uint8_t* sc_row = sm + (agrp < 2 ? C::OFF_P : C::OFF_SC - 2 * C::SC_BOX) +
-                          agrp * C::SC_BOX + arow * 128;
+  const int abox = agrp >> 1;
+  const uint8_t* sc_row = sm + (abox < 2 ? C::OFF_P : C::OFF_SC - 2 * C::SC_BOX) +
+                          abox * C::SC_BOX + arow * 128;
+  const int sc_chunk0 = 4 * (agrp & 1);
 
   // per-row phase A inputs (lse, Delta), loaded one tile ahead
   float lse2 = 0.f, dlt = 0.f;
@@ -696,9 +725,6 @@ attn_bwd_tc_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constan
   };
   load_row_stats(0);
 
-  float dka[8][2];  // fp32 dK partials of this warp's keys over all tiles
-#pragma unroll
-  for (int j = 0; j < 8; ++j) dka[j][0] = dka[j][1] = 0.f;
   float dwa0 = 0.f, dwa1 = 0.f;
   __half* sDS = reinterpret_cast<__half*>(sm + C::OFF_DS);  // dS tile, scaled, fp16
 
@@ -711,19 +737,27 @@ attn_bwd_tc_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constan
     if (t >= 1 && !mbar_wait(&dv_bar, (uint32_t)(t - 1) & 1u, kWaitLimit)) atomicExch(err, 13);
     if (!mbar_wait(&sc_bar, (uint32_t)t & 1u, kWaitLimit)) atomicExch(err, 17);
     tc_fence_after();
-    // ---- phase A: P and dS for (row arow, keys 32*agrp .. +31) ------------------------------
-    float sc[32];
+    // ---- phase A: P and dS for (row arow, keys 16*agrp .. +15) ------------------------------
+    // P = exp(s - lse) is formed from the saved scores before the barrier and kept packed in
+    // the dtype of V (8 registers for 16 keys), the operand precision of the dV MMA
+    uint32_t pk[8];
     {
       const int i = q0 + arow;
 #pragma unroll
-      for (int c = 0; c < 8; ++c) {
-        const float4 v4 = *reinterpret_cast<const float4*>(sc_row + ((c ^ (arow & 7)) << 4));
-        sc[4 * c] = v4.x; sc[4 * c + 1] = v4.y; sc[4 * c + 2] = v4.z; sc[4 * c + 3] = v4.w;
-      }
+      for (int c = 0; c < 4; ++c) {
+        const float4 v4 =
+            *reinterpret_cast<const float4*>(sc_row + (((sc_chunk0 + c) ^ (arow & 7)) << 4));
+        const float s4[4] = {v4.x, v4.y, v4.z, v4.w};
+        float p4[4];
 #pragma unroll
-      for (int e = 0; e < 32; ++e) {
-        const int key = kb0 + 32 * agrp + e;
-        if (!(i < N && key < N && (!causal || key <= i))) sc[e] = -INFINITY;
+        for (int e = 0; e < 4; ++e) {
+          const int key = kb0 + 16 * agrp + 4 * c + e;
+          const bool ok = i < N && key < N && (!causal || key <= i);
+          p4[e] = ok ? ex2_approx(s4[e] * kLog2e - lse2) : 0.f;
+        }
+        float r0, r1;
+        pk[2 * c] = U::pack(p4[0], p4[1], r0, r1);
+        pk[2 * c + 1] = U::pack(p4[2], p4[3], r0, r1);
       }
     }
     if constexpr (U::is_bf16) {
@@ -736,30 +770,29 @@ attn_bwd_tc_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constan
       }
       fence_async_shared();  // the stage is refilled by TMA later
     }
-    // boxes 0-1 share the P buffer: every thread's scores are in registers before P is written
+    // boxes 0-1 share the P buffer: every thread's scores are read before P is written
     __syncthreads();
-    float ds[32];
+    float ds[16];
     {
-      uint32_t r[32];
-      tmem_ld32(tmem + ((uint32_t)(32 * (warp & 3)) << 16) + 32 * agrp, r);
-      tmem_wait_ld();
-      uint8_t* sP = sm + C::OFF_P + (agrp >> 1) * (C::BM * 128);
+      // P as the MN-major A operand of the dV MMA: keys 0-63 in the first 16 KB atom, 64-127 in
+      // the second; 8 keys per 16-byte chunk of a query row
+      uint8_t* sP = sm + C::OFF_P + (agrp >> 2) * (C::BM * 128);
       float amax = 0.f;
 #pragma unroll
-      for (int g = 0; g < 4; ++g) {
-        uint32_t pk[4];
+      for (int g = 0; g < 2; ++g) {
+        *reinterpret_cast<uint4*>(sP + sw128_offset(arow, 2 * (agrp & 3) + g)) =
+            make_uint4(pk[4 * g], pk[4 * g + 1], pk[4 * g + 2], pk[4 * g + 3]);
+        uint32_t r[8];
+        tmem_ld8(tmem + ((uint32_t)(32 * (warp & 3)) << 16) + 16 * agrp + 8 * g, r);
+        tmem_wait_ld();
 #pragma unroll
         for (int e = 0; e < 4; ++e) {
-          const float p0 = ex2_approx(sc[8 * g + 2 * e] * kLog2e - lse2);
-          const float p1 = ex2_approx(sc[8 * g + 2 * e + 1] * kLog2e - lse2);
-          float r0, r1;
-          pk[e] = U::pack(p0, p1, r0, r1);
-          ds[8 * g + 2 * e] = r0 * (__uint_as_float(r[8 * g + 2 * e]) - dlt);
-          ds[8 * g + 2 * e + 1] = r1 * (__uint_as_float(r[8 * g + 2 * e + 1]) - dlt);
+          float p0, p1;
+          U::run(pk[4 * g + e], p0, p1);
+          ds[8 * g + 2 * e] = p0 * (__uint_as_float(r[2 * e]) - dlt);
+          ds[8 * g + 2 * e + 1] = p1 * (__uint_as_float(r[2 * e + 1]) - dlt);
           amax = fmaxf(amax, fmaxf(fabsf(ds[8 * g + 2 * e]), fabsf(ds[8 * g + 2 * e + 1])));
         }
-        *reinterpret_cast<uint4*>(sP + sw128_offset(arow, 4 * (agrp & 1) + g)) =
-            make_uint4(pk[0], pk[1], pk[2], pk[3]);
       }
       amax = warp_max(amax);
       if (lane == 0) atomicMax(&s_amax, __float_as_uint(amax));
@@ -771,9 +804,9 @@ attn_bwd_tc_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constan
     const int ex = amax_tile > 0.f ? ilogbf(amax_tile) : 0;
     const float ds_scale = ldexpf(1.f, 8 - ex), ds_unscale = ldexpf(1.f, ex - 8);
     {
-      __half* dsrow = sDS + arow * C::DS_LD + 32 * agrp;
+      __half* dsrow = sDS + arow * C::DS_LD + 16 * agrp;
 #pragma unroll
-      for (int c = 0; c < 4; ++c) {
+      for (int c = 0; c < 2; ++c) {
         uint32_t v[4];
 #pragma unroll
         for (int e = 0; e < 4; ++e) {
@@ -815,88 +848,79 @@ attn_bwd_tc_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constan
     if (t + 1 < ntiles) load_row_stats(t + 1);
 
     // ---- phase B: the tanh grid, packed f16x2 (lane = head dims 2l, 2l+1) ----------------------
-    // Rows are software-pipelined over two register buffers: the tanh of the next row is issued
-    // before the sums of the current one, so the MUFU queue stays fed across the per-row
-    // reductions. The Q tile holds f16x2 pairs here (converted in place in phase A).
+    // 32 warps (8 per scheduler) keep the MUFU and FMA pipes fed across each row's dependency
+    // chains. The Q tile holds f16x2 pairs here (converted in place in phase A).
     {
       const __half2* sQh = reinterpret_cast<const __half2*>(sm + C::OFF_Q + st * C::TILE);
-      const int key_lo = kb0 + warp * 8;
+      const int key_lo = kb0 + kg * 16;
       const int rmax = min(C::BM, N - q0);
       // causal: rows r < key_lo - q0 mask every key of this warp
-      const int r_lo = causal ? max(0, key_lo - q0) : 0;
+      const int r_begin = causal ? max(32 * rq, key_lo - q0) : 32 * rq;
+      const int r_end = min(32 * rq + 32, rmax);
       const __half2 hz = __floats2half2_rn(0.f, 0.f);
-      __half2 dk2[8];
-#pragma unroll
-      for (int j = 0; j < 8; ++j) dk2[j] = hz;
-      // rows are addressed through running pointers (row strides: Q 32 half2, dS DS_LD halves,
-      // dQ partials D floats)
+      const __half2 one2 = __floats2half2_rn(1.f, 1.f);
       constexpr int DS_ROW = C::DS_LD / 8;  // uint4 per dS row
-      auto tanh_row = [&](const __half2* qp, __half2 (&tt)[8]) {
-        const __half2 q2 = *qp;
+      if (r_begin < r_end) {
+        // dK of the warp's keys over its rows of this tile, in f16 (|sum| <= 32 * 512), moved to
+        // the fp32 accumulators in TMEM at the end of the tile
+        __half2 dk2[16];
 #pragma unroll
-        for (int j = 0; j < 8; ++j) tt[j] = tanh_h2(__hadd2(q2, kr[j]));
-      };
-      // per row: g = dS (1 - t^2) into dQ (summed over the warp's keys) and dK (per key, over
-      // rows); u = dS t into dw. Row sums are pairwise trees (short dependency chains).
-      auto sums_row = [&](const uint4* dsp, float* dqp, const __half2 (&tt)[8]) -> __half2 {
-        const uint4 dsv = *dsp;
-        const uint32_t dsu[4] = {dsv.x, dsv.y, dsv.z, dsv.w};
-        __half2 g2[8], u2[8];
+        for (int j = 0; j < 16; ++j) dk2[j] = hz;
+        // rows are addressed through running pointers (row strides: Q 32 half2, dS DS_LD halves,
+        // dQ partials D floats)
+        const __half2* qp = sQh + r_begin * (D / 2) + lane;
+        const uint4* dsp = reinterpret_cast<const uint4*>(sDS + kg * 16) + r_begin * DS_ROW;
+        float* dqp = sDQ + r_begin * D + lane;
+#pragma unroll 1
+        for (int r = r_begin; r < r_end; ++r) {
+          // one query row against the warp's 16 keys, five f16x2 FMA-pipe ops per key: x = q + k,
+          // s = 1 - t^2 and three fused accumulations: dS s into dK (per key) and dQ (over the
+          // keys), dS t into dw
+          const __half2 q2 = *qp;
+          const uint4 dv0 = dsp[0], dv1 = dsp[1];
+          const uint32_t dsu[8] = {dv0.x, dv0.y, dv0.z, dv0.w, dv1.x, dv1.y, dv1.z, dv1.w};
+          __half2 dqa = hz, dqb = hz, dwa = hz, dwb = hz;
 #pragma unroll
-        for (int j = 0; j < 8; ++j) {
-          const __half2 dpair = *reinterpret_cast<const __half2*>(&dsu[j >> 1]);
-          const __half2 d2 = (j & 1) ? __high2half2(dpair) : __low2half2(dpair);
-          u2[j] = __hmul2(d2, tt[j]);
-          g2[j] = __hfma2(__hneg2(u2[j]), tt[j], d2);
-          dk2[j] = __hadd2(dk2[j], g2[j]);
-        }
-        const __half2 dq2 = __hadd2(__hadd2(__hadd2(g2[0], g2[1]), __hadd2(g2[2], g2[3])),
-                                    __hadd2(__hadd2(g2[4], g2[5]), __hadd2(g2[6], g2[7])));
-        const float2 dqf = __half22float2(dq2);
-        // dQ partials (scaled; the flush unscales): layout [row][c * 32 + lane] for head dim
-        // 2 * lane + c (conflict-free)
-        red_shared_f32(dqp, dqf.x);
-        red_shared_f32(dqp + 32, dqf.y);
-        return __hadd2(__hadd2(__hadd2(u2[0], u2[1]), __hadd2(u2[2], u2[3])),
-                       __hadd2(__hadd2(u2[4], u2[5]), __hadd2(u2[6], u2[7])));
-      };
-      const __half2* qp = sQh + r_lo * (D / 2) + lane;
-      const uint4* dsp = reinterpret_cast<const uint4*>(sDS + warp * 8) + r_lo * DS_ROW;
-      float* dqp = sDQ + r_lo * D + lane;
-      const uint4* dsp_zero = reinterpret_cast<const uint4*>(sDS + warp * 8) + C::BM * DS_ROW;
-      float* dqp_dummy = sDQ + C::BM * D + lane;
-      __half2 ta[8], tb[8];
-      if (r_lo < rmax) tanh_row(qp, ta);
-      // two rows per iteration, branch-free: an odd last row pairs with the zero dS row (its
-      // contributions are exactly zero) and the dummy dQ row; the clamped Q offsets read valid
-      // rows whose results go unused
-      // chunks of 32 rows: dk2 holds at most 32 rows (|sum| <= 32 * 512) and is moved to the
-      // fp32 accumulators after each chunk
-#pragma unroll 1
-      for (int c0 = r_lo; c0 < rmax; c0 += 32) {
-        const int cend = min(c0 + 32, rmax);
-#pragma unroll 1
-        for (int r = c0; r < cend; r += 2) {
-          const bool two = r + 1 < rmax, three = r + 2 < rmax;
-          tanh_row(qp + (two ? D / 2 : 0), tb);
-          __half2 dw2 = sums_row(dsp, dqp, ta);  // dw over both rows: |sum| <= 16 * 512
-          tanh_row(qp + (three ? D : (two ? D / 2 : 0)), ta);
-          dw2 = __hadd2(dw2, sums_row(two ? dsp + DS_ROW : dsp_zero, two ? dqp + D : dqp_dummy,
-                                      tb));
-          qp += D;
-          dsp += 2 * DS_ROW;
-          dqp += 2 * D;
-          const float2 dwf = __half22float2(dw2);
+          for (int j = 0; j < 16; ++j) {
+            const __half2 tt = tanh_h2(__hadd2(q2, kr[j]));
+            const __half2 dpair = *reinterpret_cast<const __half2*>(&dsu[j >> 1]);
+            const __half2 d2 = (j & 1) ? __high2half2(dpair) : __low2half2(dpair);
+            const __half2 s2 = __hfma2(__hneg2(tt), tt, one2);
+            dk2[j] = __hfma2(d2, s2, dk2[j]);
+            if (j & 1) {
+              dqb = __hfma2(d2, s2, dqb);
+              dwb = __hfma2(d2, tt, dwb);
+            } else {
+              dqa = __hfma2(d2, s2, dqa);
+              dwa = __hfma2(d2, tt, dwa);
+            }
+          }
+          // dQ partials (scaled; the flush unscales): layout [row][c * 32 + lane] for head dim
+          // 2 * lane + c (conflict-free); |sum| <= 16 * 512
+          const float2 dqf = __half22float2(__hadd2(dqa, dqb));
+          red_shared_f32(dqp, dqf.x);
+          red_shared_f32(dqp + 32, dqf.y);
+          const float2 dwf = __half22float2(__hadd2(dwa, dwb));
           dwa0 = fmaf(dwf.x, ds_unscale, dwa0);
           dwa1 = fmaf(dwf.y, ds_unscale, dwa1);
+          qp += D / 2;
+          dsp += DS_ROW;
+          dqp += D;
         }
 #pragma unroll
-        for (int j = 0; j < 8; ++j) {
-          const float2 f = __half22float2(dk2[j]);
-          dka[j][0] = fmaf(f.x, ds_unscale, dka[j][0]);
-          dka[j][1] = fmaf(f.y, ds_unscale, dka[j][1]);
-          dk2[j] = hz;
+        for (int hh = 0; hh < 2; ++hh) {
+          uint32_t a[16];
+          tmem_ld16(dk_taddr + 16 * hh, a);
+          tmem_wait_ld();
+#pragma unroll
+          for (int j = 0; j < 8; ++j) {
+            const float2 f = __half22float2(dk2[8 * hh + j]);
+            a[2 * j] = __float_as_uint(fmaf(f.x, ds_unscale, __uint_as_float(a[2 * j])));
+            a[2 * j + 1] = __float_as_uint(fmaf(f.y, ds_unscale, __uint_as_float(a[2 * j + 1])));
+          }
+          tmem_st16(dk_taddr + 16 * hh, a);
         }
+        tmem_wait_st();
       }
     }
     __syncthreads();
@@ -923,6 +947,7 @@ attn_bwd_tc_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constan
       fence_async_shared();
       issue_tile(t + 2);
     }
+    tc_fence_before();  // the dK accumulators in TMEM are read by other warps in the epilogue
     __syncthreads();
   }
 
@@ -950,21 +975,40 @@ attn_bwd_tc_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constan
       }
     }
   }
-  {
+  // dK: the first row quarter's warp adds the other three quarters' accumulators (same lane
+  // quarter, 64, 128 and 192 columns further) and stores the key group's rows
+  red_shared_f32(&s_dw[2 * lane], dwa0);
+  red_shared_f32(&s_dw[2 * lane + 1], dwa1);
+  if (rq == 0) {
     const float w0 = wrow[2 * lane] * inv_sqrt_d, w1 = wrow[2 * lane + 1] * inv_sqrt_d;
 #pragma unroll
-    for (int j = 0; j < 8; ++j) {
-      const int key = kb0 + warp * 8 + j;
-      if (key < N) {
-        float r0, r1;
-        reinterpret_cast<uint32_t*>(dk + ((int64_t)bh * N + key) * D)[lane] =
-            U::pack(dka[j][0] * w0, dka[j][1] * w1, r0, r1);
+    for (int hh = 0; hh < 2; ++hh) {
+      uint32_t a[16];
+      tmem_ld16(dk_taddr + 16 * hh, a);
+      tmem_wait_ld();
+      float acc[16];
+#pragma unroll
+      for (int i = 0; i < 16; ++i) acc[i] = __uint_as_float(a[i]);
+#pragma unroll
+      for (int p = 1; p < 4; ++p) {
+        tmem_ld16(dk_taddr + 64 * p + 16 * hh, a);
+        tmem_wait_ld();
+#pragma unroll
+        for (int i = 0; i < 16; ++i) acc[i] += __uint_as_float(a[i]);
+      }
+#pragma unroll
+      for (int j = 0; j < 8; ++j) {
+        const int key = kb0 + kg * 16 + 8 * hh + j;
+        if (key < N) {
+          float r0, r1;
+          reinterpret_cast<uint32_t*>(dk + ((int64_t)bh * N + key) * D)[lane] =
+              U::pack(acc[2 * j] * w0, acc[2 * j + 1] * w1, r0, r1);
+        }
       }
     }
-    float* dwr = dw + (int64_t)w_index[bh] * D;
-    atomicAdd(dwr + 2 * lane, dwa0 * inv_sqrt_d);
-    atomicAdd(dwr + 2 * lane + 1, dwa1 * inv_sqrt_d);
   }
+  __syncthreads();
+  if (tid < D) atomicAdd(dw + (int64_t)w_index[bh] * D + tid, s_dw[tid] * inv_sqrt_d);
   tc_fence_before();
   __syncthreads();
   if (warp == 0) tmem_dealloc(tmem, C::TMEM_COLS);
@@ -1008,7 +1052,7 @@ int launch_bwd_tc(const void* q, const void* k, const void* v, const float* w, c
   st = ensure_dyn_smem((const void*)attn_bwd_tc_kernel<T>, C::SMEM, "attn_bwd_tc smem attribute");
   if (st != FLB_OK) return st;
   const unsigned grid = (unsigned)(((N + C::BN - 1) / C::BN) * BH);
-  attn_bwd_tc_kernel<T><<<grid, 512, C::SMEM, s>>>(tmQ, tmDO, tmV, tmSC, (const T*)k, w, wi, lse,
+  attn_bwd_tc_kernel<T><<<grid, C::NT, C::SMEM, s>>>(tmQ, tmDO, tmV, tmSC, (const T*)k, w, wi, lse,
                                                    delta, dq_acc, (T*)dk, (T*)dv, dw, N, causal,
                                                    (int)BH, err);
   bwd_finish_kernel<T><<<(unsigned)((rows * 32 + 255) / 256), 256, 0, s>>>(dq_acc, w, wi, (T*)dq, N,

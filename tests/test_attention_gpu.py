@@ -137,7 +137,10 @@ def test_a2_dv_a_all_units(a2_run):
     """dv_a is the one reduction across (batch, head) units: each head's row of the gradient
     sums the contributions of all 8 batch elements (atomics from every key block of every unit
     in the kernel). Checked against the oracle's grad_va evaluated on the host in float32 for
-    all 128 units; bf16 output, so the bound is 2e-2 plus half a bf16 ulp of the value."""
+    all 128 units. Each head's row sums ~17 M products dS * tanh with heavy cancellation (every
+    softmax row's dS sums to zero) to values of magnitude ~8, where a bf16 ulp alone is 0.06, so
+    the error is bounded relative to the tensor's largest magnitude, as for the grid layer's
+    weight gradients: max|a - ref| <= 2e-2 * max(1, max|ref|)."""
     (q, k, v, w, g), _, grads = a2_run
     B, H = q.shape[:2]
     ref = torch.zeros(H, 1, q.shape[-1], dtype=torch.float64)
@@ -148,9 +151,8 @@ def test_a2_dv_a_all_units(a2_run):
                                             dtype=torch.float32, row_chunk=64)[3][0].double()
     dva = grads[3]
     assert dva.shape == w.shape and dva.dtype == w.dtype
-    assert excess_half(dva, ref) <= 0
-    # the quantity is not trivially small: a wrong reduction would show
-    assert ref.abs().max().item() > 0.1
+    scale = max(1.0, ref.abs().max().item())
+    assert maxdiff(dva, ref) <= 2e-2 * scale
 
 
 A3_RESCALE_HEAD = 5
@@ -162,18 +164,20 @@ def test_a3_config_sampled_rows(cuda):
     """Long-context configuration B4 H8 N8192 D128 bf16 causal, forward, the whole launch on the
     GPU; output and lse checked against the oracle on the first, a middle and the last 128 query
     rows of three (batch, head) slices (each softmax row is independent, so sampled rows are
-    exact checks). Head 5's score vector is scaled to w_std = 3.5 (sum|w|/sqrt(D) ~ 33, scores
-    ~ 8 log2 units apart within a row) so that later keys exceed a row's first-group maximum by
-    more than the kernel's rescale threshold: that slice runs the accumulator-rescale path, and
-    the test asserts on the oracle's scores that its sampled rows do. Bound: 2e-2 plus half a
-    bf16 ulp; for the scaled head 5e-2 (score errors grow with sum|w|, as in
-    test_large_weights_stable at the same sum|w|/sqrt(D)). lse: 1e-2 absolute."""
+    exact checks). Head 5 is set up so that the kernel's row-rescale path runs on every row
+    i >= 8: its score vector is w ~ N(0, 1) and its keys 0-7 are -8 sign(w), so the first key
+    group of every row scores about -sum|w|/sqrt(D) (~ -9, ~ -13 in log2 units) and later keys
+    exceed that first-group maximum by more than the kernel's threshold (8 log2 units); the
+    test confirms this on the oracle's scores of the sampled rows. Bound: 2e-2 plus half a bf16
+    ulp; for head 5 5e-2 (score errors grow with sum|w|, as in test_large_weights_stable).
+    lse: 1e-2 absolute."""
     from kernels.additive_attention import attention_forward
     B, H, N, D = 4, 8, 8192, 128
     q, k, v, w = oa.make_inputs(B, H, N, D, seed=7, dtype=torch.bfloat16)
-    w = w.clone()
+    w, k = w.clone(), k.clone()
     gw = torch.Generator().manual_seed(70)
-    w[A3_RESCALE_HEAD] = (torch.randn(1, D, generator=gw) * 3.5).bfloat16()
+    w[A3_RESCALE_HEAD] = torch.randn(1, D, generator=gw).bfloat16()
+    k[:, A3_RESCALE_HEAD, :8, :] = (-8.0 * torch.sign(w[A3_RESCALE_HEAD].float())).bfloat16()
     out, lse, _, _, _ = attention_forward(*(t.to(cuda) for t in (q, k, v, w)), True)
     out, lse = out.cpu(), lse.view(B, H, N).cpu()
     assert torch.isfinite(out.float()).all()
@@ -194,7 +198,7 @@ def test_a3_config_sampled_rows(cuda):
                 s2 = s2 * 1.4426950408889634  # log2 units, as the kernel compares
                 first = s2[:, :8].max(dim=-1).values
                 rescaled_rows += int((s2.max(dim=-1).values > first + 8.0).sum())
-    assert rescaled_rows > 0, "the rescale path was not exercised"
+    assert rescaled_rows >= 3 * 128 - 8, rescaled_rows
 
 
 def test_v_a_broadcast_shapes(cuda):
