@@ -339,6 +339,36 @@ def a3_sharded(world, rank, device, steps=3, warmup=2):
             "scaling": "strong"}
 
 
+def grid_row_bands(world, rank, device, steps=10, warmup=3):
+    """The W4 grid layer (64x64, batch 32, hidden 256, forward + backward) split into `world`
+    row bands, one per GPU, the halos crossing NVLink inside the sweep kernels
+    (wavefront/row_bands.py); each rank times its band's step, the time is the max over ranks.
+    The weight gradients' all-reduce (the one collective) is part of the step."""
+    from wavefront.grid_layer import grid_inputs
+    from wavefront.row_bands import GridRowBands
+    from wavefront.sharding import all_reduce_grads
+    B, R, C, H = 32, 64, 64, 256
+    x, Wl, Wt, U, b, dh = grid_inputs(B, R, C, H, device, seed=3)
+    bands = GridRowBands(R, C, B, H)
+    rows = slice(bands.row0, bands.row0 + bands.rows)
+    xb = x[:, rows].contiguous().requires_grad_(True)
+    Wl, Wt, U = (t.requires_grad_(True) for t in (Wl, Wt, U))
+    bf = b.float().requires_grad_(True)
+    dhb = dh[rows].contiguous()
+
+    def step():
+        h = bands.layer(xb, Wl, Wt, U, bf)
+        h.backward(dhb)
+        all_reduce_grads([Wl, Wt, U, bf])
+    for _ in range(warmup):
+        step()
+    ms = time_steps(step, steps, world) / steps
+    bands.close()
+    return {"workload": f"wavefront grid 64x64 batch32 hidden256 bf16 fwd+bwd in {world} row "
+                        "bands", "rows_per_band": bands.rows, "ms": round(ms, 3),
+            "cells_per_s": R * C / (ms * 1e-3)}
+
+
 def extra_grid(device, steps=3, warmup=1, with_cpu=True):
     try:
         from wavefront.grid_layer import wavefront_grid_layer, grid_inputs
@@ -450,9 +480,10 @@ def reference_engine_timing(cfg, layers, x, fast_out, device, steps=2, warmup=1)
     """The reference's own engine (baseline/_ref: its WavefrontEngine with the Triton gather,
     the vmapped cell, its C++ tick loop built from its csrc/) on the same grid, weights and
     input, timed in a child process (its packages share names with this one's). Returns its
-    fwd+bwd time per step (CUDA events) and how its outputs compare with the persistent
-    kernel's (h: max-abs excess over 2e-2 + half a bf16 ulp; gradients: max-abs error relative
-    to the tensor's largest magnitude)."""
+    bf16 fwd+bwd time per step (CUDA events) and how outputs compare, both against the
+    reference engine run again in fp32 (its own code at full precision): this package's
+    persistent kernels and the reference's own bf16 run (h: max-abs excess over 2e-2 + half a
+    bf16 ulp; gradients: max-abs error relative to the tensor's largest magnitude)."""
     import tempfile
     if not os.path.isdir(os.path.join(REF_DIR, "wavefront")):
         return {"unavailable": "reference not installed under baseline/_ref"}
@@ -474,16 +505,22 @@ def reference_engine_timing(cfg, layers, x, fast_out, device, steps=2, warmup=1)
             tail = " | ".join(r.stdout.strip().splitlines()[-3:])
             return {"unavailable": f"reference engine run failed (rc {r.returncode}): {tail}"}
         got = torch.load(fout, weights_only=False)
-    res = {"ms": round(got["ms"], 3), "mode": got["mode"], "steps": steps}
-    if fast_out is not None:
-        h, hr = fast_out["h"].double(), got["h"].double()
-        res["h_excess"] = ((h - hr).abs() - (2e-2 + 2.0 ** -8 * hr.abs())).max().item()
+    res = {"ms": round(got["ms"], 3), "mode": got["mode"], "steps": steps,
+           "dtype": "bf16 (timed); fp32 run as the comparison"}
+
+    def compare(out, ref):
+        h, hr = out["h"].double(), ref["h"].double()
         rel = lambda a, b: ((a.double() - b.double()).abs().max()
                             / max(1.0, b.double().abs().max().item())).item()
-        res["x_grad_rel"] = rel(fast_out["x_grad"], got["x_grad"])
-        res["param_grad_rel"] = {k: rel(v, got["grads"][k]) for k, v in fast_out["grads"].items()}
-        res["within_tolerance"] = bool(res["h_excess"] <= 0 and res["x_grad_rel"] < 2e-2 and
-                                       all(v < 2e-2 for v in res["param_grad_rel"].values()))
+        c = {"h_excess": ((h - hr).abs() - (2e-2 + 2.0 ** -8 * hr.abs())).max().item(),
+             "x_grad_rel": rel(out["x_grad"], ref["x_grad"]),
+             "param_grad_rel_max": max(rel(v, ref["grads"][k]) for k, v in out["grads"].items())}
+        c["within_tolerance"] = bool(c["h_excess"] <= 0 and c["x_grad_rel"] < 2e-2
+                                     and c["param_grad_rel_max"] < 2e-2)
+        return c
+    res["reference_bf16_vs_reference_fp32"] = compare(got["bf16"], got["fp32"])
+    if fast_out is not None:
+        res["persistent_vs_reference_fp32"] = compare(fast_out, got["fp32"])
     return res
 
 
@@ -543,9 +580,17 @@ def run_ref_engine(fin, fout, steps, warmup):
     for _ in range(max(0, warmup - 1)):
         step()
     ms = time_steps(step, steps, 1) / steps
-    h, gx = step()
-    torch.save({"ms": ms, "mode": mode, "h": h.float().cpu(), "x_grad": gx.float().cpu(),
-                "grads": {k: p.grad.float().cpu() for k, p in layers.named_parameters()}}, fout)
+
+    def outputs():
+        h, gx = step()
+        return {"h": h.float().cpu(), "x_grad": gx.float().cpu(),
+                "grads": {k: p.grad.float().cpu() for k, p in layers.named_parameters()}}
+    res = {"ms": ms, "mode": mode, "bf16": outputs()}
+    # the same engine code at fp32 compute (buffers follow x's dtype): the comparison values
+    x = x.float()
+    eng = wfe.WavefrontEngine(cfg, layers).to(device)
+    res["fp32"] = outputs()
+    torch.save(res, fout)
 
 
 def extra_flb_e2e(device, steps=3, decode_steps=256):
@@ -637,6 +682,7 @@ def run_flb(args):
     del pipe
     # the long-context configuration split over the ranks (every rank takes part)
     a3 = a3_sharded(world, rank, device)
+    bands = grid_row_bands(world, rank, device) if args.row_bands and world > 1 else None
 
     # roofline: dominant launch against the measured MUFU tanh rate
     tanh_peak = nat.microbench(0, device)
@@ -671,6 +717,8 @@ def run_flb(args):
         "clocks": clk.summary(),
         "a3_sharded": a3,
     }
+    if bands is not None:
+        out["grid_row_bands"] = bands
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         cps, sample, threads = cpu_attention_sample(cfg)
         out["cpu_baseline"] = {"value": cps, "unit": "pairs/s", "cores": threads, "kind": "port",
@@ -773,6 +821,8 @@ def main():
     ap.add_argument("--impl", choices=["flb", "reference"], default="flb")
     ap.add_argument("--no-extras", action="store_true")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--row-bands", action="store_true",
+                    help="N > 1: also time the W4 grid layer split into N row bands")
     ap.add_argument("--profile", choices=["attn", "grid", "flb", "flb_train"], default=None,
                     help="run one fixed warm-up + profiled step for ncu and exit")
     ap.add_argument("--ref-engine", nargs=2, metavar=("IN", "OUT"), default=None,

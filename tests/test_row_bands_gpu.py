@@ -1,6 +1,6 @@
 """Row bands of the grid layer across GPUs (wavefront/row_bands.py, flb_grid_band_fwd/bwd).
 
-Two ranks, one GPU each (skipped with fewer GPUs): each rank sweeps its band while the halos
+Two or four ranks, one GPU each (skipped with fewer GPUs): each rank sweeps its band while the halos
 cross NVLink inside the kernels, and the result is compared with the unsplit grid layer run on
 the rank's own GPU: h bit for bit without the x term (the same cell arithmetic); with it, h and
 dx within bf16 rounding (the hoisted x U^T GEMM runs over fewer rows); the all-reduced weight
@@ -110,12 +110,16 @@ def _band_worker(rank, world, port, res_path, case):
         dist.destroy_process_group()
 
 
-@pytest.mark.skipif(not torch.cuda.is_available() or torch.cuda.device_count() < 2,
-                    reason="row bands need two GPUs")
+@pytest.mark.parametrize("world", [2, 4])
 @pytest.mark.parametrize("case", sorted(CASES))
-def test_two_gpu_row_bands_match_unsplit_grid(tmp_path, case):
+def test_row_bands_match_unsplit_grid(tmp_path, case, world):
+    """2 ranks: a first and a last band. 4 ranks: two middle bands as well (a halo in from
+    above and out to below in the same sweep), and with 7 rows a band of a single row, whose
+    one row is both edges."""
+    if not torch.cuda.is_available() or torch.cuda.device_count() < world:
+        pytest.skip(f"row bands over {world} ranks need {world} GPUs")
     res = str(tmp_path / "res.pt")
-    mp.start_processes(_band_worker, args=(2, _free_port(), res, case), nprocs=2,
+    mp.start_processes(_band_worker, args=(world, _free_port(), res, case), nprocs=world,
                        start_method="spawn", join=True)
     out = torch.load(res)
     for rank, r in enumerate(out):
