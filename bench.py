@@ -482,8 +482,8 @@ def reference_engine_timing(cfg, layers, x, fast_out, device, steps=2, warmup=1)
     input, timed in a child process (its packages share names with this one's). Returns its
     bf16 fwd+bwd time per step (CUDA events) and how outputs compare, both against the
     reference engine run again in fp32 (its own code at full precision): this package's
-    persistent kernels and the reference's own bf16 run (h: max-abs excess over 2e-2 + half a
-    bf16 ulp; gradients: max-abs error relative to the tensor's largest magnitude)."""
+    persistent kernels and the reference's own bf16 run (h: max-abs error; gradients: max-abs
+    error relative to the tensor's largest magnitude)."""
     import tempfile
     if not os.path.isdir(os.path.join(REF_DIR, "wavefront")):
         return {"unavailable": "reference not installed under baseline/_ref"}
@@ -509,18 +509,21 @@ def reference_engine_timing(cfg, layers, x, fast_out, device, steps=2, warmup=1)
            "dtype": "bf16 (timed); fp32 run as the comparison"}
 
     def compare(out, ref):
-        h, hr = out["h"].double(), ref["h"].double()
         rel = lambda a, b: ((a.double() - b.double()).abs().max()
                             / max(1.0, b.double().abs().max().item())).item()
-        c = {"h_excess": ((h - hr).abs() - (2e-2 + 2.0 ** -8 * hr.abs())).max().item(),
-             "x_grad_rel": rel(out["x_grad"], ref["x_grad"]),
-             "param_grad_rel_max": max(rel(v, ref["grads"][k]) for k, v in out["grads"].items())}
-        c["within_tolerance"] = bool(c["h_excess"] <= 0 and c["x_grad_rel"] < 2e-2
-                                     and c["param_grad_rel_max"] < 2e-2)
-        return c
-    res["reference_bf16_vs_reference_fp32"] = compare(got["bf16"], got["fp32"])
+        return {"h_max_abs_err": (out["h"].double() - ref["h"].double()).abs().max().item(),
+                "x_grad_rel_err": rel(out["x_grad"], ref["x_grad"]),
+                "param_grad_rel_err_max": max(rel(v, ref["grads"][k])
+                                              for k, v in out["grads"].items())}
+    own = compare(got["bf16"], got["fp32"])
+    res["reference_bf16_vs_reference_fp32"] = own
     if fast_out is not None:
-        res["persistent_vs_reference_fp32"] = compare(fast_out, got["fp32"])
+        mine = compare(fast_out, got["fp32"])
+        res["persistent_vs_reference_fp32"] = mine
+        # the persistent kernels are at least as close to the reference's fp32 result as the
+        # reference's own bf16 run is (errors within 10% of it, or below 2e-2)
+        res["persistent_within_reference_bf16_error"] = all(
+            mine[k] <= max(2e-2, 1.1 * own[k]) for k in mine)
     return res
 
 

@@ -118,7 +118,8 @@ attn_fwd_tc_kernel(const __grid_constant__ CUtensorMap tmK, const __grid_constan
                    const T* __restrict__ q, T* __restrict__ out, float* __restrict__ lse,
                    float* __restrict__ scores, const float* __restrict__ w,
                    const int32_t* __restrict__ w_index, int N, int causal, int nbh,
-                   int scores_vec, int* __restrict__ err) {
+                   int scores_vec, float* __restrict__ part_o, float* __restrict__ part_ml,
+                   int* __restrict__ err) {
   using namespace sm100;
   using C = FwdCfg<D>;
   using U = Unpack<T>;
@@ -141,17 +142,35 @@ attn_fwd_tc_kernel(const __grid_constant__ CUtensorMap tmK, const __grid_constan
   const int quarter = warp & 3, wsub = warp >> 2;
   const int dh = lane % TPR;
   const int mrow = 32 * quarter + RPW * wsub + lane / TPR;
-  // 1-D grid over (query block, head), heaviest query blocks of every head first (causal work
-  // grows with the block index): the longest CTAs start in the first wave, not in the tail
-  const int nqb = gridDim.x / nbh;
+  // 1-D grid over (work item, head), heaviest items of every head first (causal work grows with
+  // the block index): the longest CTAs start in the first wave, not in the tail. A work item is
+  // a query block, or, when part_o is given (causal, few CTAs per SM), half of the key tiles of
+  // a query block qb >= 1: items u = 0, 1 are the two halves of block nqb - 1, u = 2, 3 those
+  // of block nqb - 2, ..., and the last item is block 0 whole. Each half writes fp32 partials
+  // (unnormalised O, reference max and row sum) that a combine kernel merges.
+  const int nqb = (N + C::BM - 1) / C::BM;
+  const bool split = part_o != nullptr;
   const int lin = blockIdx.x;
-  const int qb = causal ? (nqb - 1 - lin / nbh) : (lin / nbh);
   const int bh = lin % nbh;
+  const int u = lin / nbh;
+  int qb, half = -1;
+  if (split) {
+    qb = u < 2 * (nqb - 1) ? nqb - 1 - (u >> 1) : 0;
+    if (qb > 0) half = u & 1;
+  } else {
+    qb = causal ? (nqb - 1 - u) : u;
+  }
   const int m0 = qb * C::BM;
   const int row = m0 + mrow;
   const bool row_ok = row < N;
   const int kend = causal ? min(N, m0 + C::BM) : N;
-  const int ntiles = (kend + C::BN - 1) / C::BN;
+  const int ntiles_all = (kend + C::BN - 1) / C::BN;
+  // a half's key tiles: [0, mid) or [mid, ntiles_all). For qb >= 1 the first key of the second
+  // half, 64 mid <= 64 (qb + 1) <= 128 qb, is at or before every row of the block, so each half's
+  // first key group holds a valid key of every row (its reference max is finite)
+  const int mid = (ntiles_all + 1) / 2;
+  const int tile0 = half == 1 ? mid : 0;
+  const int ntiles = half < 0 ? ntiles_all : (half == 0 ? mid : ntiles_all - mid);
   const int warp_last_row = m0 + 32 * quarter + RPW * wsub + RPW - 1;
 
   float* sW = reinterpret_cast<float*>(sm + C::OFF_W);
@@ -189,11 +208,11 @@ attn_fwd_tc_kernel(const __grid_constant__ CUtensorMap tmK, const __grid_constan
   auto issue_tile = [&](int t) {
     const int s = t % C::STAGES;
     mbar_arrive_expect_tx(&full_bar[s], C::KTILE + C::VTILE);
-    tma_load_3d(sm + C::OFF_K + s * C::KTILE, &tmK, &full_bar[s], 0, t * C::BN, bh);
+    tma_load_3d(sm + C::OFF_K + s * C::KTILE, &tmK, &full_bar[s], 0, (tile0 + t) * C::BN, bh);
 #pragma unroll
     for (int vb = 0; vb < D / 64; ++vb)
       tma_load_3d(sm + C::OFF_V + s * C::VTILE + vb * (C::BN * 128), &tmV, &full_bar[s], vb * 64,
-                  t * C::BN, bh);
+                  (tile0 + t) * C::BN, bh);
   };
   if (tid == 0) {
     tma_prefetch_desc(&tmK);
@@ -209,7 +228,7 @@ attn_fwd_tc_kernel(const __grid_constant__ CUtensorMap tmK, const __grid_constan
 
   for (int t = 0; t < ntiles; ++t) {
     const int s = t % C::STAGES;
-    const int j0 = t * C::BN;
+    const int j0 = (tile0 + t) * C::BN;
     if (!mbar_wait(&full_bar[s], (uint32_t)(t / C::STAGES) & 1u, kWaitLimit)) atomicExch(err, 1);
     const uint8_t* sK = sm + C::OFF_K + s * C::KTILE;
     const int b = t & 1;
@@ -389,12 +408,36 @@ attn_fwd_tc_kernel(const __grid_constant__ CUtensorMap tmK, const __grid_constan
   float l_row = l;
 #pragma unroll
   for (int o = 1; o < TPR; o <<= 1) l_row += __shfl_xor_sync(0xffffffffu, l_row, o);
+  // a half of a split block: its partial state goes to the workspace for the combine kernel
+  const int64_t item = ((int64_t)bh * nqb + qb) * 2 + (half < 0 ? 0 : half);
   if (dh == 0) {
     sL[mrow] = l_row;
-    if (row_ok) lse[(int64_t)bh * N + row] = (m_ref + __log2f(l_row)) * kLn2;
+    if (half >= 0)
+      reinterpret_cast<float2*>(part_ml)[item * C::BM + mrow] = make_float2(m_ref, l_row);
+    else if (row_ok)
+      lse[(int64_t)bh * N + row] = (m_ref + __log2f(l_row)) * kLn2;
   }
   __syncthreads();
   tc_fence_after();
+  if (half >= 0) {
+    // unnormalised fp32 rows of O (relative to the row's reference max), straight from TMEM
+    float* prow = part_o + (item * C::BM + 32 * quarter + lane) * D + wsub * DH;
+#pragma unroll
+    for (int cb = 0; cb < DH / 32; ++cb) {
+      uint32_t r[32];
+      tmem_ld32(tmem_quarter + wsub * DH + cb * 32, r);
+      tmem_wait_ld();
+#pragma unroll
+      for (int g = 0; g < 8; ++g)
+        reinterpret_cast<float4*>(prow + cb * 32)[g] =
+            make_float4(__uint_as_float(r[4 * g]), __uint_as_float(r[4 * g + 1]),
+                        __uint_as_float(r[4 * g + 2]), __uint_as_float(r[4 * g + 3]));
+    }
+    tc_fence_before();
+    __syncthreads();
+    if (warp == 0) tmem_dealloc(tmem, C::TMEM_COLS);
+    return;
+  }
   // warp w stores columns [DH (w / 4), DH (w / 4 + 1)) of the 32 rows of its lane quarter
   const int orow_m = 32 * quarter + lane;
   const bool orow_ok = m0 + orow_m < N;
@@ -425,10 +468,64 @@ attn_fwd_tc_kernel(const __grid_constant__ CUtensorMap tmK, const __grid_constan
   if (warp == 0) tmem_dealloc(tmem, C::TMEM_COLS);
 }
 
+// Merges the two halves of every split query block (blocks 1 .. nqb - 1 of each head): one warp
+// per query row, lanes over head dims. With the halves' reference maxima m0, m1 (log2 units),
+// row sums l0, l1 and unnormalised rows O0, O1: M = max(m0, m1), a_i = 2^(m_i - M),
+// out = (a0 O0 + a1 O1) / (a0 l0 + a1 l1), lse = (M + log2(a0 l0 + a1 l1)) ln 2.
+template <int D, typename T>
+__global__ void attn_fwd_combine_kernel(const float* __restrict__ part_o,
+                                        const float* __restrict__ part_ml, T* __restrict__ out,
+                                        float* __restrict__ lse, int N, int nbh) {
+  constexpr int BM = FwdCfg<D>::BM;
+  const int nqb = (N + BM - 1) / BM;
+  const int64_t per_bh = (int64_t)(nqb - 1) * BM;
+  const int64_t rid = (int64_t)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
+  const int lane = threadIdx.x & 31;
+  if (rid >= per_bh * nbh) return;
+  const int bh = (int)(rid / per_bh);
+  const int qb = 1 + (int)((rid % per_bh) / BM), mrow = (int)(rid % BM);
+  const int row = qb * BM + mrow;
+  if (row >= N) return;
+  const int64_t i0 = (((int64_t)bh * nqb + qb) * 2) * BM + mrow, i1 = i0 + BM;
+  const float2 ml0 = reinterpret_cast<const float2*>(part_ml)[i0];
+  const float2 ml1 = reinterpret_cast<const float2*>(part_ml)[i1];
+  const float M = fmaxf(ml0.x, ml1.x);
+  const float a0 = ex2_approx(ml0.x - M), a1 = ex2_approx(ml1.x - M);
+  const float lsum = ml0.y * a0 + ml1.y * a1;
+  const float inv = lsum > 0.f ? 1.f / lsum : 0.f;
+  const float2* o0 = reinterpret_cast<const float2*>(part_o + i0 * D);
+  const float2* o1 = reinterpret_cast<const float2*>(part_o + i1 * D);
+  uint32_t* dst = reinterpret_cast<uint32_t*>(out + ((int64_t)bh * N + row) * D);
+#pragma unroll
+  for (int c = lane; c < D / 2; c += 32) {
+    const float2 x0 = o0[c], x1 = o1[c];
+    float r0, r1;
+    dst[c] = Unpack<T>::pack((x0.x * a0 + x1.x * a1) * inv, (x0.y * a0 + x1.y * a1) * inv, r0, r1);
+  }
+  if (lane == 0) lse[(int64_t)bh * N + row] = (M + __log2f(lsum)) * kLn2;
+}
+
+// Whether a causal forward splits its query blocks 1 .. nqb - 1 into key-range halves: when the
+// grid would hold fewer than four CTAs per SM, the longest causal blocks (their key range grows
+// with the block index) would otherwise leave the last wave's SMs idle.
+bool fwd_split(int64_t BH, int64_t N, int flags) {
+  if (!(flags & FLB_ATTN_CAUSAL) || N < 256) return false;
+  const int64_t nqb = (N + 127) / 128;
+  return BH * nqb < 4 * (int64_t)num_sms();
+}
+// Workspace of a split forward: 256 B error word, then the partial O rows [BH, nqb, 2, 128, D]
+// and the (max, sum) pairs [BH, nqb, 2, 128] (fp32).
+size_t fwd_part_o_bytes(int64_t BH, int64_t N, int64_t D) {
+  return (size_t)BH * ((N + 127) / 128) * 2 * 128 * D * sizeof(float);
+}
+size_t fwd_part_ml_bytes(int64_t BH, int64_t N) {
+  return (size_t)BH * ((N + 127) / 128) * 2 * 128 * 2 * sizeof(float);
+}
+
 template <int D, typename T>
 int launch_fwd_tc(const void* q, const void* k, const void* v, const float* w, const int32_t* wi,
                   void* out, float* lse, float* scores, int64_t BH, int N, int causal, int* err,
-                  cudaStream_t s) {
+                  float* part_o, float* part_ml, cudaStream_t s) {
   using C = FwdCfg<D>;
   const CUtensorMapDataType dt =
       Unpack<T>::is_bf16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
@@ -443,13 +540,21 @@ int launch_fwd_tc(const void* q, const void* k, const void* v, const float* w, c
   if (st != FLB_OK) return st;
   st = ensure_dyn_smem((const void*)attn_fwd_tc_kernel<D, T>, C::SMEM, "attn_fwd_tc smem attribute");
   if (st != FLB_OK) return st;
-  const unsigned grid = (unsigned)(((N + C::BM - 1) / C::BM) * BH);
+  const int64_t nqb = (N + C::BM - 1) / C::BM;
+  const unsigned grid = (unsigned)((part_o ? 2 * nqb - 1 : nqb) * BH);
   // vector score stores (8 / TPR floats) need an aligned base (rows are padded to 16 bytes)
   const int kpt = 8 / C::TPR;
   const int scores_vec = (reinterpret_cast<uintptr_t>(scores) & (uintptr_t)(4 * kpt - 1)) == 0;
   attn_fwd_tc_kernel<D, T><<<grid, C::THREADS, C::SMEM, s>>>(
-      tmK, tmV, (const T*)q, (T*)out, lse, scores, w, wi, N, causal, (int)BH, scores_vec, err);
+      tmK, tmV, (const T*)q, (T*)out, lse, scores, w, wi, N, causal, (int)BH, scores_vec, part_o,
+      part_ml, err);
   count_launches(1);
+  if (part_o) {
+    const int64_t rows = BH * (nqb - 1) * C::BM;
+    attn_fwd_combine_kernel<D, T><<<(unsigned)((rows + 7) / 8), 256, 0, s>>>(part_o, part_ml,
+                                                                             (T*)out, lse, N, (int)BH);
+    count_launches(1);
+  }
   return check_cuda(cudaGetLastError(), "attn_fwd_tc launch");
 }
 
@@ -465,7 +570,10 @@ int attn_fwd_fast_supported(int64_t BH, int64_t N, int64_t D, int dtype, int fla
   return 1;
 }
 
-size_t attn_fwd_fast_workspace(int64_t, int64_t, int64_t, int, int) { return 256; }
+size_t attn_fwd_fast_workspace(int64_t BH, int64_t N, int64_t D, int, int flags) {
+  if (!fwd_split(BH, N, flags)) return 256;
+  return 256 + fwd_part_o_bytes(BH, N, D) + fwd_part_ml_bytes(BH, N);
+}
 
 int attn_fwd_fast(const void* q, const void* k, const void* v, const float* w, const int32_t* wi,
                   void* out, float* lse, float* scores, int64_t BH, int N, int D, int dtype,
@@ -476,12 +584,20 @@ int attn_fwd_fast(const void* q, const void* k, const void* v, const float* w, c
   cudaError_t e = cudaMemsetAsync(err, 0, sizeof(int), s);
   if (e != cudaSuccess) return check_cuda(e, "attn_fwd error-word reset");
   const int causal = (flags & FLB_ATTN_CAUSAL) ? 1 : 0;
-  if (dtype == FLB_BF16) {
-    return D == 64 ? launch_fwd_tc<64, __nv_bfloat16>(q, k, v, w, wi, out, lse, scores, BH, N, causal, err, s)
-                   : launch_fwd_tc<128, __nv_bfloat16>(q, k, v, w, wi, out, lse, scores, BH, N, causal, err, s);
+  float* po = nullptr;
+  float* pml = nullptr;
+  if (fwd_split(BH, N, flags)) {
+    if (ws_bytes < attn_fwd_fast_workspace(BH, N, D, dtype, flags))
+      return fail(FLB_ERR_WORKSPACE, "attn_fwd: workspace smaller than flb_attn_fwd_workspace_bytes()");
+    po = reinterpret_cast<float*>(reinterpret_cast<uint8_t*>(ws) + 256);
+    pml = reinterpret_cast<float*>(reinterpret_cast<uint8_t*>(po) + fwd_part_o_bytes(BH, N, D));
   }
-  return D == 64 ? launch_fwd_tc<64, __half>(q, k, v, w, wi, out, lse, scores, BH, N, causal, err, s)
-                 : launch_fwd_tc<128, __half>(q, k, v, w, wi, out, lse, scores, BH, N, causal, err, s);
+  if (dtype == FLB_BF16) {
+    return D == 64 ? launch_fwd_tc<64, __nv_bfloat16>(q, k, v, w, wi, out, lse, scores, BH, N, causal, err, po, pml, s)
+                   : launch_fwd_tc<128, __nv_bfloat16>(q, k, v, w, wi, out, lse, scores, BH, N, causal, err, po, pml, s);
+  }
+  return D == 64 ? launch_fwd_tc<64, __half>(q, k, v, w, wi, out, lse, scores, BH, N, causal, err, po, pml, s)
+                 : launch_fwd_tc<128, __half>(q, k, v, w, wi, out, lse, scores, BH, N, causal, err, po, pml, s);
 }
 
 // =============================================================================================

@@ -2,14 +2,14 @@
 
 TEST INFRASTRUCTURE ONLY. The reference module (csrc/wavefront_backend.cpp of FLB-Transformer,
 a torch CppExtension per its setup.py:8-12) is compiled from the source file where it lies
-under /root/reference, with the same flags (-O3), as oracle/_ref/wavefront_backend*.so. It is
+under $FLB_REFERENCE_DIR (default /root/reference), with the same flags (-O3), as oracle/_ref/wavefront_backend*.so. It is
 used only to generate the golden fixtures under tests/golden/ in a container that has the
 reference checked out; nothing on the GPU box needs it.
 """
 import os
 import sys
 
-REF = "/root/reference"
+REF = os.environ.get("FLB_REFERENCE_DIR", "/root/reference")
 OUT = os.path.join(os.path.dirname(os.path.abspath(__file__)), "_ref")
 
 

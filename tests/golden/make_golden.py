@@ -1,6 +1,7 @@
 """Generate the golden fixtures in tests/golden/ by running the REFERENCE implementation.
 
-Run in a container where the reference is checked out at /root/reference (read-only) and its
+Run in a container where the reference is checked out at $FLB_REFERENCE_DIR (default
+/root/reference; read-only) and its
 C++ orchestrator has been compiled by oracle/build_ref.py:
 
     python oracle/build_ref.py && python tests/golden/make_golden.py
@@ -27,7 +28,7 @@ import sys
 
 import torch
 
-REF = "/root/reference"
+REF = os.environ.get("FLB_REFERENCE_DIR", "/root/reference")
 HERE = os.path.dirname(os.path.abspath(__file__))
 REPO = os.path.dirname(os.path.dirname(HERE))
 sys.path.insert(0, os.path.join(REPO, "oracle", "_ref"))

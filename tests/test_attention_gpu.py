@@ -160,17 +160,13 @@ A3_SLICES = ((0, 0), (3, 7), (1, A3_RESCALE_HEAD))
 A3_ROWS = ((0, 128), (4032, 4160), (8064, 8192))
 
 
-def test_a3_config_sampled_rows(cuda):
-    """Long-context configuration B4 H8 N8192 D128 bf16 causal, forward, the whole launch on the
-    GPU; output and lse checked against the oracle on the first, a middle and the last 128 query
-    rows of three (batch, head) slices (each softmax row is independent, so sampled rows are
-    exact checks). Head 5 is set up so that the kernel's row-rescale path runs on every row
-    i >= 8: its score vector is w ~ N(0, 1) and its keys 0-7 are -8 sign(w), so the first key
-    group of every row scores about -sum|w|/sqrt(D) (~ -9, ~ -13 in log2 units) and later keys
-    exceed that first-group maximum by more than the kernel's threshold (8 log2 units); the
-    test confirms this on the oracle's scores of the sampled rows. Bound: 2e-2 plus half a bf16
-    ulp; for head 5 5e-2 (score errors grow with sum|w|, as in test_large_weights_stable).
-    lse: 1e-2 absolute."""
+@pytest.fixture(scope="module")
+def a3_run(cuda):
+    """B4 H8 N8192 D128 bf16 causal forward of the whole configuration on the GPU. Head 5 is set
+    up so that the kernel's row-rescale path runs on every row i >= 8: its score vector is
+    w ~ N(0, 1) and its keys 0-7 are -8 sign(w), so the first key group of every row scores about
+    -sum|w|/sqrt(D) (~ -9, ~ -13 in log2 units) and later keys exceed that first-group maximum by
+    more than the kernel's threshold (8 log2 units)."""
     from kernels.additive_attention import attention_forward
     B, H, N, D = 4, 8, 8192, 128
     q, k, v, w = oa.make_inputs(B, H, N, D, seed=7, dtype=torch.bfloat16)
@@ -179,26 +175,68 @@ def test_a3_config_sampled_rows(cuda):
     w[A3_RESCALE_HEAD] = torch.randn(1, D, generator=gw).bfloat16()
     k[:, A3_RESCALE_HEAD, :8, :] = (-8.0 * torch.sign(w[A3_RESCALE_HEAD].float())).bfloat16()
     out, lse, _, _, _ = attention_forward(*(t.to(cuda) for t in (q, k, v, w)), True)
-    out, lse = out.cpu(), lse.view(B, H, N).cpu()
-    assert torch.isfinite(out.float()).all()
+    return (q, k, v, w), out.cpu(), lse.view(B, H, N).cpu()
+
+
+def _check_a3_rows(q, k, v, out, lse, cases):
+    """out/lse [b, h, N, ...] of the cases (b, h, score vector [1, 1, D], rescale head?) against
+    the oracle on the first, a middle and the last 128 query rows; returns how many sampled rows
+    of rescale heads take the rescale path (from the oracle's scores)."""
     rescaled_rows = 0
-    for b, h in A3_SLICES:
+    for b, h, wv, rescale in cases:
         sl = lambda t: t[b:b + 1, h:h + 1]
-        tol = 5e-2 if h == A3_RESCALE_HEAD else TOL_HALF
+        tol = 5e-2 if rescale else TOL_HALF
         for r0, r1 in A3_ROWS:
-            ref_o, ref_l = oa.attention_forward(sl(q), sl(k), sl(v), w[h:h + 1], causal=True,
+            ref_o, ref_l = oa.attention_forward(sl(q), sl(k), sl(v), wv, causal=True,
                                                 row_range=(r0, r1), row_chunk=32)
             got = out[b, h, r0:r1].double()
             excess = ((got - ref_o[0, 0]).abs() - (tol + 2.0 ** -8 * ref_o[0, 0].abs())).max()
             assert excess.item() <= 0, (b, h, r0)
             assert maxdiff(lse[b, h, r0:r1], ref_l[0, 0]) < 1e-2, (b, h, r0)
-            if h == A3_RESCALE_HEAD:
-                s2 = oa.attention_scores(sl(q), sl(k), w[h:h + 1], causal=True,
+            if rescale:
+                s2 = oa.attention_scores(sl(q), sl(k), wv, causal=True,
                                          row_range=(r0, r1), dtype=torch.float32)[0, 0]
                 s2 = s2 * 1.4426950408889634  # log2 units, as the kernel compares
                 first = s2[:, :8].max(dim=-1).values
                 rescaled_rows += int((s2.max(dim=-1).values > first + 8.0).sum())
-    assert rescaled_rows >= 3 * 128 - 8, rescaled_rows
+    return rescaled_rows
+
+
+def test_a3_config_sampled_rows(a3_run):
+    """Long-context configuration B4 H8 N8192 D128 bf16 causal, forward, the whole launch on the
+    GPU (32 units: one CTA per query block); output and lse checked against the oracle on
+    sampled rows of three (batch, head) slices (each softmax row is independent, so sampled rows
+    are exact checks), one of them the head set up to take the rescale path (confirmed on the
+    oracle's scores). Bound: 2e-2 plus half a bf16 ulp; for the rescale head 5e-2 (score errors
+    grow with sum|w|, as in test_large_weights_stable). lse: 1e-2 absolute."""
+    (q, k, v, w), out, lse = a3_run
+    assert torch.isfinite(out.float()).all()
+    cases = [(b, h, w[h:h + 1], h == A3_RESCALE_HEAD) for b, h in A3_SLICES]
+    assert _check_a3_rows(q, k, v, out, lse, cases) >= 3 * 128 - 8
+
+
+def test_a3_shard_of_four_units_splits_blocks(cuda, a3_run):
+    """The long-context configuration's share of one GPU out of eight: 4 (batch, head) units.
+    With that few CTAs the causal forward splits each query block but the first into two
+    key-range halves merged by a combine kernel. Checked against the oracle on sampled rows
+    (the rescale head among them) and against the unsplit 32-unit launch on the same units
+    (one bf16 ulp plus 2e-2; lse 1e-2)."""
+    from kernels.additive_attention import attention_forward
+    import flb_native as nat
+    (q, k, v, w), out_all, lse_all = a3_run
+    units = [(1, 2), (1, 3), (1, 4), (1, A3_RESCALE_HEAD)]
+    qs, ks, vs = (torch.stack([t[b, h] for b, h in units]).unsqueeze(1) for t in (q, k, v))
+    ws = torch.stack([w[h] for _, h in units]).unsqueeze(1)          # [4, 1, 1, D]
+    ws_bytes = nat.lib.flb_attn_fwd_workspace_bytes(4, 8192, 128, nat.BF16, nat.ATTN_CAUSAL)
+    assert ws_bytes > 256  # the split path is the one taken at this size
+    out, lse, _, _, _ = attention_forward(*(t.to(cuda) for t in (qs, ks, vs, ws)), True)
+    out, lse = out.cpu(), lse.view(4, 1, -1).cpu()
+    for i, (b, h) in enumerate(units):
+        assert excess_half(out[i, 0], out_all[b, h], ulps=1.0) <= 0, (b, h)
+        assert maxdiff(lse[i, 0], lse_all[b, h]) < 1e-2
+    cases = [(i, 0, ws[i], h == A3_RESCALE_HEAD) for i, (_, h) in enumerate(units)
+             if i in (0, 3)]
+    assert _check_a3_rows(qs, ks, vs, out, lse, cases) >= 128 * 3 - 8
 
 
 def test_v_a_broadcast_shapes(cuda):
