@@ -137,8 +137,9 @@ def test_native_flb_forward_matches_generic_path(cuda):
 
 @pytest.mark.gpu
 def test_native_flb_forward_against_reference(cuda, flb_golden):
-    """The native path (bf16) against the reference model in fp32 on the golden case: its error
-    stays within that of the per-tick path at the same precision (plus a small margin)."""
+    """The native path (bf16) against the reference model in fp32 on the golden case: logits
+    within 2e-2 of the reference relative to their largest magnitude (the bf16 tolerance; the
+    per-tick path at the same precision is shown beside it)."""
     g = flb_golden
     c = g["config"]
     m = _model(c, cuda)
@@ -152,7 +153,7 @@ def test_native_flb_forward_against_reference(cuda, flb_golden):
         m.engine.native_cells = True
         ln_, _, _ = m(tok)
     e_gen, e_nat = _max_rel(lg, ref), _max_rel(ln_, ref)
-    assert e_nat <= 2 * e_gen + 1e-2, (e_nat, e_gen)
+    assert e_nat < 2e-2, (e_nat, e_gen)
 
 
 @pytest.mark.gpu
@@ -197,8 +198,9 @@ def test_native_flb_training_matches_generic_path(cuda):
 
 @pytest.mark.gpu
 def test_native_flb_training_against_reference(cuda, flb_golden):
-    """Native bf16 gradients against the reference model's fp32 gradients (golden): within
-    twice the per-tick path's bf16 error plus a small margin, for every parameter."""
+    """Native bf16 gradients against the reference model's fp32 gradients (golden): every
+    parameter's gradient within 2e-2 of the reference relative to the tensor's largest
+    magnitude, the bf16 tolerance (measured worst 0.016; the per-tick path's 0.017)."""
     g = flb_golden
     c = g["config"]
     m = _model(c, cuda)
@@ -210,7 +212,7 @@ def test_native_flb_training_against_reference(cuda, flb_golden):
     for k, ref in g["grads"].items():
         ref = ref.to(cuda)
         e_nat, e_gen = _max_rel(gn[k], ref), _max_rel(gg[k], ref)
-        assert e_nat <= 2 * e_gen + 3e-2, (k, e_nat, e_gen)
+        assert e_nat < 2e-2, (k, e_nat, e_gen)
 
 
 @pytest.mark.gpu
