@@ -95,10 +95,11 @@ def test_greedy_decode_graphed_equals_eager(cuda):
     assert torch.equal(a[:, 0], logits[:, -1].argmax(-1))
 
 
-def _bf16_model(seed, V=50, D=64, L=4, S=6, B=3):
+def _bf16_model(seed, V=50, D=64, L=4, S=6, B=3, heads=8):
     from flb_model import FLBTransformer
     torch.manual_seed(seed)
-    m = FLBTransformer(V, hidden_dim=D, num_layers=L, seq_len=S, batch_size=B).cuda().eval()
+    m = FLBTransformer(V, hidden_dim=D, num_layers=L, seq_len=S, batch_size=B,
+                       num_heads=heads).cuda().eval()
     with torch.no_grad():
         for name, p in m.named_parameters():
             if name.endswith("v_a"):
@@ -133,6 +134,38 @@ def test_native_flb_forward_matches_generic_path(cuda):
     assert abs(an.item() - ag.item()) <= 3e-2 * abs(ag.item()) + 1e-6
     for a, b in zip(cn, cg):
         assert _max_rel(a, b) < 3e-2
+
+
+@pytest.mark.gpu
+def test_native_flb_forward_e2e_cell_shape(cuda):
+    """Batch 16, d_model 768, 12 heads (the end-to-end configuration's cell) through the native
+    whole-grid forward: every port grid, the logits and the contexts against the per-tick
+    vmapped path of the same engine under bf16 autocast (3e-2 relative to each tensor's largest
+    magnitude), and the CUDA-graph replay of the native forward against eager (equal)."""
+    from wavefront.wavefront_graph import GraphedWavefrontEngine
+    m = _bf16_model(23, D=768, L=6, S=5, B=16, heads=12)
+    tok = torch.randint(0, 50, (16, 5), device=cuda)
+    with torch.no_grad(), torch.autocast("cuda", dtype=torch.bfloat16):
+        x = m.embedding(tok)
+        # the native path first, on the engine's freshly allocated (zero) grids, so that nothing
+        # the per-tick path leaves in the shared buffers can stand in for its outputs
+        nat_ = [g.clone() for g in m.engine(x)]
+        ln_, an, cn = m(tok)
+        m.engine.native_cells = False
+        gen = [g.clone() for g in m.engine(x)]
+        lg, ag, cg = m(tok)
+        m.engine.native_cells = True
+        graphed = GraphedWavefrontEngine(m.engine, x, backward=False)
+        assert graphed.native_flb
+        lgr, _, _ = m(tok, engine=graphed)
+    for p in range(4):
+        assert torch.isfinite(nat_[p].float()).all(), p
+        assert _max_rel(nat_[p], gen[p]) < 3e-2, (p, _max_rel(nat_[p], gen[p]))
+    assert _max_rel(ln_, lg) < 3e-2
+    assert abs(an.item() - ag.item()) <= 3e-2 * abs(ag.item()) + 1e-6
+    for a, b in zip(cn, cg):
+        assert _max_rel(a, b) < 3e-2
+    assert torch.equal(lgr, ln_)
 
 
 @pytest.mark.gpu
