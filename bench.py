@@ -624,6 +624,16 @@ def extra_flb_e2e(device, steps=3, decode_steps=256):
         fwd_ms = time_steps(lambda: m(prompt, engine=g), steps, 1) / steps
         greedy_decode(m, prompt, 1, engine=g)
         dec_ms = time_steps(lambda: greedy_decode(m, prompt, decode_steps, engine=g), 1, 1)
+        logits_ticks, _, _ = m(prompt, engine=g)
+        # the same forward as ONE persistent tcgen05 kernel (flb_block_grid_fwd_ex, path 2)
+        m.engine.native_flb_path = 2
+        gp = m.engine.graphed(m.embedding(prompt), backward=False)
+        logits_p, _, _ = m(prompt, engine=gp)
+        fwd_p_ms = time_steps(lambda: m(prompt, engine=gp), steps, 1) / steps
+        p_rel = ((logits_p.float() - logits_ticks.float()).abs().max()
+                 / logits_ticks.float().abs().max()).item()
+        m.engine.native_flb_path = 0
+        del gp
     del g
     # training step (forward + backward, cross-entropy + aux), forward and backward captured
     m.train()
@@ -645,6 +655,8 @@ def extra_flb_e2e(device, steps=3, decode_steps=256):
                         f"{decode_steps} greedy decode steps, bf16",
             "native_cells": bool(gt.native_flb), "capture_s": round(capture_s, 2),
             "forward_ms": round(fwd_ms, 2), "cells_per_s": L * S / (fwd_ms * 1e-3),
+            "forward_ms_persistent_kernel": round(fwd_p_ms, 2),
+            "persistent_logits_max_rel_diff": p_rel,
             "prompt_tokens_per_s": B * S / (fwd_ms * 1e-3),
             "decode_steps": decode_steps, "decode_ms_per_step": round(dec_ms / decode_steps, 2),
             "decode_tokens_per_s": B * decode_steps / (dec_ms * 1e-3),

@@ -71,6 +71,11 @@ size_t block_grid_workspace_bytes(int64_t L, int64_t S, int64_t B, int64_t D);
 int block_grid_fwd(const flb_block_weights* W, const void* x, void* grids, int64_t L, int64_t S,
                    int64_t B, int64_t D, int64_t H, float eps, void* ws, size_t ws_bytes,
                    cudaStream_t s);
+int block_grid_fwd_ex(const flb_block_weights* W, const void* x, void* grids, int64_t L,
+                      int64_t S, int64_t B, int64_t D, int64_t H, float eps, void* ws,
+                      size_t ws_bytes, cudaStream_t s, int path, int drop_cta, int drop_bar,
+                      uint32_t spin_limit);
+int block_grid_status(const void* ws, cudaStream_t s);
 size_t block_grid_bwd_workspace_bytes(int64_t L, int64_t S, int64_t B, int64_t D);
 int block_grid_bwd(const flb_block_weights* W, const void* x, const void* grids,
                    const void* const* dgrids, float* dx, const flb_block_grads* G, int64_t L,
@@ -268,6 +273,45 @@ int flb_block_grid_fwd(const flb_block_weights* weights, const void* x, void* gr
     return fail(FLB_ERR_WORKSPACE, "block_grid_fwd: workspace smaller than flb_block_grid_workspace_bytes()");
   return block_grid_fwd(weights, x, grids, L, S, batch, D, heads, ln_eps, workspace,
                         workspace_bytes, as_stream(stream));
+}
+
+int flb_block_grid_fwd_ex(const flb_block_weights* weights, const void* x, void* grids,
+                          int64_t L, int64_t S, int64_t batch, int64_t D, int64_t heads,
+                          float ln_eps, void* workspace, size_t workspace_bytes, int path,
+                          void* stream) {
+  int st = check_block_args(weights, x, grids, L, S, batch, D, heads);
+  if (st != FLB_OK) return st;
+  if (path < FLB_BLOCK_PATH_AUTO || path > FLB_BLOCK_PATH_PERSISTENT)
+    return fail(FLB_ERR_SHAPE, "block_grid_fwd_ex: unknown path");
+  const size_t need = block_grid_workspace_bytes(L, S, batch, D);
+  if (!workspace || workspace_bytes < need)
+    return fail(FLB_ERR_WORKSPACE, "block_grid_fwd_ex: workspace smaller than flb_block_grid_workspace_bytes()");
+  return block_grid_fwd_ex(weights, x, grids, L, S, batch, D, heads, ln_eps, workspace,
+                           workspace_bytes, as_stream(stream), path, -1, -1, 0);
+}
+
+int flb_block_grid_status(const void* workspace, void* stream) {
+  if (!workspace) return fail(FLB_ERR_WORKSPACE, "block_grid_status: null workspace");
+  return block_grid_status(workspace, as_stream(stream));
+}
+
+int flb_block_grid_fwd_drop_barrier_test(const flb_block_weights* weights, const void* x,
+                                         void* grids, int64_t L, int64_t S, int64_t batch,
+                                         int64_t D, int64_t heads, float ln_eps, void* workspace,
+                                         size_t workspace_bytes, int64_t drop_cta,
+                                         int64_t drop_barrier, uint32_t spin_limit, void* stream) {
+  int st = check_block_args(weights, x, grids, L, S, batch, D, heads);
+  if (st != FLB_OK) return st;
+  const size_t need = block_grid_workspace_bytes(L, S, batch, D);
+  if (!workspace || workspace_bytes < need)
+    return fail(FLB_ERR_WORKSPACE, "block_grid drop test: workspace smaller than flb_block_grid_workspace_bytes()");
+  if (drop_cta < 0 || drop_cta >= num_sms() || drop_barrier < 0 || spin_limit < 1)
+    return fail(FLB_ERR_SHAPE, "block_grid drop test: drop_cta must name a CTA of the launch, drop_barrier >= 0, spin_limit >= 1");
+  st = block_grid_fwd_ex(weights, x, grids, L, S, batch, D, heads, ln_eps, workspace,
+                         workspace_bytes, as_stream(stream), FLB_BLOCK_PATH_PERSISTENT,
+                         (int)drop_cta, (int)drop_barrier, spin_limit);
+  if (st != FLB_OK) return st;
+  return block_grid_status(workspace, as_stream(stream));
 }
 
 size_t flb_block_grid_bwd_workspace_bytes(int64_t L, int64_t S, int64_t batch, int64_t D) {

@@ -51,6 +51,12 @@ PROTOTYPES = {
     "flb_block_grid_workspace_bytes": (_sz, [_i64, _i64, _i64, _i64]),
     "flb_block_grid_fwd": (_i32, [_vp, _vp, _vp, _i64, _i64, _i64, _i64, _i64, ctypes.c_float,
                                   _vp, _sz, _vp]),
+    "flb_block_grid_fwd_ex": (_i32, [_vp, _vp, _vp, _i64, _i64, _i64, _i64, _i64, ctypes.c_float,
+                                     _vp, _sz, _i32, _vp]),
+    "flb_block_grid_status": (_i32, [_vp, _vp]),
+    "flb_block_grid_fwd_drop_barrier_test": (_i32, [_vp, _vp, _vp, _i64, _i64, _i64, _i64, _i64,
+                                                    ctypes.c_float, _vp, _sz, _i64, _i64,
+                                                    ctypes.c_uint32, _vp]),
     "flb_block_grid_bwd_workspace_bytes": (_sz, [_i64, _i64, _i64, _i64]),
     "flb_block_grid_bwd": (_i32, [_vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _i64, _i64, _i64,
                                   _i64, _i64, ctypes.c_float, _vp, _sz, _vp]),

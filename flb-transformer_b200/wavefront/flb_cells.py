@@ -9,7 +9,8 @@ gate, three-token attention and residual kernels) instead of the per-tick gather
 index_select, vmapped cell and scatters. With gradients required it runs behind
 FLBGridFunction, whose backward is flb_block_grid_bwd (ticks in reverse, per-tick recompute,
 per-layer fp32 weight-gradient stacks). bf16 compute only (the reference model runs under bf16
-autocast).
+autocast). Setting engine.native_flb_path = 2 (FLB_BLOCK_PATH_PERSISTENT) runs the inference
+forward as one persistent tcgen05 kernel instead (batch 16, d_model a multiple of 128).
 """
 from __future__ import annotations
 
@@ -108,9 +109,11 @@ def native_flb_forward(engine, static_x: torch.Tensor, grids: torch.Tensor, weig
     w = weights or BlockWeightStacks(list(engine.layers))
     ws_bytes = nat.lib.flb_block_grid_workspace_bytes(L, S, B, D)
     ws = nat.workspace(ws_bytes, grids.device)
-    nat.check(nat.lib.flb_block_grid_fwd(
+    # engine.native_flb_path: FLB_BLOCK_PATH_* (0 = the default, 2 = the persistent kernel)
+    path = int(getattr(engine, "native_flb_path", 0))
+    nat.check(nat.lib.flb_block_grid_fwd_ex(
         ctypes.cast(ctypes.pointer(w.struct), ctypes.c_void_p), static_x.data_ptr(), grids.data_ptr(), L, S, B, D, w.heads,
-        w.eps, nat.ptr(ws), ws_bytes, nat.stream_of(grids)), "flb_block_grid_fwd")
+        w.eps, nat.ptr(ws), ws_bytes, path, nat.stream_of(grids)), "flb_block_grid_fwd_ex")
 
 
 # parameter name inside a block -> (gradient stack, slice of its per-layer entry)

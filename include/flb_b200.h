@@ -276,15 +276,48 @@ typedef struct flb_block_weights {
 
 size_t flb_block_grid_workspace_bytes(int64_t L, int64_t S, int64_t batch, int64_t D);
 
-/* Whole-grid forward of FLB block cells, tick by tick on `stream` (no host synchronisation).
+/* Whole-grid forward of FLB block cells on `stream` (no host synchronisation).
  * x: bf16 [batch, S, D] (row 0's top input). grids: bf16 [4, L*S + L, batch, D], the engine's
  * port grids (cell l*S + t; the last L rows are its boundary dock and are not touched); every
  * cell of ports 0-3 is written: h_x, h_lat, h_fdbk and the auxiliary loss term. D must be a
  * multiple of 16 and of `heads`, D <= 1024 and D / heads <= 128; ln_eps is the LayerNorms'
- * epsilon. */
+ * epsilon. Runs tick by tick (own kernels and cuBLAS projections); flb_block_grid_fwd_ex also
+ * offers the persistent path. */
 int flb_block_grid_fwd(const flb_block_weights* weights, const void* x, void* grids,
                        int64_t L, int64_t S, int64_t batch, int64_t D, int64_t heads,
                        float ln_eps, void* workspace, size_t workspace_bytes, void* stream);
+
+#define FLB_BLOCK_PATH_AUTO       0  /* the faster path measured on B200: tick by tick */
+#define FLB_BLOCK_PATH_TICKS      1  /* tick by tick */
+#define FLB_BLOCK_PATH_PERSISTENT 2  /* persistent; FLB_ERR_UNSUPPORTED for other shapes */
+
+/* flb_block_grid_fwd with the evaluation path chosen (no reference counterpart: the reference
+ * has one path, the engine's tick loop). The persistent path (batch 16, D a multiple of 128 up
+ * to 1024) evaluates the whole grid in ONE cooperative kernel, one CTA per SM: every projection
+ * on tcgen05 tensor cores with weights streamed by TMA, the elementwise steps fused into its
+ * activation loads and epilogues, grid barriers between a tick's five stages. It is
+ * deterministic (bit-identical across runs). */
+int flb_block_grid_fwd_ex(const flb_block_weights* weights, const void* x, void* grids,
+                          int64_t L, int64_t S, int64_t batch, int64_t D, int64_t heads,
+                          float ln_eps, void* workspace, size_t workspace_bytes, int path,
+                          void* stream);
+
+/* Error word of the last persistent forward run with `workspace` (no reference counterpart):
+ * synchronises `stream`, returns FLB_ERR_TIMEOUT if a bounded wait in the kernel gave up (the
+ * grids are then incomplete), else FLB_OK. */
+int flb_block_grid_status(const void* workspace, void* stream);
+
+/* Failure-detection check of the persistent forward's grid barriers (no reference
+ * counterpart). Runs the persistent forward with CTA drop_cta never arriving at its
+ * drop_barrier-th grid barrier and the barrier-poll bound lowered to spin_limit: the other CTAs
+ * give up, record the error word and raise the abort flag, every CTA drains its copies and MMAs
+ * and returns, and the call returns FLB_ERR_TIMEOUT (read back synchronously) with the context
+ * still usable. No GPU fault or trap is involved. */
+int flb_block_grid_fwd_drop_barrier_test(const flb_block_weights* weights, const void* x,
+                                         void* grids, int64_t L, int64_t S, int64_t batch,
+                                         int64_t D, int64_t heads, float ln_eps, void* workspace,
+                                         size_t workspace_bytes, int64_t drop_cta,
+                                         int64_t drop_barrier, uint32_t spin_limit, void* stream);
 
 /* Gradient accumulators of flb_block_grid_bwd: float32 stacks shaped like the matching fields
  * of flb_block_weights (w_qkv: [L, 3D, D], v_a: [L, H, D/H]). Gradients are ADDED into them. */

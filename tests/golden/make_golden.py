@@ -191,10 +191,9 @@ def wavefront_goldens():
     return out
 
 
-def flb_model_goldens():
-    """The reference FLB_Transformer (models/FLB_Model.py) end to end on CPU, eval mode, on a
-    small configuration: its attention op replaced by the reference's eager ground truth
-    (the Triton kernel has no CPU path), the engine as in wavefront_goldens()."""
+def _reference_flb_on_cpu():
+    """models.FLB_Model with its attention op replaced by the reference's eager ground truth
+    (the Triton kernel has no CPU path) and the engine's gather by fetch_mapped_context."""
     import wavefront.wavefront_engine as we
     import models.FLB_Model as fm
     from kernels.kernel_tests import pure_torch_additive_attention
@@ -213,6 +212,13 @@ def flb_model_goldens():
 
     we.run_fetch_kernel = cpu_fetch
     fm.fused_additive_attention = pure_torch_additive_attention
+    return fm
+
+
+def flb_model_goldens():
+    """The reference FLB_Transformer (models/FLB_Model.py) end to end on CPU, eval mode, on a
+    small configuration, the engine as in wavefront_goldens()."""
+    fm = _reference_flb_on_cpu()
     torch.manual_seed(21)
     V, D, L, S, B = 40, 32, 3, 5, 2
     model = fm.FLB_Transformer(V, hidden_dim=D, num_layers=L, seq_len=S, batch_size=B)
@@ -234,13 +240,34 @@ def flb_model_goldens():
                        if p.grad is not None})
 
 
-def main():
-    torch.save(attention_goldens(), os.path.join(HERE, "attention.pt"))
-    torch.save(wavefront_goldens(), os.path.join(HERE, "wavefront.pt"))
-    torch.save(flb_model_goldens(), os.path.join(HERE, "flb_model.pt"))
-    for f in ("attention.pt", "wavefront.pt", "flb_model.pt"):
+def flb_model_b16_goldens():
+    """The reference FLB_Transformer forward (eval, float32, CPU) at batch 16 and d_model 128 (its
+    8 heads of 16): the shape class of the persistent native forward. The weights are not stored:
+    flb_weights.set_hashed_weights(model, 5) regenerates them (bf16-representable values)."""
+    from flb_weights import set_hashed_weights
+    fm = _reference_flb_on_cpu()
+    V, D, L, S, B = 40, 128, 3, 4, 16
+    model = fm.FLB_Transformer(V, hidden_dim=D, num_layers=L, seq_len=S, batch_size=B)
+    set_hashed_weights(model, 5)
+    model.eval()
+    tokens = torch.randint(0, V, (B, S), generator=torch.Generator().manual_seed(6))
+    with torch.no_grad():
+        logits, aux, (lat, fdbk) = model(tokens)
+    return dict(config=dict(vocab=V, hidden=D, layers=L, seq_len=S, batch=B, weight_seed=5),
+                tokens=tokens, logits=logits.clone(), aux_loss=aux.clone(),
+                next_lat=lat.clone(), next_fdbk=fdbk.clone())
+
+
+GOLDENS = {"attention.pt": attention_goldens, "wavefront.pt": wavefront_goldens,
+           "flb_model.pt": flb_model_goldens, "flb_model_b16.pt": flb_model_b16_goldens}
+
+
+def main(names):
+    """python make_golden.py [file ...]: regenerate the named fixtures (default: all)."""
+    for f in names or list(GOLDENS):
+        torch.save(GOLDENS[f](), os.path.join(HERE, f))
         print(f, os.path.getsize(os.path.join(HERE, f)), "bytes")
 
 
 if __name__ == "__main__":
-    main()
+    main(sys.argv[1:])
