@@ -317,21 +317,8 @@ grid_sweep_kernel(const __grid_constant__ CUtensorMap tmWa, const __grid_constan
           if (!lready) issue_left();
           if (!tready) issue_top();
         }
-        const uint32_t wa = smem_u32(sm + Cfg::OFF_W), ia = smem_u32(sIn);
-        auto mma_range = [&](int k0, int k1) {
-#pragma unroll
-          for (int kk = k0; kk < k1; ++kk) {
-            const uint64_t adesc = make_smem_desc(wa + (kk >> 2) * Cfg::W_ATOM + (kk & 3) * 32, 16, 1024, kSwizzle128B);
-            const uint64_t bdesc = make_smem_desc(ia + (kk >> 2) * B * 128 + (kk & 3) * 32, 16, 1024, kSwizzle128B);
-            umma_f16(tmem, adesc, bdesc, idesc, kk > 0 ? 1u : 0u);
-          }
-        };
-        // same-row half of K first: it runs while the other-row tile may still be in flight
-        if (!mbar_wait(&bar_l, n_cell & 1u, kWaitLimit)) atomicExch(p.err, 3);
-        tc_fence_after();
-        mma_range(0, H / 16);
-        if (!mbar_wait(&bar_t, n_cell & 1u, kWaitLimit)) atomicExch(p.err, 3);
         if (halo_in) {
+          if (!mbar_wait(&bar_t, n_cell & 1u, kWaitLimit)) atomicExch(p.err, 3);
           if (p.save_top) {  // this CTA's feature half of the received rows, back out of shared memory
 #pragma unroll
             for (int a = half * 2; a < half * 2 + 2; ++a)
@@ -340,17 +327,35 @@ grid_sweep_kernel(const __grid_constant__ CUtensorMap tmWa, const __grid_constan
           }
           st_release_sys(p.halo_in_ack + c * 2 + half, p.epoch);
         }
-        tc_fence_after();
-        mma_range(H / 16, 2 * H / 16);
         if (halo_out) {  // the neighbour has loaded the previous epoch's column c: it may be rewritten
           bool ok_ack = true;
           for (int hh = 0; hh < NH; ++hh)
             ok_ack &= wait_flag_sys(p.halo_out_ack + c * 2 + hh, p.epoch - 1, p.spin_limit);
           if (!ok_ack) atomicExch(p.err, 6);
         }
-        umma_commit(&bar_mma);
         // the next cell's loads overwrite these rows: the store must have read them by then
         if (halo_in && p.save_top) bulk_wait_read_all();
+      } else if (tid == 32) {
+        // The MMAs are issued by their own thread (warp 1) so that the same-row half of K runs
+        // as soon as its tile has landed, while thread 0 still polls for the other-row input
+        // (an M = 128 K-step takes ~120 cycles to issue whatever N is: the same-row half is
+        // ~0.6 us at H = 256).
+        const uint32_t wa = smem_u32(sm + Cfg::OFF_W), ia = smem_u32(sm + Cfg::OFF_IN);
+        auto mma_range = [&](int k0, int k1) {
+#pragma unroll
+          for (int kk = k0; kk < k1; ++kk) {
+            const uint64_t adesc = make_smem_desc(wa + (kk >> 2) * Cfg::W_ATOM + (kk & 3) * 32, 16, 1024, kSwizzle128B);
+            const uint64_t bdesc = make_smem_desc(ia + (kk >> 2) * B * 128 + (kk & 3) * 32, 16, 1024, kSwizzle128B);
+            umma_f16(tmem, adesc, bdesc, idesc, kk > 0 ? 1u : 0u);
+          }
+        };
+        if (!mbar_wait(&bar_l, n_cell & 1u, kWaitLimit)) atomicExch(p.err, 3);
+        tc_fence_after();
+        mma_range(0, H / 16);
+        if (!mbar_wait(&bar_t, n_cell & 1u, kWaitLimit)) atomicExch(p.err, 3);
+        tc_fence_after();
+        mma_range(H / 16, 2 * H / 16);
+        umma_commit(&bar_mma);
       }
       // a halo wait lasts as long as the other GPU takes to get there (its launch may start late):
       // hold the CTA here, behind thread 0's bounded spins, rather than in the MMA barrier's
@@ -371,34 +376,43 @@ grid_sweep_kernel(const __grid_constant__ CUtensorMap tmWa, const __grid_constan
         ++ep_used;
       }
       const float bias_f = p.reverse ? 0.f : p.bias[(int64_t)g * H + f];
+      // All 32 columns' arithmetic first, then the stores: the per-column chains (shared-memory
+      // operand, tanh, convert) are independent and overlap instead of running one after another.
       for (int cb = 0; cb < B; cb += 32) {
         uint32_t acc[32];
         tmem_ld32(tmem + ((uint32_t)(warp * 32) << 16) + cb, acc);
         tmem_wait_ld();
         const int nb = min(32, B - cb);
+        __nv_bfloat16 ov[32];
+        if (!p.reverse) {
+          const float* sEf = reinterpret_cast<const float*>(sE);
+#pragma unroll
+          for (int j = 0; j < 32; ++j) {
+            const float a = (stage_add && j < nb) ? sEf[(cb + j) * 128 + fl] : 0.f;
+            ov[j] = __float2bfloat16_rn(tanh_approx(__uint_as_float(acc[j]) + bias_f + a));
+          }
+        } else {
+          const __nv_bfloat16* sH = reinterpret_cast<const __nv_bfloat16*>(sE);
+          const __nv_bfloat16* sD = reinterpret_cast<const __nv_bfloat16*>(sE + B * 128 * 2);
+#pragma unroll
+          for (int j = 0; j < 32; ++j) {
+            float dz = 0.f;
+            if (j < nb) {
+              const float hv = __bfloat162float(sH[(cb + j) * 128 + fl]);
+              const float dhv = __bfloat162float(sD[(cb + j) * 128 + fl]);
+              dz = (__uint_as_float(acc[j]) + dhv) * (1.f - hv * hv);
+            }
+            ov[j] = __float2bfloat16_rn(dz);
+            db_acc += dz;  // zero past nb: the sum over the batch is unchanged
+          }
+        }
 #pragma unroll
         for (int j = 0; j < 32; ++j) {
           if (j >= nb) break;
           const int b = cb + j;
-          const int64_t o = (cell * B + b) * H + f;
-          float z = __uint_as_float(acc[j]);
-          if (!p.reverse) {
-            z += bias_f;
-            if (stage_add) z += reinterpret_cast<const float*>(sE)[b * 128 + fl];
-            const __nv_bfloat16 hb = __float2bfloat16_rn(tanh_approx(z));
-            p.out[o] = hb;
-            if (halo_out) p.halo_out[((int64_t)c * B + b) * H + f] = hb;
-          } else {
-            const float hv = __bfloat162float(reinterpret_cast<const __nv_bfloat16*>(sE)[b * 128 + fl]);
-            const float dhv = __bfloat162float(
-                reinterpret_cast<const __nv_bfloat16*>(sE + B * 128 * 2)[b * 128 + fl]);
-            const float dz = (z + dhv) * (1.f - hv * hv);
-            const __nv_bfloat16 dzb = __float2bfloat16_rn(dz);
-            p.out[o] = dzb;
-            if (halo_out) p.halo_out[((int64_t)c * B + b) * H + f] = dzb;
-            if (p.out2) p.out2[(((int64_t)b * R + r) * C + c) * H + f] = dzb;
-            db_acc += dz;
-          }
+          p.out[(cell * B + b) * H + f] = ov[j];
+          if (halo_out) p.halo_out[((int64_t)c * B + b) * H + f] = ov[j];
+          if (p.reverse && p.out2) p.out2[(((int64_t)b * R + r) * C + c) * H + f] = ov[j];
         }
       }
       tc_fence_before();
