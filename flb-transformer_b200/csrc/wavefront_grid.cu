@@ -226,6 +226,8 @@ grid_sweep_kernel(const __grid_constant__ CUtensorMap tmWa, const __grid_constan
       if (!mbar_wait(&bar_w, n_wload & 1u, kWaitLimit)) atomicExch(p.err, 1);
       ++n_wload;
     }
+    // this thread's bias for the row (loaded once per row, off the cells' chain)
+    const float bias_f = p.reverse ? 0.f : p.bias[(int64_t)g * H + f];
     if (p.reverse && db_group != g) {  // flush the bias-gradient partial of the previous group
       if (db_group >= 0) atomicAdd(p.dbias + (int64_t)db_group * H + f, db_acc);
       db_acc = 0.f;
@@ -375,7 +377,6 @@ grid_sweep_kernel(const __grid_constant__ CUtensorMap tmWa, const __grid_constan
           atomicExch(p.err, 5);
         ++ep_used;
       }
-      const float bias_f = p.reverse ? 0.f : p.bias[(int64_t)g * H + f];
       // All 32 columns' arithmetic first, then the stores: the per-column chains (shared-memory
       // operand, tanh, convert) are independent and overlap instead of running one after another.
       for (int cb = 0; cb < B; cb += 32) {
