@@ -407,14 +407,29 @@ grid_sweep_kernel(const __grid_constant__ CUtensorMap tmWa, const __grid_constan
             db_acc += dz;  // zero past nb: the sum over the batch is unchanged
           }
         }
+        // Out through shared memory: the warp's 32 x 32 tile (features x batch rows) is written
+        // into this cell's operand stage, whose contents every warp has read by the barrier, and
+        // leaves as 16-byte row chunks (4 stores per thread instead of 32 two-byte ones).
+        __syncthreads();
+        __nv_bfloat16* stg = reinterpret_cast<__nv_bfloat16*>(const_cast<uint8_t*>(sE)) + warp * 1024;
 #pragma unroll
-        for (int j = 0; j < 32; ++j) {
-          if (j >= nb) break;
-          const int b = cb + j;
-          p.out[(cell * B + b) * H + f] = ov[j];
-          if (halo_out) p.halo_out[((int64_t)c * B + b) * H + f] = ov[j];
-          if (p.reverse && p.out2) p.out2[(((int64_t)b * R + r) * C + c) * H + f] = ov[j];
+        for (int j = 0; j < 32; ++j) stg[j * 32 + lane] = ov[j];
+        __syncwarp();
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+          const int row = (lane >> 2) + 8 * i, ch = lane & 3;
+          if (row < nb) {
+            const uint4 v = *reinterpret_cast<const uint4*>(stg + row * 32 + ch * 8);
+            const int b = cb + row;
+            const int fo = half * 128 + warp * 32 + ch * 8;
+            *reinterpret_cast<uint4*>(p.out + (cell * B + b) * H + fo) = v;
+            if (halo_out) *reinterpret_cast<uint4*>(p.halo_out + ((int64_t)c * B + b) * H + fo) = v;
+            if (p.reverse && p.out2)
+              *reinterpret_cast<uint4*>(p.out2 + (((int64_t)b * R + r) * C + c) * H + fo) = v;
+          }
         }
+        fence_async_shared();  // a later TMA load overwrites this stage
+        __syncwarp();
       }
       tc_fence_before();
       __syncthreads();
