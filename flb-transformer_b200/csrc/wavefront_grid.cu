@@ -103,6 +103,8 @@ __device__ __forceinline__ void tma_load_4d(void* dst, const void* tmap, uint64_
       : "memory");
 }
 
+constexpr int kGridThreads = 256;  // 8 warps: thread 0 polls, thread 32 issues MMAs, all run the epilogue
+
 template <int H>
 struct GridCfg {
   static constexpr int KATOMS = 2 * H / 64;          // 64-element K atoms of [left | top]
@@ -155,7 +157,7 @@ struct GridParams {
 // inputs are h[r][c-1] (left) and h[r-1][c] (top). Backward (reverse = 1): rows descend, cells
 // walk left, inputs are dz[r][c+1] and dz[r+1][c], weights are the transposed W_l^T, W_t^T.
 template <int H>
-__global__ void __launch_bounds__(128, 1)
+__global__ void __launch_bounds__(kGridThreads, 1)
 grid_sweep_kernel(const __grid_constant__ CUtensorMap tmWa, const __grid_constant__ CUtensorMap tmWb,
                   const __grid_constant__ CUtensorMap tmIn, const __grid_constant__ CUtensorMap tmTop,
                   const __grid_constant__ CUtensorMap tmE1, const __grid_constant__ CUtensorMap tmE2,
@@ -197,7 +199,8 @@ grid_sweep_kernel(const __grid_constant__ CUtensorMap tmWa, const __grid_constan
   tc_fence_after();
   const uint32_t tmem = tmem_slot;
   const uint32_t idesc = make_idesc_f16(128, B, 1, 0, 0);
-  const int f = half * 128 + warp * 32 + lane;  // this thread's output feature
+  const int wq = warp & 3;  // TMEM lane quarter: features 32 wq .. +31 of the half
+  const int f = half * 128 + wq * 32 + lane;  // this thread's output feature
   uint32_t n_wload = 0, n_cell = 0;
   uint32_t ep_issued = 0, ep_used = 0;  // epilogue operand tiles issued / consumed (stage = k % S)
   const int S = p.ep_stages;
@@ -371,57 +374,60 @@ grid_sweep_kernel(const __grid_constant__ CUtensorMap tmWa, const __grid_constan
       // ---- epilogue: this thread owns feature f for every batch element --------------------
       const int64_t cell = (int64_t)r * C + c;
       const uint8_t* sE = sm + Cfg::off_ep(B) + (int)(ep_used % (uint32_t)S) * Cfg::ep_bytes(B);
-      const int fl = warp * 32 + lane;  // feature within this CTA's half
+      const int fl = wq * 32 + lane;  // feature within this CTA's half
+      const int cg = warp >> 2;       // column group: batch rows 16 cg .. +15 of each 32
       if (p.reverse || stage_add) {
         if (!mbar_wait(&bar_ep[ep_used % (uint32_t)S], (ep_used / (uint32_t)S) & 1u, kWaitLimit))
           atomicExch(p.err, 5);
         ++ep_used;
       }
-      // All 32 columns' arithmetic first, then the stores: the per-column chains (shared-memory
-      // operand, tanh, convert) are independent and overlap instead of running one after another.
+      // Eight warps: two per TMEM lane quarter, each with 16 of every 32 batch columns, so that
+      // each scheduler has two warps to overlap the per-column chains (shared-memory operand,
+      // tanh, convert). All 16 columns' arithmetic first, then the stores.
       for (int cb = 0; cb < B; cb += 32) {
-        uint32_t acc[32];
-        tmem_ld32(tmem + ((uint32_t)(warp * 32) << 16) + cb, acc);
+        const int c0 = cb + 16 * cg;           // first batch row of this warp
+        const int nb = max(0, min(16, B - c0));
+        uint32_t acc[16];
+        tmem_ld16(tmem + ((uint32_t)(wq * 32) << 16) + c0, acc);
         tmem_wait_ld();
-        const int nb = min(32, B - cb);
-        __nv_bfloat16 ov[32];
+        __nv_bfloat16 ov[16];
         if (!p.reverse) {
           const float* sEf = reinterpret_cast<const float*>(sE);
 #pragma unroll
-          for (int j = 0; j < 32; ++j) {
-            const float a = (stage_add && j < nb) ? sEf[(cb + j) * 128 + fl] : 0.f;
+          for (int j = 0; j < 16; ++j) {
+            const float a = (stage_add && j < nb) ? sEf[(c0 + j) * 128 + fl] : 0.f;
             ov[j] = __float2bfloat16_rn(tanh_approx(__uint_as_float(acc[j]) + bias_f + a));
           }
         } else {
           const __nv_bfloat16* sH = reinterpret_cast<const __nv_bfloat16*>(sE);
           const __nv_bfloat16* sD = reinterpret_cast<const __nv_bfloat16*>(sE + B * 128 * 2);
 #pragma unroll
-          for (int j = 0; j < 32; ++j) {
+          for (int j = 0; j < 16; ++j) {
             float dz = 0.f;
             if (j < nb) {
-              const float hv = __bfloat162float(sH[(cb + j) * 128 + fl]);
-              const float dhv = __bfloat162float(sD[(cb + j) * 128 + fl]);
+              const float hv = __bfloat162float(sH[(c0 + j) * 128 + fl]);
+              const float dhv = __bfloat162float(sD[(c0 + j) * 128 + fl]);
               dz = (__uint_as_float(acc[j]) + dhv) * (1.f - hv * hv);
             }
             ov[j] = __float2bfloat16_rn(dz);
             db_acc += dz;  // zero past nb: the sum over the batch is unchanged
           }
         }
-        // Out through shared memory: the warp's 32 x 32 tile (features x batch rows) is written
+        // Out through shared memory: the warp's 16 x 32 tile (batch rows x features) is written
         // into this cell's operand stage, whose contents every warp has read by the barrier, and
-        // leaves as 16-byte row chunks (4 stores per thread instead of 32 two-byte ones).
+        // leaves as 16-byte row chunks (2 stores per thread instead of 16 two-byte ones).
         __syncthreads();
-        __nv_bfloat16* stg = reinterpret_cast<__nv_bfloat16*>(const_cast<uint8_t*>(sE)) + warp * 1024;
+        __nv_bfloat16* stg = reinterpret_cast<__nv_bfloat16*>(const_cast<uint8_t*>(sE)) + warp * 512;
 #pragma unroll
-        for (int j = 0; j < 32; ++j) stg[j * 32 + lane] = ov[j];
+        for (int j = 0; j < 16; ++j) stg[j * 32 + lane] = ov[j];
         __syncwarp();
 #pragma unroll
-        for (int i = 0; i < 4; ++i) {
+        for (int i = 0; i < 2; ++i) {
           const int row = (lane >> 2) + 8 * i, ch = lane & 3;
           if (row < nb) {
             const uint4 v = *reinterpret_cast<const uint4*>(stg + row * 32 + ch * 8);
-            const int b = cb + row;
-            const int fo = half * 128 + warp * 32 + ch * 8;
+            const int b = c0 + row;
+            const int fo = half * 128 + wq * 32 + ch * 8;
             *reinterpret_cast<uint4*>(p.out + (cell * B + b) * H + fo) = v;
             if (halo_out) *reinterpret_cast<uint4*>(p.halo_out + ((int64_t)c * B + b) * H + fo) = v;
             if (p.reverse && p.out2)
@@ -550,7 +556,7 @@ int launch_sweep(const CUtensorMap& wa, const CUtensorMap& wb, const CUtensorMap
                            "grid_sweep smem attribute");
   if (st != FLB_OK) return st;
   int per_sm = 0;
-  cudaError_t e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, grid_sweep_kernel<H>, 128, smem);
+  cudaError_t e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, grid_sweep_kernel<H>, kGridThreads, smem);
   if (e != cudaSuccess || per_sm < 1) return fail(FLB_ERR_LAUNCH, "grid_sweep: kernel does not fit on an SM");
   constexpr int NH = H / 128;
   // every CTA must be resident at once (they wait on one another): cap the workers
@@ -558,7 +564,7 @@ int launch_sweep(const CUtensorMap& wa, const CUtensorMap& wb, const CUtensorMap
   int workers = std::min<int>(p.R, capacity / NH);
   if (workers < 1) return fail(FLB_ERR_LAUNCH, "grid_sweep: not enough resident CTAs");
   *grid_ctas = workers * NH;
-  grid_sweep_kernel<H><<<workers * NH, 128, smem, s>>>(wa, wb, in, top, e1, e2, save, p);
+  grid_sweep_kernel<H><<<workers * NH, kGridThreads, smem, s>>>(wa, wb, in, top, e1, e2, save, p);
   count_launches(1);
   return check_cuda(cudaGetLastError(), "grid_sweep launch");
 }
