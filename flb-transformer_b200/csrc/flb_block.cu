@@ -5,7 +5,8 @@
 // launch stream: cell (l, t) runs at tick T = l + 2t, so a tick's cells are l = l0, l0+2, ...
 // with t = (T - l) / 2, and their flat grid rows l*S + t form an arithmetic progression of step
 // 2S - 1. Per tick, for all its cells at once:
-//   1. LayerNorm (fp32 statistics) of the left and bottom-left neighbours   [own kernel]
+//   1. LayerNorm (fp32 statistics) of the left and bottom-left neighbours   [fused into the
+//      output kernel (8.) of the ticks that produce them; own kernel in the backward's recompute]
 //   2. lat_prior = P_lat LN(left), fdbk_prior = P_fb LN(diag)              [strided GEMMs]
 //   3. lat' = lat_prior * sigmoid(G_L fdbk_prior + b_L)                    [GEMM + own kernel]
 //   4. x'   = top * sigmoid(G_X lat' + b_X)                                [GEMM + own kernel]
@@ -245,43 +246,163 @@ __global__ void blk_attn3_kernel(const bf16* __restrict__ qkv, const float* __re
   attn3_task(qkv, v_a, att, l0, B, D, H, task, lane);
 }
 
-// 8. residuals and the auxiliary loss, written into the four port grids at the tick's cells.
-//    Grid: x over bf16 pairs of a row, y over the tick's (cell, batch) rows.
-__global__ void blk_out_kernel(const bf16* __restrict__ o, const bf16* __restrict__ lat_prior,
-                               const bf16* __restrict__ tok, const bf16* __restrict__ x,
-                               bf16* __restrict__ grids, int64_t port_stride, int T, int l0,
-                               int S, int B, int D) {
+// 8. residuals and the auxiliary loss into the four port grids, with the next ticks'
+//    LayerNorms fused in: a block per (cell, batch row) writes the four port outputs of the
+//    row and normalises the two it has just produced for their consumers, so that no LayerNorm
+//    launch opens a forward tick:
+//    h_lat of cell (l, t) is the left input of (l, t+1) at tick T+2 (norm_lat of layer l),
+//    h_fdbk the bottom-left input of (l-1, t+1) at tick T+1 (norm_fdbk of layer l-1). They go
+//    to a ring of three LayerNorm buffers [slot = consumer tick % 3][left | diag][layer][B][D],
+//    which blk_ln_init_kernel fills with the LayerNorm biases (the normalised zero boundary rows,
+//    which no producer overwrites before their consumer's tick). Statistics over the bf16
+//    values the port grids hold.
+// One (cell, batch row) per block, one 16-byte chunk (8 features) per thread; LayerNorm
+// statistics by warp sums and a fixed-order sum over the block's warps.
+constexpr int kOutLnMaxWarps = 4;  // D <= 1024: 128 chunks
+
+__device__ __forceinline__ void ln_chunk_store(const float (&v)[8], float mean, float rstd,
+                                               const float4 (&w)[2], const float4 (&bb)[2],
+                                               bf16* dst, int c) {
+  const float wv[8] = {w[0].x, w[0].y, w[0].z, w[0].w, w[1].x, w[1].y, w[1].z, w[1].w};
+  const float bv[8] = {bb[0].x, bb[0].y, bb[0].z, bb[0].w, bb[1].x, bb[1].y, bb[1].z, bb[1].w};
+  uint32_t o[4];
+#pragma unroll
+  for (int e = 0; e < 4; ++e) {
+    const __nv_bfloat162 h = __floats2bfloat162_rn((v[2 * e] - mean) * rstd * wv[2 * e] + bv[2 * e],
+                                                   (v[2 * e + 1] - mean) * rstd * wv[2 * e + 1] + bv[2 * e + 1]);
+    o[e] = *reinterpret_cast<const uint32_t*>(&h);
+  }
+  reinterpret_cast<uint4*>(dst)[c] = make_uint4(o[0], o[1], o[2], o[3]);
+}
+
+__global__ void blk_out_ln_kernel(const bf16* __restrict__ o, const bf16* __restrict__ lat_prior,
+                                  const bf16* __restrict__ tok, const bf16* __restrict__ x,
+                                  bf16* __restrict__ grids, int64_t port_stride,
+                                  bf16* __restrict__ lnr, const float* __restrict__ lw0,
+                                  const float* __restrict__ lb0, const float* __restrict__ lw1,
+                                  const float* __restrict__ lb1, float eps, int T, int l0, int n,
+                                  int L, int S, int B, int D) {
+  __shared__ float red[4][kOutLnMaxWarps];  // per warp: sum and sum of squares of h_lat, h_fdbk
+  const int row = blockIdx.x;               // i * B + b
+  const int c = threadIdx.x, warp = c >> 5, lane = c & 31, nw = blockDim.x >> 5;
+  const int i = row / B, b = row - i * B;
+  const int l = l0 + 2 * i, t = (T - l) / 2;
+  const int nch = D / 8;
+  const bool act = c < nch;
+  // the LayerNorm parameters do not depend on the previous kernel: load them before the wait
+  float4 wl[2], bl[2], wf[2], bf[2];
+  if (act) {
+    const float4* p0 = reinterpret_cast<const float4*>(lw0 + (int64_t)l * D) + 2 * c;
+    const float4* p1 = reinterpret_cast<const float4*>(lb0 + (int64_t)l * D) + 2 * c;
+    wl[0] = __ldg(p0); wl[1] = __ldg(p0 + 1); bl[0] = __ldg(p1); bl[1] = __ldg(p1 + 1);
+    if (l >= 1) {
+      const float4* p2 = reinterpret_cast<const float4*>(lw1 + (int64_t)(l - 1) * D) + 2 * c;
+      const float4* p3 = reinterpret_cast<const float4*>(lb1 + (int64_t)(l - 1) * D) + 2 * c;
+      wf[0] = __ldg(p2); wf[1] = __ldg(p2 + 1); bf[0] = __ldg(p3); bf[1] = __ldg(p3 + 1);
+    }
+  }
   pdl_wait();
+  const int64_t r3 = (int64_t)row * 3;
+  const int64_t off = (cell_row(l, t, S) * B + b) * D;
+  float hl[8], hf[8];
+  float sl = 0.f, ssl = 0.f, sf = 0.f, ssf = 0.f;
+  if (act) {
+    auto ld8 = [&](const bf16* p, float (&f)[8]) {
+      const uint4 u = reinterpret_cast<const uint4*>(p)[c];
+      const uint32_t* r = reinterpret_cast<const uint32_t*>(&u);
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        const float2 v = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&r[e]));
+        f[2 * e] = v.x;
+        f[2 * e + 1] = v.y;
+      }
+    };
+    float o0[8], o1[8], o2[8], tp[8], lp[8], fp[8];
+    ld8(o + r3 * D, o0);
+    ld8(o + (r3 + 1) * D, o1);
+    ld8(o + (r3 + 2) * D, o2);
+    ld8(top_row(grids, x, l, t, b, S, B, D), tp);
+    ld8(lat_prior + (int64_t)row * D, lp);
+    ld8(tok + (r3 + 2) * D, fp);
+    uint32_t px[4], pl[4], pf[4], pa[4];
+#pragma unroll
+    for (int e = 0; e < 4; ++e) {
+      // the outputs as stored (bf16), as the aux term and the next LayerNorms see them
+      const __nv_bfloat162 hx = __floats2bfloat162_rn(o0[2 * e] + tp[2 * e], o0[2 * e + 1] + tp[2 * e + 1]);
+      const __nv_bfloat162 hl2 = __floats2bfloat162_rn(o1[2 * e] + lp[2 * e], o1[2 * e + 1] + lp[2 * e + 1]);
+      const __nv_bfloat162 hf2 = __floats2bfloat162_rn(o2[2 * e] + fp[2 * e], o2[2 * e + 1] + fp[2 * e + 1]);
+      const float2 hlf = __bfloat1622float2(hl2), hff = __bfloat1622float2(hf2);
+      const float ax = (lp[2 * e] - hlf.x) * (lp[2 * e] - hlf.x) + (fp[2 * e] - hff.x) * (fp[2 * e] - hff.x);
+      const float ay = (lp[2 * e + 1] - hlf.y) * (lp[2 * e + 1] - hlf.y) +
+                       (fp[2 * e + 1] - hff.y) * (fp[2 * e + 1] - hff.y);
+      const __nv_bfloat162 a2 = __floats2bfloat162_rn(ax, ay);
+      px[e] = *reinterpret_cast<const uint32_t*>(&hx);
+      pl[e] = *reinterpret_cast<const uint32_t*>(&hl2);
+      pf[e] = *reinterpret_cast<const uint32_t*>(&hf2);
+      pa[e] = *reinterpret_cast<const uint32_t*>(&a2);
+      hl[2 * e] = hlf.x;
+      hl[2 * e + 1] = hlf.y;
+      hf[2 * e] = hff.x;
+      hf[2 * e + 1] = hff.y;
+      sl += hlf.x + hlf.y;
+      ssl += hlf.x * hlf.x + hlf.y * hlf.y;
+      sf += hff.x + hff.y;
+      ssf += hff.x * hff.x + hff.y * hff.y;
+    }
+    reinterpret_cast<uint4*>(grids + off)[c] = make_uint4(px[0], px[1], px[2], px[3]);
+    reinterpret_cast<uint4*>(grids + port_stride + off)[c] = make_uint4(pl[0], pl[1], pl[2], pl[3]);
+    reinterpret_cast<uint4*>(grids + 2 * port_stride + off)[c] = make_uint4(pf[0], pf[1], pf[2], pf[3]);
+    reinterpret_cast<uint4*>(grids + 3 * port_stride + off)[c] = make_uint4(pa[0], pa[1], pa[2], pa[3]);
+  }
+  if (t + 1 >= S) return;  // the last column has no consumers (block-uniform)
+  sl = warp_sum(sl);
+  ssl = warp_sum(ssl);
+  sf = warp_sum(sf);
+  ssf = warp_sum(ssf);
+  if (lane == 0) {
+    red[0][warp] = sl;
+    red[1][warp] = ssl;
+    red[2][warp] = sf;
+    red[3][warp] = ssf;
+  }
+  __syncthreads();
+  if (!act) return;
+  float tot[4] = {0.f, 0.f, 0.f, 0.f};
+  for (int w = 0; w < nw; ++w)
+#pragma unroll
+    for (int q = 0; q < 4; ++q) tot[q] += red[q][w];
+  const int64_t LBD = (int64_t)L * B * D;
+  {
+    const float mean = tot[0] / D;
+    const float rstd = rsqrtf(fmaxf(tot[1] / D - mean * mean, 0.f) + eps);
+    ln_chunk_store(hl, mean, rstd, wl, bl,
+                   lnr + (int64_t)((T + 2) % 3) * 2 * LBD + ((int64_t)l * B + b) * D, c);
+  }
+  if (l >= 1) {
+    const float mean = tot[2] / D;
+    const float rstd = rsqrtf(fmaxf(tot[3] / D - mean * mean, 0.f) + eps);
+    ln_chunk_store(hf, mean, rstd, wf, bf,
+                   lnr + (int64_t)((T + 1) % 3) * 2 * LBD + LBD + ((int64_t)(l - 1) * B + b) * D, c);
+  }
+}
+
+// The LayerNorm ring's initial contents: every row the LayerNorm bias of its layer (the
+// normalised zero row). Grid: x over bf16 pairs, y over [slot][left | diag][layer][batch] rows.
+__global__ void blk_ln_init_kernel(bf16* __restrict__ lnr, const float* __restrict__ lb0,
+                                   const float* __restrict__ lb1, int L, int B, int D) {
   const int j = blockIdx.x * blockDim.x + threadIdx.x;
   if (j >= D / 2) return;
-  const int rb = blockIdx.y;
-  const int i = rb / B, b = rb - i * B;
-  const int l = l0 + 2 * i, t = (T - l) / 2;
-  auto ld2 = [&](const bf16* p) {
-    return __bfloat1622float2(reinterpret_cast<const __nv_bfloat162*>(p)[j]);
-  };
-  const int64_t r3 = (int64_t)rb * 3;
-  const float2 o0 = ld2(o + r3 * D), o1 = ld2(o + (r3 + 1) * D), o2 = ld2(o + (r3 + 2) * D);
-  const float2 top = ld2(top_row(grids, x, l, t, b, S, B, D));
-  const float2 lp = ld2(lat_prior + (int64_t)rb * D), fp = ld2(tok + (r3 + 2) * D);
-  // the outputs as stored (bf16), as the aux term sees them
-  const __nv_bfloat162 hx = __floats2bfloat162_rn(o0.x + top.x, o0.y + top.y);
-  const __nv_bfloat162 hl = __floats2bfloat162_rn(o1.x + lp.x, o1.y + lp.y);
-  const __nv_bfloat162 hf = __floats2bfloat162_rn(o2.x + fp.x, o2.y + fp.y);
-  const float2 hlf = __bfloat1622float2(hl), hff = __bfloat1622float2(hf);
-  const float ax = (lp.x - hlf.x) * (lp.x - hlf.x) + (fp.x - hff.x) * (fp.x - hff.x);
-  const float ay = (lp.y - hlf.y) * (lp.y - hlf.y) + (fp.y - hff.y) * (fp.y - hff.y);
-  const int64_t off = (cell_row(l, t, S) * B + b) * D;
-  reinterpret_cast<__nv_bfloat162*>(grids + off)[j] = hx;
-  reinterpret_cast<__nv_bfloat162*>(grids + port_stride + off)[j] = hl;
-  reinterpret_cast<__nv_bfloat162*>(grids + 2 * port_stride + off)[j] = hf;
-  reinterpret_cast<__nv_bfloat162*>(grids + 3 * port_stride + off)[j] = __floats2bfloat162_rn(ax, ay);
+  const int rowi = blockIdx.y;  // ((slot * 2 + which) * L + l) * B + b
+  const int l = (rowi / B) % L, which = (rowi / (B * L)) % 2;
+  const float2 bv = reinterpret_cast<const float2*>((which ? lb1 : lb0) + (int64_t)l * D)[j];
+  reinterpret_cast<__nv_bfloat162*>(lnr + (int64_t)rowi * D)[j] = __floats2bfloat162_rn(bv.x, bv.y);
 }
 
 constexpr size_t kBlkBlasWs = 32u << 20;
 
 struct BlockWs {
   unsigned* sync;  // persistent forward: [0] barrier counter, [1] error word, [2] abort flag
+  bf16* lnr;       // LayerNorm ring of the tick path: [3][left | diag][L][B][D]
   bf16 *ln, *lat, *tok, *z, *qkv, *att, *o;
   bf16* glpf;  // [L, D, D] folded lateral-gate weights G_L P_fb
   void* blas;
@@ -298,6 +419,7 @@ size_t block_ws_layout(int64_t nmax, int64_t L, int64_t B, int64_t D, BlockWs* w
     return o;
   };
   const size_t o_sync = take(256);  // first: flb_block_grid_status reads it at offset 0
+  const size_t o_lnr = take((size_t)3 * 2 * L * B * D * sizeof(bf16));
   const size_t o_ln = take(2 * rowb), o_lat = take(rowb), o_tok = take(3 * rowb), o_z = take(rowb),
                o_qkv = take(9 * rowb), o_att = take(3 * rowb), o_o = take(3 * rowb),
                o_blas = take(kBlkBlasWs), o_blas_side = take(kBlkBlasWs),
@@ -305,6 +427,7 @@ size_t block_ws_layout(int64_t nmax, int64_t L, int64_t B, int64_t D, BlockWs* w
   if (w && base) {
     uint8_t* p = reinterpret_cast<uint8_t*>(base);
     w->sync = (unsigned*)(p + o_sync);
+    w->lnr = (bf16*)(p + o_lnr);
     w->ln = (bf16*)(p + o_ln);
     w->lat = (bf16*)(p + o_lat);
     w->tok = (bf16*)(p + o_tok);
@@ -490,13 +613,25 @@ struct Side {
 int tick_forward(cublasHandle_t hb, const Side& side, const flb_block_weights* W, const bf16* xb,
                  const bf16* g, int64_t port_stride, const TickBufs& b, int T, int l0, int n,
                  int L, int S, int B, int D, int H, float eps, cudaStream_t s,
-                 const bf16* w_glpf = nullptr) {
+                 const bf16* w_glpf = nullptr, const bf16* lnr = nullptr) {
   const long long DD = (long long)D * D, BD = (long long)B * D;
   int st;
-  cudaError_t e = launch_pdl(blk_ln_kernel, dim3((2 * n * B + 7) / 8), dim3(256), 0, s,
-                             g + port_stride, g + 2 * port_stride, W->ln_lat_w, W->ln_lat_b,
-                             W->ln_fdbk_w, W->ln_fdbk_b, b.ln, T, l0, n, L, S, B, D, eps);
-  if (e != cudaSuccess) return check_cuda(e, "block_grid LayerNorm launch");
+  cudaError_t e = cudaSuccess;
+  // LayerNorm outputs of the tick's cells: from the ring the previous ticks' output kernels
+  // filled (lnr: [T % 3][left | diag][layer][B][D], cells two layers apart), or computed here
+  const bf16 *ln_left = b.ln, *ln_diag = b.ln + n * BD;
+  long long ln_stride = BD;
+  if (lnr) {
+    const long long LBD = (long long)L * BD;
+    ln_left = lnr + (long long)(T % 3) * 2 * LBD + (long long)l0 * BD;
+    ln_diag = ln_left + LBD;
+    ln_stride = 2 * BD;
+  } else {
+    e = launch_pdl(blk_ln_kernel, dim3((2 * n * B + 7) / 8), dim3(256), 0, s, g + port_stride,
+                   g + 2 * port_stride, W->ln_lat_w, W->ln_lat_b, W->ln_fdbk_w, W->ln_fdbk_b, b.ln,
+                   T, l0, n, L, S, B, D, eps);
+    if (e != cudaSuccess) return check_cuda(e, "block_grid LayerNorm launch");
+  }
   e = cudaEventRecord(side.ss->fwd_fork, s);
   if (e == cudaSuccess) e = cudaStreamWaitEvent(side.ss->s, side.ss->fwd_fork, 0);
   if (e != cudaSuccess) return check_cuda(e, "block_grid tick fork");
@@ -507,23 +642,23 @@ int tick_forward(cublasHandle_t hb, const Side& side, const flb_block_weights* W
   const bf16* Wqkv = reinterpret_cast<const bf16*>(W->w_qkv) + (int64_t)l0 * 3 * DD;
   // priors: lat_prior -> b.lat (side stream: first needed by the lateral gate kernel);
   // fdbk_prior -> token slot 2 (row pitch 3D)
-  if ((st = gemm_rm(side.h, false, true, B, D, D, b.ln, D, BD, Wpl, D, 2 * DD, b.lat, D, BD, n, 0.f,
-                    CUDA_R_16BF)) != FLB_OK)
+  if ((st = gemm_rm(side.h, false, true, B, D, D, ln_left, D, ln_stride, Wpl, D, 2 * DD, b.lat, D,
+                    BD, n, 0.f, CUDA_R_16BF)) != FLB_OK)
     return st;
   e = cudaEventRecord(side.ss->fwd_join, side.ss->s);
   if (e != cudaSuccess) return check_cuda(e, "block_grid tick join");
   if (w_glpf) {
     // fdbk_prior on the side stream (first needed by the q|k|v GEMM); z_l from the folded weights
-    if ((st = gemm_rm(side.h, false, true, B, D, D, b.ln + n * BD, D, BD, Wpf, D, 2 * DD,
+    if ((st = gemm_rm(side.h, false, true, B, D, D, ln_diag, D, ln_stride, Wpf, D, 2 * DD,
                       b.tok + 2 * D, 3 * D, 3 * BD, n, 0.f, CUDA_R_16BF)) != FLB_OK)
       return st;
     e = cudaEventRecord(side.ss->fwd_join2, side.ss->s);
     if (e != cudaSuccess) return check_cuda(e, "block_grid tick join");
-    if ((st = gemm_rm(hb, false, true, B, D, D, b.ln + n * BD, D, BD, w_glpf + (int64_t)l0 * DD, D,
+    if ((st = gemm_rm(hb, false, true, B, D, D, ln_diag, D, ln_stride, w_glpf + (int64_t)l0 * DD, D,
                       2 * DD, b.zl, D, BD, n, 0.f, CUDA_R_16BF)) != FLB_OK)
       return st;
   } else {
-    if ((st = gemm_rm(hb, false, true, B, D, D, b.ln + n * BD, D, BD, Wpf, D, 2 * DD, b.tok + 2 * D,
+    if ((st = gemm_rm(hb, false, true, B, D, D, ln_diag, D, ln_stride, Wpf, D, 2 * DD, b.tok + 2 * D,
                       3 * D, 3 * BD, n, 0.f, CUDA_R_16BF)) != FLB_OK)
       return st;
     // lateral gate
@@ -590,23 +725,29 @@ int block_grid_fwd_ex(const flb_block_weights* W, const void* x, void* grids, in
   if (persist)
     return launch_persist(W, w.glpf, xb, g, port_stride, w, Li, Si, Di, Hi, eps, s, drop_cta,
                           drop_bar, spin_limit ? spin_limit : kPsSpinLimit);
-  int launches = 0;
+  // the LayerNorm ring starts as the normalised zero rows (the LayerNorm biases)
+  cudaError_t ie = launch_pdl(blk_ln_init_kernel, dim3((unsigned)((D / 2 + 127) / 128), (unsigned)(6 * L * B)),
+                              dim3(128), 0, s, w.lnr, W->ln_lat_b, W->ln_fdbk_b, Li, Bi, Di);
+  if (ie != cudaSuccess) return check_cuda(ie, "block_grid LayerNorm init launch");
+  int launches = 1;
   for (int T = 0; T < ticks; ++T) {
     const Tick tk = tick_of(T, Li, Si);
     const int n = tk.n, l0 = tk.l0;
     if (n == 0) continue;
     if ((st = tick_forward(hb, side, W, xb, g, port_stride, tb, T, l0, n, Li, Si, Bi, Di, Hi, eps,
-                           s, w.glpf)) != FLB_OK)
+                           s, w.glpf, w.lnr)) != FLB_OK)
       return st;
     const bf16* Wo = reinterpret_cast<const bf16*>(W->w_o) + (int64_t)l0 * DD;
     if ((st = gemm_rm(hb, false, true, 3 * Bi, Di, Di, w.att, Di, 3 * BD, Wo, Di, 2 * DD, w.o, Di,
                       3 * BD, n, 0.f, CUDA_R_16BF)) != FLB_OK)
       return st;
-    const dim3 ew_grid((unsigned)((D / 2 + 127) / 128), (unsigned)(n * Bi));
-    cudaError_t e = launch_pdl(blk_out_kernel, ew_grid, dim3(128), 0, s, w.o, w.lat, w.tok, xb,
-                               g, port_stride, T, l0, Si, Bi, Di);
+    // residuals, aux and the next ticks' LayerNorms: a warp per (cell, batch row)
+    const int out_threads = std::max(32, (Di / 8 + 31) / 32 * 32);
+    cudaError_t e = launch_pdl(blk_out_ln_kernel, dim3((unsigned)(n * Bi)), dim3(out_threads), 0,
+                               s, w.o, w.lat, w.tok, xb, g, port_stride, w.lnr, W->ln_lat_w,
+                               W->ln_lat_b, W->ln_fdbk_w, W->ln_fdbk_b, eps, T, l0, n, Li, Si, Bi, Di);
     if (e != cudaSuccess) return check_cuda(e, "block_grid output launch");
-    launches += 6;  // own kernels (the GEMMs are cuBLAS's)
+    launches += 5;  // own kernels (the GEMMs are cuBLAS's)
   }
   count_launches(launches);
   return check_cuda(cudaGetLastError(), "flb block grid launch");
