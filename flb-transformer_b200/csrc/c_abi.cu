@@ -74,13 +74,14 @@ int block_grid_fwd(const flb_block_weights* W, const void* x, void* grids, int64
 int block_grid_fwd_ex(const flb_block_weights* W, const void* x, void* grids, int64_t L,
                       int64_t S, int64_t B, int64_t D, int64_t H, float eps, void* ws,
                       size_t ws_bytes, cudaStream_t s, int path, int drop_cta, int drop_bar,
-                      uint32_t spin_limit);
+                      uint32_t spin_limit, void* saved);
+size_t block_grid_saved_bytes(int64_t L, int64_t S, int64_t B, int64_t D);
 int block_grid_status(const void* ws, cudaStream_t s);
 size_t block_grid_bwd_workspace_bytes(int64_t L, int64_t S, int64_t B, int64_t D);
 int block_grid_bwd(const flb_block_weights* W, const void* x, const void* grids,
                    const void* const* dgrids, float* dx, const flb_block_grads* G, int64_t L,
                    int64_t S, int64_t B, int64_t D, int64_t H, float eps, void* ws,
-                   size_t ws_bytes, cudaStream_t s);
+                   size_t ws_bytes, cudaStream_t s, const void* saved);
 size_t grid_workspace_bytes(int64_t R, int64_t C, int64_t B, int64_t H, int64_t G, int has_U);
 int grid_fwd(const void* x, int x_layout, const void* W_l, const void* W_t, const void* U,
              const float* bias, const void* top, void* h_out, int64_t R, int64_t C, int64_t B,
@@ -287,7 +288,7 @@ int flb_block_grid_fwd_ex(const flb_block_weights* weights, const void* x, void*
   if (!workspace || workspace_bytes < need)
     return fail(FLB_ERR_WORKSPACE, "block_grid_fwd_ex: workspace smaller than flb_block_grid_workspace_bytes()");
   return block_grid_fwd_ex(weights, x, grids, L, S, batch, D, heads, ln_eps, workspace,
-                           workspace_bytes, as_stream(stream), path, -1, -1, 0);
+                           workspace_bytes, as_stream(stream), path, -1, -1, 0, nullptr);
 }
 
 int flb_block_grid_status(const void* workspace, void* stream) {
@@ -309,7 +310,7 @@ int flb_block_grid_fwd_drop_barrier_test(const flb_block_weights* weights, const
     return fail(FLB_ERR_SHAPE, "block_grid drop test: drop_cta must name a CTA of the launch, drop_barrier >= 0, spin_limit >= 1");
   st = block_grid_fwd_ex(weights, x, grids, L, S, batch, D, heads, ln_eps, workspace,
                          workspace_bytes, as_stream(stream), FLB_BLOCK_PATH_PERSISTENT,
-                         (int)drop_cta, (int)drop_barrier, spin_limit);
+                         (int)drop_cta, (int)drop_barrier, spin_limit, nullptr);
   if (st != FLB_OK) return st;
   return block_grid_status(workspace, as_stream(stream));
 }
@@ -340,7 +341,56 @@ int flb_block_grid_bwd(const flb_block_weights* weights, const void* x, const vo
     return fail(FLB_ERR_WORKSPACE, "block_grid_bwd: workspace smaller than flb_block_grid_bwd_workspace_bytes()");
   const void* dg[4] = {dgrid0, dgrid1, dgrid2, dgrid3};
   return block_grid_bwd(weights, x, grids, dg, dx, grads, L, S, batch, D, heads, ln_eps,
-                        workspace, workspace_bytes, as_stream(stream));
+                        workspace, workspace_bytes, as_stream(stream), nullptr);
+}
+
+size_t flb_block_grid_saved_bytes(int64_t L, int64_t S, int64_t batch, int64_t D) {
+  if (L < 1 || S < 1 || batch < 1 || D < 1) return 0;
+  return block_grid_saved_bytes(L, S, batch, D);
+}
+
+int flb_block_grid_fwd_save(const flb_block_weights* weights, const void* x, void* grids, int64_t L,
+                            int64_t S, int64_t batch, int64_t D, int64_t heads, float ln_eps,
+                            void* workspace, size_t workspace_bytes, void* saved,
+                            size_t saved_bytes, void* stream) {
+  int st = check_block_args(weights, x, grids, L, S, batch, D, heads);
+  if (st != FLB_OK) return st;
+  const size_t need = block_grid_workspace_bytes(L, S, batch, D);
+  if (!workspace || workspace_bytes < need)
+    return fail(FLB_ERR_WORKSPACE, "block_grid_fwd_save: workspace smaller than flb_block_grid_workspace_bytes()");
+  if (!saved || saved_bytes < block_grid_saved_bytes(L, S, batch, D))
+    return fail(FLB_ERR_WORKSPACE, "block_grid_fwd_save: saved buffer smaller than flb_block_grid_saved_bytes()");
+  if ((uintptr_t)saved & 15u) return fail(FLB_ERR_ALIGN, "block_grid_fwd_save: saved must be 16-byte aligned");
+  return block_grid_fwd_ex(weights, x, grids, L, S, batch, D, heads, ln_eps, workspace,
+                           workspace_bytes, as_stream(stream), FLB_BLOCK_PATH_TICKS, -1, -1, 0, saved);
+}
+
+int flb_block_grid_bwd_saved(const flb_block_weights* weights, const void* x, const void* grids,
+                             const void* dgrid0, const void* dgrid1, const void* dgrid2,
+                             const void* dgrid3, float* dx, const flb_block_grads* grads,
+                             int64_t L, int64_t S, int64_t batch, int64_t D, int64_t heads,
+                             float ln_eps, void* workspace, size_t workspace_bytes,
+                             const void* saved, size_t saved_bytes, void* stream) {
+  if (!saved || saved_bytes < block_grid_saved_bytes(L, S, batch, D))
+    return fail(FLB_ERR_WORKSPACE, "block_grid_bwd_saved: saved buffer smaller than flb_block_grid_saved_bytes()");
+  if ((uintptr_t)saved & 15u) return fail(FLB_ERR_ALIGN, "block_grid_bwd_saved: saved must be 16-byte aligned");
+  int st = check_block_args(weights, x, grids, L, S, batch, D, heads);
+  if (st != FLB_OK) return st;
+  if (!dx || !grads) return fail(FLB_ERR_SHAPE, "block_grid_bwd_saved: null dx or grads");
+  const flb_block_grads& g = *grads;
+  if (!g.ln_lat_w || !g.ln_lat_b || !g.ln_fdbk_w || !g.ln_fdbk_b || !g.w_prior_lat ||
+      !g.w_prior_fdbk || !g.w_gate_l || !g.b_gate_l || !g.w_gate_x || !g.b_gate_x || !g.w_qkv ||
+      !g.w_o || !g.v_a)
+    return fail(FLB_ERR_SHAPE, "block_grid_bwd_saved: null gradient pointer");
+  if (((uintptr_t)dgrid0 | (uintptr_t)dgrid1 | (uintptr_t)dgrid2 | (uintptr_t)dgrid3 |
+       (uintptr_t)dx) & 15u)
+    return fail(FLB_ERR_ALIGN, "block_grid_bwd_saved: gradient grids and dx must be 16-byte aligned");
+  const size_t need = block_grid_bwd_workspace_bytes(L, S, batch, D);
+  if (!workspace || workspace_bytes < need)
+    return fail(FLB_ERR_WORKSPACE, "block_grid_bwd_saved: workspace smaller than flb_block_grid_bwd_workspace_bytes()");
+  const void* dg[4] = {dgrid0, dgrid1, dgrid2, dgrid3};
+  return block_grid_bwd(weights, x, grids, dg, dx, grads, L, S, batch, D, heads, ln_eps,
+                        workspace, workspace_bytes, as_stream(stream), saved);
 }
 
 size_t flb_grid_workspace_bytes(int64_t R, int64_t C, int64_t B, int64_t H, int64_t G, int has_U) {

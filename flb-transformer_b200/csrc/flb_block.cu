@@ -398,12 +398,59 @@ __global__ void blk_ln_init_kernel(bf16* __restrict__ lnr, const float* __restri
   reinterpret_cast<__nv_bfloat162*>(lnr + (int64_t)rowi * D)[j] = __floats2bfloat162_rn(bv.x, bv.y);
 }
 
+// Per-cell records of a training forward's tick intermediates, which the backward restores in
+// place of recomputing its ticks' forward stages: per grid cell (l*S + t) the units
+// [ln_left | ln_diag | lat_prior | tokens x' lat' fdbk_prior | z_l | z_x | q|k|v (9) | att (3)],
+// each B x D bf16 (20 units). dir 0: tick buffers -> records (after a forward tick); 1: records
+// -> tick buffers (before a backward tick). Grid: x over 16-byte chunks of a record, y over the
+// tick's cells.
+constexpr int kCellUnits = 20;
+struct CellBufs {
+  bf16 *ln_left, *ln_diag;  // cell i's LayerNorm rows at + i * ln_cell
+  int64_t ln_cell;
+  bf16 *lat, *tok, *zl, *zx, *qkv, *att;
+};
+
+__global__ void blk_cells_copy_kernel(bf16* __restrict__ rec, CellBufs cb, int dir, int T, int l0,
+                                      int S, int B, int D) {
+  pdl_wait();
+  const int i = blockIdx.y;
+  const int l = l0 + 2 * i, t = (T - l) / 2;
+  const int64_t BD = (int64_t)B * D;
+  const int64_t e0 = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) * 8;
+  if (e0 >= kCellUnits * BD) return;
+  const int unit = (int)(e0 / BD);  // B * D is a multiple of 8: a chunk lies in one unit
+  const int64_t in = e0 - unit * BD;
+  bf16* buf;
+  if (unit == 0) buf = cb.ln_left + i * cb.ln_cell + in;
+  else if (unit == 1) buf = cb.ln_diag + i * cb.ln_cell + in;
+  else if (unit == 2) buf = cb.lat + i * BD + in;
+  else if (unit < 6) buf = cb.tok + (3 * i + (unit - 3)) * BD + in;
+  else if (unit == 6) buf = cb.zl + i * BD + in;
+  else if (unit == 7) buf = cb.zx + i * BD + in;
+  else if (unit < 17) buf = cb.qkv + (9 * i + (unit - 8)) * BD + in;
+  else buf = cb.att + (3 * i + (unit - 17)) * BD + in;
+  uint4* r = reinterpret_cast<uint4*>(rec + cell_row(l, t, S) * kCellUnits * BD + e0);
+  uint4* b = reinterpret_cast<uint4*>(buf);
+  if (dir == 0) *r = *b;
+  else *b = *r;
+}
+
+int launch_cells_copy(bf16* rec, const CellBufs& cb, int dir, int T, int l0, int n, int S, int B,
+                      int D, cudaStream_t s) {
+  const int64_t chunks = (int64_t)kCellUnits * B * D / 8;
+  const dim3 grid((unsigned)((chunks + 255) / 256), (unsigned)n);
+  return check_cuda(launch_pdl(blk_cells_copy_kernel, grid, dim3(256), 0, s, rec, cb, dir, T, l0,
+                               S, B, D),
+                    "block_grid intermediates copy");
+}
+
 constexpr size_t kBlkBlasWs = 32u << 20;
 
 struct BlockWs {
   unsigned* sync;  // persistent forward: [0] barrier counter, [1] error word, [2] abort flag
   bf16* lnr;       // LayerNorm ring of the tick path: [3][left | diag][L][B][D]
-  bf16 *ln, *lat, *tok, *z, *qkv, *att, *o;
+  bf16 *ln, *lat, *tok, *z, *zx, *qkv, *att, *o;
   bf16* glpf;  // [L, D, D] folded lateral-gate weights G_L P_fb
   void* blas;
   void* blas_side;
@@ -420,7 +467,7 @@ size_t block_ws_layout(int64_t nmax, int64_t L, int64_t B, int64_t D, BlockWs* w
   };
   const size_t o_sync = take(256);  // first: flb_block_grid_status reads it at offset 0
   const size_t o_lnr = take((size_t)3 * 2 * L * B * D * sizeof(bf16));
-  const size_t o_ln = take(2 * rowb), o_lat = take(rowb), o_tok = take(3 * rowb), o_z = take(rowb),
+  const size_t o_ln = take(2 * rowb), o_lat = take(rowb), o_tok = take(3 * rowb), o_z = take(rowb), o_zx = take(rowb),
                o_qkv = take(9 * rowb), o_att = take(3 * rowb), o_o = take(3 * rowb),
                o_blas = take(kBlkBlasWs), o_blas_side = take(kBlkBlasWs),
                o_glpf = take((size_t)L * D * D * sizeof(bf16));
@@ -432,6 +479,7 @@ size_t block_ws_layout(int64_t nmax, int64_t L, int64_t B, int64_t D, BlockWs* w
     w->lat = (bf16*)(p + o_lat);
     w->tok = (bf16*)(p + o_tok);
     w->z = (bf16*)(p + o_z);
+    w->zx = (bf16*)(p + o_zx);
     w->qkv = (bf16*)(p + o_qkv);
     w->att = (bf16*)(p + o_att);
     w->o = (bf16*)(p + o_o);
@@ -697,12 +745,14 @@ int tick_forward(cublasHandle_t hb, const Side& side, const flb_block_weights* W
 int block_grid_fwd_ex(const flb_block_weights* W, const void* x, void* grids, int64_t L,
                       int64_t S, int64_t B, int64_t D, int64_t H, float eps, void* ws,
                       size_t ws_bytes, cudaStream_t s, int path, int drop_cta, int drop_bar,
-                      uint32_t spin_limit) {
+                      uint32_t spin_limit, void* saved) {
   // the persistent forward only on request: at the end-to-end shape (12 layers x 1024
   // positions, d_model 768, batch 16) it measured 111 ms per forward against 80 ms tick by tick
   const bool persist = persist_fits(L, S, B, D, H) && path == FLB_BLOCK_PATH_PERSISTENT;
   if (path == FLB_BLOCK_PATH_PERSISTENT && !persist)
     return fail(FLB_ERR_UNSUPPORTED, "block_grid persistent forward: needs batch 16 and D a multiple of 128 up to 1024");
+  if (persist && saved)
+    return fail(FLB_ERR_UNSUPPORTED, "block_grid: the persistent forward keeps no intermediates");
   BlockWs w;
   block_ws_layout(max_cells_per_tick(L, S), L, B, D, &w, ws);
   cublasHandle_t hb;
@@ -717,7 +767,7 @@ int block_grid_fwd_ex(const flb_block_weights* W, const void* x, void* grids, in
   const long long DD = D * D, BD = B * D;
   const int Li = (int)L, Si = (int)S, Bi = (int)B, Di = (int)D, Hi = (int)H;
   const int ticks = (int)(L + 2 * S - 2);
-  const TickBufs tb{w.ln, w.lat, w.tok, w.z, w.z, w.qkv, w.att};
+  const TickBufs tb{w.ln, w.lat, w.tok, w.z, w.zx, w.qkv, w.att};
   // inference: fold the lateral gate onto the feedback prior once per call, G_L P_fb per layer
   if ((st = gemm_rm(hb, false, false, Di, Di, Di, W->w_gate_l, Di, DD, W->w_prior_fdbk, Di, DD,
                     w.glpf, Di, DD, Li, 0.f, CUDA_R_16BF)) != FLB_OK)
@@ -748,6 +798,14 @@ int block_grid_fwd_ex(const flb_block_weights* W, const void* x, void* grids, in
                                W->ln_lat_b, W->ln_fdbk_w, W->ln_fdbk_b, eps, T, l0, n, Li, Si, Bi, Di);
     if (e != cudaSuccess) return check_cuda(e, "block_grid output launch");
     launches += 5;  // own kernels (the GEMMs are cuBLAS's)
+    if (saved) {  // the tick's intermediates, for the backward
+      const long long LBD = (long long)L * BD;
+      bf16* ln_left = w.lnr + (long long)(T % 3) * 2 * LBD + (long long)l0 * BD;
+      const CellBufs cb{ln_left, ln_left + LBD, 2 * BD, w.lat, w.tok, w.z, w.zx, w.qkv, w.att};
+      if ((st = launch_cells_copy(reinterpret_cast<bf16*>(saved), cb, 0, T, l0, n, Si, Bi, Di, s)) != FLB_OK)
+        return st;
+      ++launches;
+    }
   }
   count_launches(launches);
   return check_cuda(cudaGetLastError(), "flb block grid launch");
@@ -757,7 +815,7 @@ int block_grid_fwd(const flb_block_weights* W, const void* x, void* grids, int64
                    int64_t B, int64_t D, int64_t H, float eps, void* ws, size_t ws_bytes,
                    cudaStream_t s) {
   return block_grid_fwd_ex(W, x, grids, L, S, B, D, H, eps, ws, ws_bytes, s, FLB_BLOCK_PATH_AUTO,
-                           -1, -1, 0);
+                           -1, -1, 0, nullptr);
 }
 
 int block_grid_status(const void* ws, cudaStream_t s) {
@@ -1207,6 +1265,10 @@ size_t block_bwd_ws_layout(int64_t L, int64_t S, int64_t B, int64_t D, BlockBwdW
 
 }  // namespace
 
+size_t block_grid_saved_bytes(int64_t L, int64_t S, int64_t B, int64_t D) {
+  return (size_t)L * S * kCellUnits * B * D * sizeof(bf16);
+}
+
 size_t block_grid_bwd_workspace_bytes(int64_t L, int64_t S, int64_t B, int64_t D) {
   return block_bwd_ws_layout(L, S, B, D, nullptr, nullptr);
 }
@@ -1214,7 +1276,7 @@ size_t block_grid_bwd_workspace_bytes(int64_t L, int64_t S, int64_t B, int64_t D
 int block_grid_bwd(const flb_block_weights* W, const void* x, const void* grids,
                    const void* const* dgrids, float* dx, const flb_block_grads* G, int64_t L,
                    int64_t S, int64_t B, int64_t D, int64_t H, float eps, void* ws,
-                   size_t ws_bytes, cudaStream_t s) {
+                   size_t ws_bytes, cudaStream_t s, const void* saved) {
   BlockBwdWs w;
   block_bwd_ws_layout(L, S, B, D, &w, ws);
   SideStream* side;
@@ -1255,9 +1317,16 @@ int block_grid_bwd(const flb_block_weights* W, const void* x, const void* grids,
     const Tick tk = tick_of(T, Li, Si);
     const int n = tk.n, l0 = tk.l0;
     if (n == 0) continue;
-    if ((st = tick_forward(hb, Side{side, hs}, W, xb, g, port_stride, w.f, T, l0, n, Li, Si, Bi,
-                           Di, Hi, eps, s)) != FLB_OK)
+    if (saved) {  // the forward's intermediates of the tick, restored instead of recomputed
+      const CellBufs cb{w.f.ln, w.f.ln + n * BD, BD, w.f.lat, w.f.tok, w.f.zl, w.f.zx, w.f.qkv,
+                        w.f.att};
+      if ((st = launch_cells_copy(const_cast<bf16*>(reinterpret_cast<const bf16*>(saved)), cb, 1, T,
+                                  l0, n, Si, Bi, Di, s)) != FLB_OK)
+        return st;
+    } else if ((st = tick_forward(hb, Side{side, hs}, W, xb, g, port_stride, w.f, T, l0, n, Li, Si,
+                                  Bi, Di, Hi, eps, s)) != FLB_OK) {
       return st;
+    }
     const dim3 ew_grid((unsigned)((D / 2 + 127) / 128), (unsigned)(n * Bi));
     // gate backward blocks: 32 feature pairs by up to 16 batch rows, one grid row per cell
     const dim3 pair_grid((unsigned)((D / 2 + 31) / 32), (unsigned)n);

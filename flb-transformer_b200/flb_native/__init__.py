@@ -57,6 +57,12 @@ PROTOTYPES = {
     "flb_block_grid_fwd_drop_barrier_test": (_i32, [_vp, _vp, _vp, _i64, _i64, _i64, _i64, _i64,
                                                     ctypes.c_float, _vp, _sz, _i64, _i64,
                                                     ctypes.c_uint32, _vp]),
+    "flb_block_grid_saved_bytes": (_sz, [_i64, _i64, _i64, _i64]),
+    "flb_block_grid_fwd_save": (_i32, [_vp, _vp, _vp, _i64, _i64, _i64, _i64, _i64,
+                                       ctypes.c_float, _vp, _sz, _vp, _sz, _vp]),
+    "flb_block_grid_bwd_saved": (_i32, [_vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _i64, _i64,
+                                        _i64, _i64, _i64, ctypes.c_float, _vp, _sz, _vp, _sz,
+                                        _vp]),
     "flb_block_grid_bwd_workspace_bytes": (_sz, [_i64, _i64, _i64, _i64]),
     "flb_block_grid_bwd": (_i32, [_vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _i64, _i64, _i64,
                                   _i64, _i64, ctypes.c_float, _vp, _sz, _vp]),

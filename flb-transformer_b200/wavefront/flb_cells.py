@@ -10,7 +10,10 @@ index_select, vmapped cell and scatters. With gradients required it runs behind
 FLBGridFunction, whose backward is flb_block_grid_bwd (ticks in reverse, per-tick recompute,
 per-layer fp32 weight-gradient stacks). bf16 compute only (the reference model runs under bf16
 autocast). Setting engine.native_flb_path = 2 (FLB_BLOCK_PATH_PERSISTENT) runs the inference
-forward as one persistent tcgen05 kernel instead (batch 16, d_model a multiple of 128).
+forward as one persistent tcgen05 kernel instead (batch 16, d_model a multiple of 128). A
+training forward keeps every cell's intermediates (flb_block_grid_fwd_save) so that the backward
+restores them instead of recomputing its ticks' forward stages; engine.native_flb_save = False
+trades that memory (L * S * 20 * batch * d_model bf16) for the recompute.
 """
 from __future__ import annotations
 
@@ -100,19 +103,46 @@ class BlockWeightStacks:
         self.eps = float(layers[0].norm_lat.eps)
 
 
-def native_flb_forward(engine, static_x: torch.Tensor, grids: torch.Tensor, weights=None) -> None:
+def saved_buffer(engine, device) -> torch.Tensor | None:
+    """The engine's buffer for a training forward's per-cell intermediates
+    (flb_block_grid_saved_bytes), or None when engine.native_flb_save is False (the backward
+    then recomputes each tick's forward stages). One buffer per engine, like its static grids:
+    a forward overwrites what the previous one kept."""
+    if not getattr(engine, "native_flb_save", True):
+        return None
+    cfg = engine.config
+    L, S = cfg.grid_shape
+    nbytes = nat.lib.flb_block_grid_saved_bytes(L, S, cfg.batch_size, cfg.dim)
+    ws = engine.graph_workspace
+    buf = ws.get("flb_saved")
+    if buf is None or buf.numel() != nbytes or buf.device != torch.device(device):
+        buf = torch.empty(nbytes, dtype=torch.uint8, device=device)
+        ws["flb_saved"] = buf
+    return buf
+
+
+def native_flb_forward(engine, static_x: torch.Tensor, grids: torch.Tensor, weights=None,
+                       saved: torch.Tensor | None = None) -> None:
     """Evaluate every cell of the engine's grid into `grids` ([ports, cells + L, batch, dim],
-    bf16) from static_x ([batch, seq, dim], bf16), with the layers' current weights."""
+    bf16) from static_x ([batch, seq, dim], bf16), with the layers' current weights. With
+    `saved` (saved_buffer) the cells' intermediates are kept for native_flb_backward."""
     cfg = engine.config
     L, S = cfg.grid_shape
     B, D = cfg.batch_size, cfg.dim
     w = weights or BlockWeightStacks(list(engine.layers))
     ws_bytes = nat.lib.flb_block_grid_workspace_bytes(L, S, B, D)
     ws = nat.workspace(ws_bytes, grids.device)
+    wptr = ctypes.cast(ctypes.pointer(w.struct), ctypes.c_void_p)
+    if saved is not None:
+        nat.check(nat.lib.flb_block_grid_fwd_save(
+            wptr, static_x.data_ptr(), grids.data_ptr(), L, S, B, D, w.heads, w.eps, nat.ptr(ws),
+            ws_bytes, saved.data_ptr(), saved.numel(), nat.stream_of(grids)),
+            "flb_block_grid_fwd_save")
+        return
     # engine.native_flb_path: FLB_BLOCK_PATH_* (0 = the default, 2 = the persistent kernel)
     path = int(getattr(engine, "native_flb_path", 0))
     nat.check(nat.lib.flb_block_grid_fwd_ex(
-        ctypes.cast(ctypes.pointer(w.struct), ctypes.c_void_p), static_x.data_ptr(), grids.data_ptr(), L, S, B, D, w.heads,
+        wptr, static_x.data_ptr(), grids.data_ptr(), L, S, B, D, w.heads,
         w.eps, nat.ptr(ws), ws_bytes, path, nat.stream_of(grids)), "flb_block_grid_fwd_ex")
 
 
@@ -147,21 +177,24 @@ class FLBGridFunction(torch.autograd.Function):
         ws = engine.graph_workspace
         ws["static_x"].copy_(x)
         w = BlockWeightStacks(list(engine.layers))
-        native_flb_forward(engine, ws["static_x"], ws["static_stacked_grids"], weights=w)
-        ctx.engine, ctx.weights = engine, w
+        saved = saved_buffer(engine, x.device)
+        native_flb_forward(engine, ws["static_x"], ws["static_stacked_grids"], weights=w,
+                           saved=saved)
+        ctx.engine, ctx.weights, ctx.saved = engine, w, saved
         ctx.x_meta = (x.shape, x.dtype)
         n = math.prod(engine.config.grid_shape)
         return tuple(ws["static_stacked_grids"][p][:n] for p in range(engine.config.num_ports))
 
     @staticmethod
     def backward(ctx, *grad_grids):
-        gstacks, dx = native_flb_backward(ctx.engine, ctx.weights, grad_grids)
+        gstacks, dx = native_flb_backward(ctx.engine, ctx.weights, grad_grids, saved=ctx.saved)
         shape, dtype = ctx.x_meta
         return (None, dx.to(dtype).reshape(shape), *flb_param_grads(ctx.engine, gstacks))
 
 
-def native_flb_backward(engine, w, grad_grids):
-    """flb_block_grid_bwd over the engine's saved grids: (fp32 gradient stacks keyed like the
+def native_flb_backward(engine, w, grad_grids, saved: torch.Tensor | None = None):
+    """flb_block_grid_bwd over the engine's saved grids (flb_block_grid_bwd_saved with the
+    forward's intermediates when `saved` holds them): (fp32 gradient stacks keyed like the
     weight stacks, dx float32 [batch, seq, dim])."""
     cfg = engine.config
     L, S = cfg.grid_shape
@@ -174,11 +207,15 @@ def native_flb_backward(engine, w, grad_grids):
     dx = torch.empty((B, S, D), dtype=torch.float32, device=dev)
     ws_bytes = nat.lib.flb_block_grid_bwd_workspace_bytes(L, S, B, D)
     wsb = nat.workspace(ws_bytes, dev)
-    nat.check(nat.lib.flb_block_grid_bwd(
-        ctypes.cast(ctypes.pointer(w.struct), ctypes.c_void_p), ws["static_x"].data_ptr(),
-        ws["static_stacked_grids"].data_ptr(), *[nat.ptr(g) for g in dg], dx.data_ptr(),
-        ctypes.cast(ctypes.pointer(gstruct), ctypes.c_void_p), L, S, B, D, w.heads, w.eps,
-        nat.ptr(wsb), ws_bytes, nat.stream_of(dx)), "flb_block_grid_bwd")
+    args = (ctypes.cast(ctypes.pointer(w.struct), ctypes.c_void_p), ws["static_x"].data_ptr(),
+            ws["static_stacked_grids"].data_ptr(), *[nat.ptr(g) for g in dg], dx.data_ptr(),
+            ctypes.cast(ctypes.pointer(gstruct), ctypes.c_void_p), L, S, B, D, w.heads, w.eps,
+            nat.ptr(wsb), ws_bytes)
+    if saved is not None:
+        nat.check(nat.lib.flb_block_grid_bwd_saved(*args, saved.data_ptr(), saved.numel(),
+                                                   nat.stream_of(dx)), "flb_block_grid_bwd_saved")
+    else:
+        nat.check(nat.lib.flb_block_grid_bwd(*args, nat.stream_of(dx)), "flb_block_grid_bwd")
     return gstacks, dx
 
 

@@ -96,6 +96,7 @@ class GraphedWavefrontEngine:
             raise ValueError("GraphedWavefrontEngine: these layers take the persistent grid "
                              "kernels already; call the engine directly")
         self.engine = engine
+        self.with_backward = backward
         cfg = engine.config
         self.num_cells = math.prod(cfg.grid_shape)
         self.num_layers = cfg.grid_shape[0]
@@ -143,10 +144,12 @@ class GraphedWavefrontEngine:
         eng, cfg = self.engine, self.engine.config
         ws = eng.graph_workspace
         if self.native_flb:
-            from .flb_cells import native_flb_forward, BlockWeightStacks
+            from .flb_cells import native_flb_forward, BlockWeightStacks, saved_buffer
             self.flb_weights = BlockWeightStacks(list(eng.layers))
+            # a graph for training keeps the cells' intermediates for the backward graph
+            self.flb_saved = saved_buffer(eng, ws["static_x"].device) if self.with_backward else None
             native_flb_forward(eng, ws["static_x"], ws["static_stacked_grids"],
-                               weights=self.flb_weights)
+                               weights=self.flb_weights, saved=self.flb_saved)
             return
         refresh_stacked_params(eng.layers, eng.stacked_params)
         with torch.no_grad():
@@ -164,7 +167,8 @@ class GraphedWavefrontEngine:
             from .flb_cells import native_flb_backward
             n = self.num_cells
             self.flb_grads, self.flb_dx = native_flb_backward(
-                eng, self.flb_weights, [g[:n] for g in ws["static_grad_outputs"]])
+                eng, self.flb_weights, [g[:n] for g in ws["static_grad_outputs"]],
+                saved=self.flb_saved)
             return
         wavefront_backend.execute_backward(
             eng.active_cells_buffer.shape[0], cfg.num_ports, len(cfg.dependencies),

@@ -319,6 +319,18 @@ int flb_block_grid_fwd_drop_barrier_test(const flb_block_weights* weights, const
                                          size_t workspace_bytes, int64_t drop_cta,
                                          int64_t drop_barrier, uint32_t spin_limit, void* stream);
 
+/* Training forward that keeps the intermediates of every cell (no reference counterpart: the
+ * reference's autograd keeps the vmapped cells' tensors): flb_block_grid_fwd (tick by tick,
+ * cuBLAS projections) that also writes, per cell, its LayerNorm outputs, lat_prior, the three
+ * tokens, z_l, z_x, q|k|v and the attention output into `saved` (flb_block_grid_saved_bytes()
+ * bytes, 16-byte aligned: L * S * 20 * batch * D bf16), which flb_block_grid_bwd_saved reads
+ * back instead of recomputing each tick's forward stages. */
+size_t flb_block_grid_saved_bytes(int64_t L, int64_t S, int64_t batch, int64_t D);
+int flb_block_grid_fwd_save(const flb_block_weights* weights, const void* x, void* grids, int64_t L,
+                            int64_t S, int64_t batch, int64_t D, int64_t heads, float ln_eps,
+                            void* workspace, size_t workspace_bytes, void* saved,
+                            size_t saved_bytes, void* stream);
+
 /* Gradient accumulators of flb_block_grid_bwd: float32 stacks shaped like the matching fields
  * of flb_block_weights (w_qkv: [L, 3D, D], v_a: [L, H, D/H]). Gradients are ADDED into them. */
 typedef struct flb_block_grads {
@@ -351,6 +363,16 @@ int flb_block_grid_bwd(const flb_block_weights* weights, const void* x, const vo
                        const void* dgrid3, float* dx, const flb_block_grads* grads,
                        int64_t L, int64_t S, int64_t batch, int64_t D, int64_t heads,
                        float ln_eps, void* workspace, size_t workspace_bytes, void* stream);
+
+/* flb_block_grid_bwd with the intermediates flb_block_grid_fwd_save kept (same `grids`, weights
+ * and x as that forward): each tick restores its cells' intermediates with one copy instead of
+ * recomputing the forward stages. */
+int flb_block_grid_bwd_saved(const flb_block_weights* weights, const void* x, const void* grids,
+                             const void* dgrid0, const void* dgrid1, const void* dgrid2,
+                             const void* dgrid3, float* dx, const flb_block_grads* grads,
+                             int64_t L, int64_t S, int64_t batch, int64_t D, int64_t heads,
+                             float ln_eps, void* workspace, size_t workspace_bytes,
+                             const void* saved, size_t saved_bytes, void* stream);
 
 /* Failure-detection check of the grid kernels' bounded dependency waits (no reference
  * counterpart). Runs flb_grid_fwd with the flag of cell (drop_row, drop_col) never released and

@@ -230,6 +230,27 @@ def test_native_flb_training_matches_generic_path(cuda):
 
 
 @pytest.mark.gpu
+@pytest.mark.parametrize("D,L,S,B,H", [(64, 4, 6, 3, 8), (768, 4, 5, 16, 12)])
+def test_native_flb_training_saved_matches_recompute(cuda, D, L, S, B, H):
+    """The native backward restoring the forward's per-cell intermediates
+    (flb_block_grid_fwd_save / flb_block_grid_bwd_saved, the default) against the same backward
+    recomputing each tick's forward stages (engine.native_flb_save = False): loss and every
+    parameter gradient within 2e-2 of the largest magnitude (the two forwards round z_l and the
+    LayerNorm statistics differently in the last bit)."""
+    m = _bf16_model(19, D=D, L=L, S=S, B=B, heads=H)  # eval mode: no dropout
+    tok = torch.randint(0, 50, (B, S), device=cuda)
+    targets = torch.randint(0, 50, (B, S), device=cuda)
+    gs, ls = _train_grads(m, tok, targets, True)
+    assert m.engine.graph_workspace["flb_saved"].numel() > 0
+    m.engine.native_flb_save = False
+    gr, lr = _train_grads(m, tok, targets, True)
+    assert abs(ls - lr) <= 2e-2 * abs(lr)
+    assert set(gs) == set(gr)
+    for k in gr:
+        assert _max_rel(gs[k], gr[k]) < 2e-2, (k, _max_rel(gs[k], gr[k]))
+
+
+@pytest.mark.gpu
 def test_native_flb_training_against_reference(cuda, flb_golden):
     """Native bf16 gradients against the reference model's fp32 gradients (golden): every
     parameter's gradient within 2e-2 of the reference relative to the tensor's largest
