@@ -24,6 +24,8 @@
 #include <cuda_bf16.h>
 
 #include <algorithm>
+#include <initializer_list>
+#include <utility>
 #include <mutex>
 
 #include "blas.cuh"
@@ -398,50 +400,79 @@ __global__ void blk_ln_init_kernel(bf16* __restrict__ lnr, const float* __restri
   reinterpret_cast<__nv_bfloat162*>(lnr + (int64_t)rowi * D)[j] = __floats2bfloat162_rn(bv.x, bv.y);
 }
 
-// Per-cell records of a training forward's tick intermediates, which the backward restores in
-// place of recomputing its ticks' forward stages: per grid cell (l*S + t) the units
-// [ln_left | ln_diag | lat_prior | tokens x' lat' fdbk_prior | z_l | z_x | q|k|v (9) | att (3)],
-// each B x D bf16 (20 units). dir 0: tick buffers -> records (after a forward tick); 1: records
-// -> tick buffers (before a backward tick). Grid: x over 16-byte chunks of a record, y over the
-// tick's cells.
-constexpr int kCellUnits = 20;
-struct CellBufs {
-  bf16 *ln_left, *ln_diag;  // cell i's LayerNorm rows at + i * ln_cell
-  int64_t ln_cell;
-  bf16 *lat, *tok, *zl, *zx, *qkv, *att;
+// Planes of a training step's per-cell tensors, kept in one buffer (flb_block_grid_saved_bytes):
+// plane p holds, for every grid cell (l*S + t) in order, plane_units(p) units of B x D bf16. The forward
+// fills planes 0-7 with its tick intermediates [ln_left | ln_diag | lat_prior | tokens x' lat'
+// fdbk_prior | z_l | z_x | q|k|v | att], which the backward restores in place of recomputing its
+// ticks' forward stages; the backward fills planes 8-13 with the gradients that meet the weights
+// [d_o | d_q|k|v | d_z_x | d_z_l | d_lat_prior | d_fdbk_prior]. A layer's cells are consecutive in
+// every plane, so each weight gradient is one GEMM per layer over all of its cells at the end.
+__host__ __device__ constexpr int plane_units(int p) {  // units of B x D per cell
+  return (p == 3 || p == 7 || p == 8) ? 3 : (p == 6 || p == 9) ? 9 : 1;
+}
+constexpr int kSavedUnits = 36;  // sum of plane_units over the planes
+enum { PL_LN_LEFT, PL_LN_DIAG, PL_LAT, PL_TOK, PL_ZL, PL_ZX, PL_QKV, PL_ATT, PL_DO, PL_DQKV, PL_DZX,
+       PL_DZL, PL_DLP, PL_DFP };
+
+__host__ __device__ inline int64_t plane_offset(int p, int64_t cells, int64_t BD) {
+  int64_t u = 0;
+  for (int q = 0; q < p; ++q) u += plane_units(q);
+  return u * cells * BD;
+}
+
+// Copy of some planes' cells of one tick to or from the tick buffers: segment k is plane
+// `plane[k]`, whose cell i lies in the tick buffers at tick[k] + i * cell_stride[k] (U units
+// contiguous). dir 0: tick buffers -> planes, 1: planes -> tick buffers. Grid: x over 16-byte
+// chunks of the segments' units, y over the tick's cells.
+constexpr int kMaxSegs = 8;
+struct CopySegs {
+  int count, total_units;
+  int plane[kMaxSegs], unit0[kMaxSegs];
+  bf16* tick[kMaxSegs];
+  int64_t cell_stride[kMaxSegs];
 };
 
-__global__ void blk_cells_copy_kernel(bf16* __restrict__ rec, CellBufs cb, int dir, int T, int l0,
-                                      int S, int B, int D) {
+__global__ void blk_cells_copy_kernel(bf16* __restrict__ planes, CopySegs cs, int dir, int T,
+                                      int l0, int S, int64_t cells, int B, int D) {
   pdl_wait();
   const int i = blockIdx.y;
   const int l = l0 + 2 * i, t = (T - l) / 2;
   const int64_t BD = (int64_t)B * D;
   const int64_t e0 = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) * 8;
-  if (e0 >= kCellUnits * BD) return;
+  if (e0 >= cs.total_units * BD) return;
   const int unit = (int)(e0 / BD);  // B * D is a multiple of 8: a chunk lies in one unit
-  const int64_t in = e0 - unit * BD;
-  bf16* buf;
-  if (unit == 0) buf = cb.ln_left + i * cb.ln_cell + in;
-  else if (unit == 1) buf = cb.ln_diag + i * cb.ln_cell + in;
-  else if (unit == 2) buf = cb.lat + i * BD + in;
-  else if (unit < 6) buf = cb.tok + (3 * i + (unit - 3)) * BD + in;
-  else if (unit == 6) buf = cb.zl + i * BD + in;
-  else if (unit == 7) buf = cb.zx + i * BD + in;
-  else if (unit < 17) buf = cb.qkv + (9 * i + (unit - 8)) * BD + in;
-  else buf = cb.att + (3 * i + (unit - 17)) * BD + in;
-  uint4* r = reinterpret_cast<uint4*>(rec + cell_row(l, t, S) * kCellUnits * BD + e0);
-  uint4* b = reinterpret_cast<uint4*>(buf);
-  if (dir == 0) *r = *b;
-  else *b = *r;
+  int k = 0;
+  while (k + 1 < cs.count && unit >= cs.unit0[k + 1]) ++k;
+  const int p = cs.plane[k];
+  const int64_t in = e0 - (int64_t)cs.unit0[k] * BD;  // within the segment's units of a cell
+  uint4* pl = reinterpret_cast<uint4*>(planes + plane_offset(p, cells, BD) +
+                                       cell_row(l, t, S) * plane_units(p) * BD + in);
+  uint4* tb = reinterpret_cast<uint4*>(cs.tick[k] + i * cs.cell_stride[k] + in);
+  if (dir == 0) *pl = *tb;
+  else *tb = *pl;
 }
 
-int launch_cells_copy(bf16* rec, const CellBufs& cb, int dir, int T, int l0, int n, int S, int B,
-                      int D, cudaStream_t s) {
-  const int64_t chunks = (int64_t)kCellUnits * B * D / 8;
+CopySegs make_segs(std::initializer_list<std::pair<int, std::pair<bf16*, int64_t>>> list) {
+  CopySegs cs{};
+  int u = 0;
+  for (const auto& e : list) {
+    cs.plane[cs.count] = e.first;
+    cs.unit0[cs.count] = u;
+    cs.tick[cs.count] = e.second.first;
+    cs.cell_stride[cs.count] = e.second.second;
+    u += plane_units(e.first);
+    ++cs.count;
+  }
+  cs.total_units = u;
+  return cs;
+}
+
+int launch_cells_copy(bf16* planes, const CopySegs& cs, int dir, int T, int l0, int n, int L, int S,
+                      int B, int D, cudaStream_t s) {
+  const int64_t chunks = (int64_t)cs.total_units * B * D / 8;
   const dim3 grid((unsigned)((chunks + 255) / 256), (unsigned)n);
-  return check_cuda(launch_pdl(blk_cells_copy_kernel, grid, dim3(256), 0, s, rec, cb, dir, T, l0,
-                               S, B, D),
+  return check_cuda(launch_pdl(blk_cells_copy_kernel, grid, dim3(256), 0, s, planes, cs, dir, T,
+                               l0, S, (int64_t)L * S, B, D),
                     "block_grid intermediates copy");
 }
 
@@ -801,8 +832,15 @@ int block_grid_fwd_ex(const flb_block_weights* W, const void* x, void* grids, in
     if (saved) {  // the tick's intermediates, for the backward
       const long long LBD = (long long)L * BD;
       bf16* ln_left = w.lnr + (long long)(T % 3) * 2 * LBD + (long long)l0 * BD;
-      const CellBufs cb{ln_left, ln_left + LBD, 2 * BD, w.lat, w.tok, w.z, w.zx, w.qkv, w.att};
-      if ((st = launch_cells_copy(reinterpret_cast<bf16*>(saved), cb, 0, T, l0, n, Si, Bi, Di, s)) != FLB_OK)
+      const CopySegs cs = make_segs({{PL_LN_LEFT, {ln_left, 2 * BD}},
+                                     {PL_LN_DIAG, {ln_left + LBD, 2 * BD}},
+                                     {PL_LAT, {w.lat, BD}},
+                                     {PL_TOK, {w.tok, 3 * BD}},
+                                     {PL_ZL, {w.z, BD}},
+                                     {PL_ZX, {w.zx, BD}},
+                                     {PL_QKV, {w.qkv, 9 * BD}},
+                                     {PL_ATT, {w.att, 3 * BD}}});
+      if ((st = launch_cells_copy(reinterpret_cast<bf16*>(saved), cs, 0, T, l0, n, Li, Si, Bi, Di, s)) != FLB_OK)
         return st;
       ++launches;
     }
@@ -1266,7 +1304,7 @@ size_t block_bwd_ws_layout(int64_t L, int64_t S, int64_t B, int64_t D, BlockBwdW
 }  // namespace
 
 size_t block_grid_saved_bytes(int64_t L, int64_t S, int64_t B, int64_t D) {
-  return (size_t)L * S * kCellUnits * B * D * sizeof(bf16);
+  return (size_t)L * S * kSavedUnits * B * D * sizeof(bf16);
 }
 
 size_t block_grid_bwd_workspace_bytes(int64_t L, int64_t S, int64_t B, int64_t D) {
@@ -1277,6 +1315,7 @@ int block_grid_bwd(const flb_block_weights* W, const void* x, const void* grids,
                    const void* const* dgrids, float* dx, const flb_block_grads* G, int64_t L,
                    int64_t S, int64_t B, int64_t D, int64_t H, float eps, void* ws,
                    size_t ws_bytes, cudaStream_t s, const void* saved) {
+  bf16* planes = const_cast<bf16*>(reinterpret_cast<const bf16*>(saved));  // null: recompute
   BlockBwdWs w;
   block_bwd_ws_layout(L, S, B, D, &w, ws);
   SideStream* side;
@@ -1318,11 +1357,15 @@ int block_grid_bwd(const flb_block_weights* W, const void* x, const void* grids,
     const int n = tk.n, l0 = tk.l0;
     if (n == 0) continue;
     if (saved) {  // the forward's intermediates of the tick, restored instead of recomputed
-      const CellBufs cb{w.f.ln, w.f.ln + n * BD, BD, w.f.lat, w.f.tok, w.f.zl, w.f.zx, w.f.qkv,
-                        w.f.att};
-      if ((st = launch_cells_copy(const_cast<bf16*>(reinterpret_cast<const bf16*>(saved)), cb, 1, T,
-                                  l0, n, Si, Bi, Di, s)) != FLB_OK)
-        return st;
+      const CopySegs cs = make_segs({{PL_LN_LEFT, {w.f.ln, BD}},
+                                     {PL_LN_DIAG, {w.f.ln + n * BD, BD}},
+                                     {PL_LAT, {w.f.lat, BD}},
+                                     {PL_TOK, {w.f.tok, 3 * BD}},
+                                     {PL_ZL, {w.f.zl, BD}},
+                                     {PL_ZX, {w.f.zx, BD}},
+                                     {PL_QKV, {w.f.qkv, 9 * BD}},
+                                     {PL_ATT, {w.f.att, 3 * BD}}});
+      if ((st = launch_cells_copy(planes, cs, 1, T, l0, n, Li, Si, Bi, Di, s)) != FLB_OK) return st;
     } else if ((st = tick_forward(hb, Side{side, hs}, W, xb, g, port_stride, w.f, T, l0, n, Li, Si,
                                   Bi, Di, Hi, eps, s)) != FLB_OK) {
       return st;
@@ -1345,8 +1388,8 @@ int block_grid_bwd(const flb_block_weights* W, const void* x, const void* grids,
     if ((st = gemm_rm(hb, false, false, 3 * Bi, Di, Di, w.d_o, Di, 3 * BD, Wo, Di, 2 * DD, w.d_att,
                       Di, 3 * BD, n, 0.f, CUDA_R_16BF)) != FLB_OK)
       return st;
-    if ((st = fork(0)) != FLB_OK) return st;
-    if ((st = gemm_rm(hs, true, false, Di, Di, 3 * Bi, w.d_o, Di, 3 * BD, w.f.att, Di, 3 * BD,
+    if (!saved && (st = fork(0)) != FLB_OK) return st;
+    if (!saved && (st = gemm_rm(hs, true, false, Di, Di, 3 * Bi, w.d_o, Di, 3 * BD, w.f.att, Di, 3 * BD,
                       G->w_o + (int64_t)l0 * DD, Di, 2 * DD, n, 1.f)) != FLB_OK)
       return st;
     if ((ce = launch_pdl(blk_attn3_bwd_kernel, dim3((n * Bi * Hi + 7) / 8), dim3(256), 0, s,
@@ -1357,8 +1400,8 @@ int block_grid_bwd(const flb_block_weights* W, const void* x, const void* grids,
     if ((st = gemm_rm(hb, false, false, 3 * Bi, Di, 3 * Di, w.d_qkv, 3 * Di, 9 * BD, Wqkv, Di,
                       6 * DD, w.dT, Di, 3 * BD, n, 0.f)) != FLB_OK)
       return st;
-    if ((st = fork(1)) != FLB_OK) return st;
-    if ((st = gemm_rm(hs, true, false, 3 * Di, Di, 3 * Bi, w.d_qkv, 3 * Di, 9 * BD, w.f.tok, Di,
+    if (!saved && (st = fork(1)) != FLB_OK) return st;
+    if (!saved && (st = gemm_rm(hs, true, false, 3 * Di, Di, 3 * Bi, w.d_qkv, 3 * Di, 9 * BD, w.f.tok, Di,
                       3 * BD, G->w_qkv + (int64_t)l0 * 3 * DD, Di, 6 * DD, n, 1.f)) != FLB_OK)
       return st;
     // sensory gate
@@ -1369,8 +1412,8 @@ int block_grid_bwd(const flb_block_weights* W, const void* x, const void* grids,
     if ((st = gemm_rm(hb, false, false, Bi, Di, Di, w.d_zx, Di, BD, Wgx, Di, 2 * DD, w.d_lr, Di, BD,
                       n, 1.f)) != FLB_OK)
       return st;
-    if ((st = fork(2)) != FLB_OK) return st;
-    if ((st = gemm_rm(hs, true, false, Di, Di, Bi, w.d_zx, Di, BD, w.f.tok + D, 3 * Di, 3 * BD,
+    if (!saved && (st = fork(2)) != FLB_OK) return st;
+    if (!saved && (st = gemm_rm(hs, true, false, Di, Di, Bi, w.d_zx, Di, BD, w.f.tok + D, 3 * Di, 3 * BD,
                       G->w_gate_x + (int64_t)l0 * DD, Di, 2 * DD, n, 1.f)) != FLB_OK)
       return st;
     // lateral gate
@@ -1381,8 +1424,8 @@ int block_grid_bwd(const flb_block_weights* W, const void* x, const void* grids,
     if ((st = gemm_rm(hb, false, false, Bi, Di, Di, w.d_zl, Di, BD, Wgl, Di, 2 * DD, w.d_fp, Di, BD,
                       n, 1.f)) != FLB_OK)
       return st;
-    if ((st = fork(3)) != FLB_OK) return st;
-    if ((st = gemm_rm(hs, true, false, Di, Di, Bi, w.d_zl, Di, BD, w.f.tok + 2 * D, 3 * Di, 3 * BD,
+    if (!saved && (st = fork(3)) != FLB_OK) return st;
+    if (!saved && (st = gemm_rm(hs, true, false, Di, Di, Bi, w.d_zl, Di, BD, w.f.tok + 2 * D, 3 * Di, 3 * BD,
                       G->w_gate_l + (int64_t)l0 * DD, Di, 2 * DD, n, 1.f)) != FLB_OK)
       return st;
     if ((ce = launch_pdl(blk_cast_kernel,
@@ -1397,11 +1440,11 @@ int block_grid_bwd(const flb_block_weights* W, const void* x, const void* grids,
     if ((st = gemm_rm(hb, false, false, Bi, Di, Di, w.d_fp_h, Di, BD, Wpf, Di, 2 * DD,
                       w.dA + n * BD, Di, BD, n, 0.f)) != FLB_OK)
       return st;
-    if ((st = fork(4)) != FLB_OK) return st;
-    if ((st = gemm_rm(hs, true, false, Di, Di, Bi, w.d_lp_h, Di, BD, w.f.ln, Di, BD,
+    if (!saved && (st = fork(4)) != FLB_OK) return st;
+    if (!saved && (st = gemm_rm(hs, true, false, Di, Di, Bi, w.d_lp_h, Di, BD, w.f.ln, Di, BD,
                       G->w_prior_lat + (int64_t)l0 * DD, Di, 2 * DD, n, 1.f)) != FLB_OK)
       return st;
-    if ((st = gemm_rm(hs, true, false, Di, Di, Bi, w.d_fp_h, Di, BD, w.f.ln + n * BD, Di, BD,
+    if (!saved && (st = gemm_rm(hs, true, false, Di, Di, Bi, w.d_fp_h, Di, BD, w.f.ln + n * BD, Di, BD,
                       G->w_prior_fdbk + (int64_t)l0 * DD, Di, 2 * DD, n, 1.f)) != FLB_OK)
       return st;
     if ((ce = launch_pdl(blk_ln_bwd_kernel, dim3(2 * n), dim3(512), 4 * B * sizeof(float), s, g,
@@ -1409,8 +1452,46 @@ int block_grid_bwd(const flb_block_weights* W, const void* x, const void* grids,
                          G->ln_lat_w, G->ln_lat_b, G->ln_fdbk_w, G->ln_fdbk_b, T, l0, n, Li, Si,
                          Bi, Di, eps)) != cudaSuccess)
       return check_cuda(ce, "block_grid_bwd launch");
-    if ((st = join()) != FLB_OK) return st;
+    if (saved) {  // the gradients that meet the weights, for the GEMMs after the loop
+      const CopySegs cs = make_segs({{PL_DO, {w.d_o, 3 * BD}},
+                                     {PL_DQKV, {w.d_qkv, 9 * BD}},
+                                     {PL_DZX, {w.d_zx, BD}},
+                                     {PL_DZL, {w.d_zl, BD}},
+                                     {PL_DLP, {w.d_lp_h, BD}},
+                                     {PL_DFP, {w.d_fp_h, BD}}});
+      if ((st = launch_cells_copy(planes, cs, 0, T, l0, n, Li, Si, Bi, Di, s)) != FLB_OK) return st;
+    } else if ((st = join()) != FLB_OK) {
+      return st;
+    }
     launches += 10;  // own kernels (4 recompute + 6 backward)
+  }
+  if (saved) {
+    // Weight gradients: per layer, one GEMM over all of its cells (K = S x rows), from the
+    // gradient planes the ticks filled and the activations the forward kept. Each layer's cells
+    // are consecutive in every plane: batch = layers, stride = one layer's cells.
+    const int64_t LS = L * S;
+    auto pl = [&](int p) { return planes + plane_offset(p, LS, BD); };
+    const long long c1 = (long long)S * BD, c3 = 3 * c1, c9 = 9 * c1;  // a layer's cells, per plane
+    const int K1 = (int)(S * B), K3 = 3 * K1;
+    if ((st = gemm_rm(hb, true, false, Di, Di, K3, pl(PL_DO), Di, c3, pl(PL_ATT), Di, c3, G->w_o, Di,
+                      DD, Li, 1.f)) != FLB_OK)
+      return st;
+    if ((st = gemm_rm(hb, true, false, 3 * Di, Di, K3, pl(PL_DQKV), 3 * Di, c9, pl(PL_TOK), Di, c3,
+                      G->w_qkv, Di, 3 * DD, Li, 1.f)) != FLB_OK)
+      return st;
+    // token slots 1 (lat') and 2 (fdbk_prior): rows of pitch 3D inside the token plane
+    if ((st = gemm_rm(hb, true, false, Di, Di, K1, pl(PL_DZX), Di, c1, pl(PL_TOK) + D, 3 * Di, c3,
+                      G->w_gate_x, Di, DD, Li, 1.f)) != FLB_OK)
+      return st;
+    if ((st = gemm_rm(hb, true, false, Di, Di, K1, pl(PL_DZL), Di, c1, pl(PL_TOK) + 2 * D, 3 * Di, c3,
+                      G->w_gate_l, Di, DD, Li, 1.f)) != FLB_OK)
+      return st;
+    if ((st = gemm_rm(hb, true, false, Di, Di, K1, pl(PL_DLP), Di, c1, pl(PL_LN_LEFT), Di, c1,
+                      G->w_prior_lat, Di, DD, Li, 1.f)) != FLB_OK)
+      return st;
+    if ((st = gemm_rm(hb, true, false, Di, Di, K1, pl(PL_DFP), Di, c1, pl(PL_LN_DIAG), Di, c1,
+                      G->w_prior_fdbk, Di, DD, Li, 1.f)) != FLB_OK)
+      return st;
   }
   count_launches(launches);
   return check_cuda(cudaGetLastError(), "flb block grid backward launch");

@@ -12,8 +12,10 @@ per-layer fp32 weight-gradient stacks). bf16 compute only (the reference model r
 autocast). Setting engine.native_flb_path = 2 (FLB_BLOCK_PATH_PERSISTENT) runs the inference
 forward as one persistent tcgen05 kernel instead (batch 16, d_model a multiple of 128). A
 training forward keeps every cell's intermediates (flb_block_grid_fwd_save) so that the backward
-restores them instead of recomputing its ticks' forward stages; engine.native_flb_save = False
-trades that memory (L * S * 20 * batch * d_model bf16) for the recompute.
+restores them instead of recomputing its ticks' forward stages, and keeps the gradients that
+meet the weights beside them to form every weight gradient in a few large GEMMs at its end;
+engine.native_flb_save = False trades that memory (L * S * 36 * batch * d_model bf16) for the
+recompute and per-tick weight-gradient GEMMs.
 """
 from __future__ import annotations
 

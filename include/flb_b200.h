@@ -323,8 +323,10 @@ int flb_block_grid_fwd_drop_barrier_test(const flb_block_weights* weights, const
  * reference's autograd keeps the vmapped cells' tensors): flb_block_grid_fwd (tick by tick,
  * cuBLAS projections) that also writes, per cell, its LayerNorm outputs, lat_prior, the three
  * tokens, z_l, z_x, q|k|v and the attention output into `saved` (flb_block_grid_saved_bytes()
- * bytes, 16-byte aligned: L * S * 20 * batch * D bf16), which flb_block_grid_bwd_saved reads
- * back instead of recomputing each tick's forward stages. */
+ * bytes, 16-byte aligned: L * S * 36 * batch * D bf16), which flb_block_grid_bwd_saved reads
+ * back instead of recomputing each tick's forward stages; that backward also keeps the
+ * gradients that meet the weights there and forms every weight gradient after its tick loop,
+ * one GEMM per weight over all layers. */
 size_t flb_block_grid_saved_bytes(int64_t L, int64_t S, int64_t batch, int64_t D);
 int flb_block_grid_fwd_save(const flb_block_weights* weights, const void* x, void* grids, int64_t L,
                             int64_t S, int64_t batch, int64_t D, int64_t heads, float ln_eps,
