@@ -1433,10 +1433,17 @@ int block_grid_bwd(const flb_block_weights* W, const void* x, const void* grids,
                          dim3(256), 0, s, w.d_fp, w.d_fp_h, (int64_t)(n * BD / 2))) !=
         cudaSuccess)
       return check_cuda(ce, "block_grid_bwd launch");
-    // priors
-    if ((st = gemm_rm(hb, false, false, Bi, Di, Di, w.d_lp_h, Di, BD, Wpl, Di, 2 * DD, w.dA, Di, BD,
-                      n, 0.f)) != FLB_OK)
+    // priors (with the intermediates kept, the lateral prior's input gradient runs on the side
+    // stream beside the z_l / cast / feedback-prior chain; joined before the LayerNorm backward)
+    if (saved) {
+      if ((st = fork(4)) != FLB_OK) return st;
+      if ((st = gemm_rm(hs, false, false, Bi, Di, Di, w.d_lp_h, Di, BD, Wpl, Di, 2 * DD, w.dA, Di,
+                        BD, n, 0.f)) != FLB_OK)
+        return st;
+    } else if ((st = gemm_rm(hb, false, false, Bi, Di, Di, w.d_lp_h, Di, BD, Wpl, Di, 2 * DD, w.dA,
+                             Di, BD, n, 0.f)) != FLB_OK) {
       return st;
+    }
     if ((st = gemm_rm(hb, false, false, Bi, Di, Di, w.d_fp_h, Di, BD, Wpf, Di, 2 * DD,
                       w.dA + n * BD, Di, BD, n, 0.f)) != FLB_OK)
       return st;
@@ -1447,6 +1454,7 @@ int block_grid_bwd(const flb_block_weights* W, const void* x, const void* grids,
     if (!saved && (st = gemm_rm(hs, true, false, Di, Di, Bi, w.d_fp_h, Di, BD, w.f.ln + n * BD, Di, BD,
                       G->w_prior_fdbk + (int64_t)l0 * DD, Di, 2 * DD, n, 1.f)) != FLB_OK)
       return st;
+    if (saved && (st = join()) != FLB_OK) return st;
     if ((ce = launch_pdl(blk_ln_bwd_kernel, dim3(2 * n), dim3(512), 4 * B * sizeof(float), s, g,
                          port_stride, w.dA, W->ln_lat_w, W->ln_fdbk_w, w.dG, per_port,
                          G->ln_lat_w, G->ln_lat_b, G->ln_fdbk_w, G->ln_fdbk_b, T, l0, n, Li, Si,
