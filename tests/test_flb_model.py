@@ -114,11 +114,14 @@ def _max_rel(a, b):
 
 
 @pytest.mark.gpu
-def test_native_flb_forward_matches_generic_path(cuda):
+@pytest.mark.parametrize("D,B", [(64, 3), (96, 20), (80, 4)])
+def test_native_flb_forward_matches_generic_path(cuda, D, B):
     """Inference under bf16 autocast: the native whole-grid forward (flb_block_grid_fwd) against
-    the per-tick vmapped path of the same engine: every port grid, logits and contexts."""
-    m = _bf16_model(7)
-    tok = torch.randint(0, 50, (3, 6), device=cuda)
+    the per-tick vmapped path of the same engine: every port grid, logits and contexts, at
+    several d_model and batch sizes (batch 20: more rows per cell than the end-to-end shape's 16;
+    d_model 80 and 96: not powers of two)."""
+    m = _bf16_model(7, D=D, B=B)
+    tok = torch.randint(0, 50, (B, 6), device=cuda)
     with torch.no_grad(), torch.autocast("cuda", dtype=torch.bfloat16):
         x = m.embedding(tok)
         m.engine.native_cells = False
