@@ -403,10 +403,12 @@ __global__ void blk_ln_init_kernel(bf16* __restrict__ lnr, const float* __restri
 // Planes of a training step's per-cell tensors, kept in one buffer (flb_block_grid_saved_bytes):
 // plane p holds, for every grid cell (l*S + t) in order, plane_units(p) units of B x D bf16. The forward
 // fills planes 0-7 with its tick intermediates [ln_left | ln_diag | lat_prior | tokens x' lat'
-// fdbk_prior | z_l | z_x | q|k|v | att], which the backward restores in place of recomputing its
-// ticks' forward stages; the backward fills planes 8-13 with the gradients that meet the weights
-// [d_o | d_q|k|v | d_z_x | d_z_l | d_lat_prior | d_fdbk_prior]. A layer's cells are consecutive in
-// every plane, so each weight gradient is one GEMM per layer over all of its cells at the end.
+// fdbk_prior | z_l | z_x | q|k|v | att], which the backward reads in place of recomputing its
+// ticks' forward stages; the backward's kernels and GEMMs write planes 8-13, the gradients that
+// meet the weights [d_o | d_q|k|v | d_z_x | d_z_l | d_lat_prior | d_fdbk_prior], directly. A tick's
+// cells lie 2S - 1 cells apart in a plane (one stride per strided-batched GEMM), and a layer's
+// cells are consecutive, so each weight gradient is one GEMM per layer over all of its cells at
+// the end.
 __host__ __device__ constexpr int plane_units(int p) {  // units of B x D per cell
   return (p == 3 || p == 7 || p == 8) ? 3 : (p == 6 || p == 9) ? 9 : 1;
 }
@@ -906,7 +908,7 @@ __global__ void blk_dg_init_kernel(const bf16* __restrict__ g0, const bf16* __re
 __global__ void blk_bwd_out_kernel(const float* __restrict__ dG, int64_t per_port,
                                    const bf16* __restrict__ ext3, const bf16* __restrict__ grids,
                                    int64_t port_stride, const bf16* __restrict__ lat,
-                                   const bf16* __restrict__ tok, bf16* __restrict__ d_o,
+                                   const bf16* __restrict__ tok, bf16* __restrict__ d_o, int64_t cs,
                                    float* __restrict__ d_top, float* __restrict__ d_lp,
                                    float* __restrict__ d_fp, int T, int l0, int S, int B, int D) {
   pdl_wait();
@@ -925,11 +927,11 @@ __global__ void blk_bwd_out_kernel(const float* __restrict__ dG, int64_t per_por
     return __bfloat1622float2(reinterpret_cast<const __nv_bfloat162*>(p)[j]);
   };
   const float2 hl = ld2(grids + port_stride + off), hf = ld2(grids + 2 * port_stride + off);
-  const int64_t r3 = (int64_t)rb * 3;
-  const float2 lp = ld2(lat + (int64_t)rb * D), fp = ld2(tok + (r3 + 2) * D);
-  reinterpret_cast<__nv_bfloat162*>(d_o + r3 * D)[j] = __floats2bfloat162_rn(dhx.x, dhx.y);
-  reinterpret_cast<__nv_bfloat162*>(d_o + (r3 + 1) * D)[j] = __floats2bfloat162_rn(dhl.x, dhl.y);
-  reinterpret_cast<__nv_bfloat162*>(d_o + (r3 + 2) * D)[j] = __floats2bfloat162_rn(dhf.x, dhf.y);
+  const int64_t cr = (int64_t)i * cs + (int64_t)b * D;  // row of a one-unit cell array
+  const float2 lp = ld2(lat + cr), fp = ld2(tok + 3 * cr + 2 * D);
+  reinterpret_cast<__nv_bfloat162*>(d_o + 3 * cr)[j] = __floats2bfloat162_rn(dhx.x, dhx.y);
+  reinterpret_cast<__nv_bfloat162*>(d_o + 3 * cr + D)[j] = __floats2bfloat162_rn(dhl.x, dhl.y);
+  reinterpret_cast<__nv_bfloat162*>(d_o + 3 * cr + 2 * D)[j] = __floats2bfloat162_rn(dhf.x, dhf.y);
   reinterpret_cast<float2*>(d_top + (int64_t)rb * D)[j] = dhx;
   reinterpret_cast<float2*>(d_lp + (int64_t)rb * D)[j] =
       make_float2(dhl.x + 2.f * (lp.x - hl.x) * da.x, dhl.y + 2.f * (lp.y - hl.y) * da.y);
@@ -940,7 +942,8 @@ __global__ void blk_bwd_out_kernel(const float* __restrict__ dG, int64_t per_por
 // 3-token attention backward, one warp per (cell, batch row, head)
 __global__ void blk_attn3_bwd_kernel(const bf16* __restrict__ qkv, const float* __restrict__ v_a,
                                      const bf16* __restrict__ d_att, bf16* __restrict__ d_qkv,
-                                     float* __restrict__ d_va, int l0, int n, int B, int D, int H) {
+                                     int64_t cs, float* __restrict__ d_va, int l0, int n, int B,
+                                     int D, int H) {
   pdl_wait();
   const int warps = blockDim.x >> 5, lane = threadIdx.x & 31;
   const int task = blockIdx.x * warps + (threadIdx.x >> 5);
@@ -951,7 +954,8 @@ __global__ void blk_attn3_bwd_kernel(const bf16* __restrict__ qkv, const float* 
   const int dh = D / H;
   const int64_t wrow = ((int64_t)(l0 + 2 * i) * H + h) * dh;
   const float* w = v_a + wrow;
-  const bf16* base = qkv + rb * 3 * (3 * D) + h * dh;
+  const int64_t cr = (int64_t)i * cs + (rb - (int64_t)i * B) * D;  // one-unit row of (cell, b)
+  const bf16* base = qkv + 9 * cr + h * dh;
   const bf16* dob = d_att + rb * 3 * D + h * dh;
   float q[4][3], k[4][3], v[4][3], dout[4][3], wd[4];
   float s[3][3], dp[3][3];
@@ -1005,7 +1009,7 @@ __global__ void blk_attn3_bwd_kernel(const bf16* __restrict__ qkv, const float* 
 #pragma unroll
     for (int c = 0; c < 3; ++c) ds[a][c] = p[a][c] * (dp[a][c] - dot) * scale;
   }
-  bf16* dbase = d_qkv + rb * 3 * (3 * D) + h * dh;
+  bf16* dbase = d_qkv + 9 * cr + h * dh;
 #pragma unroll
   for (int kk = 0; kk < 4; ++kk) {
     const int d = lane + 32 * kk;
@@ -1039,8 +1043,9 @@ __global__ void blk_gx_bwd_kernel(const float* __restrict__ dT, const bf16* __re
                                   const bf16* __restrict__ x, const float* __restrict__ d_top,
                                   float* __restrict__ dG0, float* __restrict__ dx,
                                   bf16* __restrict__ d_zx, float* __restrict__ d_lr,
-                                  float* __restrict__ d_fp, float* __restrict__ db_gx, int T,
-                                  int l0, int S, int B, int D) {
+                                  const float* __restrict__ d_fp, bf16* __restrict__ d_fp_h,
+                                  int64_t cs, float* __restrict__ db_gx, int T, int l0, int S,
+                                  int B, int D) {
   pdl_wait();
   // block: 32 feature pairs (x) by up to 16 batch rows (y); the bias gradient is summed over
   // the rows in a fixed order (deterministic)
@@ -1054,8 +1059,9 @@ __global__ void blk_gx_bwd_kernel(const float* __restrict__ dT, const bf16* __re
     const float2 bias = reinterpret_cast<const float2*>(b_gx + (int64_t)l * D)[j];
     for (int b = threadIdx.y; b < B; b += blockDim.y) {
       const int64_t rb = (int64_t)i * B + b;
+      const int64_t cr = (int64_t)i * cs + (int64_t)b * D;
       const float2 dxr = reinterpret_cast<const float2*>(dT + (rb * 3) * D)[j];
-      const float2 z = __bfloat1622float2(reinterpret_cast<const __nv_bfloat162*>(zx + rb * D)[j]);
+      const float2 z = __bfloat1622float2(reinterpret_cast<const __nv_bfloat162*>(zx + cr)[j]);
       const float2 top = __bfloat1622float2(
           reinterpret_cast<const __nv_bfloat162*>(top_row(grids, x, l, t, b, S, B, D))[j]);
       const float s0 = sigm(z.x + bias.x), s1 = sigm(z.y + bias.y);
@@ -1069,15 +1075,17 @@ __global__ void blk_gx_bwd_kernel(const float* __restrict__ dT, const bf16* __re
         reinterpret_cast<float2*>(dx + ((int64_t)b * S + t) * D)[j] = dtop;
       }
       const float dz0 = dxr.x * top.x * s0 * (1.f - s0), dz1 = dxr.y * top.y * s1 * (1.f - s1);
-      reinterpret_cast<__nv_bfloat162*>(d_zx + rb * D)[j] = __floats2bfloat162_rn(dz0, dz1);
+      reinterpret_cast<__nv_bfloat162*>(d_zx + cr)[j] = __floats2bfloat162_rn(dz0, dz1);
       acc.x += dz0;
       acc.y += dz1;
       reinterpret_cast<float2*>(d_lr + rb * D)[j] =
           reinterpret_cast<const float2*>(dT + (rb * 3 + 1) * D)[j];
+      // d_fdbk_prior so far (residual + aux, then the q|k|v token's share), in bf16: the
+      // operand of the G_L GEMM that adds d_zL G_L in place (no separate cast)
       const float2 dtf = reinterpret_cast<const float2*>(dT + (rb * 3 + 2) * D)[j];
-      float2* fp = reinterpret_cast<float2*>(d_fp + rb * D) + j;
-      const float2 o = *fp;
-      *fp = make_float2(o.x + dtf.x, o.y + dtf.y);
+      const float2 o = reinterpret_cast<const float2*>(d_fp + rb * D)[j];
+      reinterpret_cast<__nv_bfloat162*>(d_fp_h + cr)[j] =
+          __floats2bfloat162_rn(o.x + dtf.x, o.y + dtf.y);
     }
   }
   part[threadIdx.y][threadIdx.x] = acc;
@@ -1098,8 +1106,8 @@ __global__ void blk_gx_bwd_kernel(const float* __restrict__ dT, const bf16* __re
 __global__ void blk_gl_bwd_kernel(const float* __restrict__ d_lr, const bf16* __restrict__ zl,
                                   const float* __restrict__ b_gl, const bf16* __restrict__ lat,
                                   float* __restrict__ d_lp, bf16* __restrict__ d_lp_h,
-                                  bf16* __restrict__ d_zl, float* __restrict__ db_gl, int l0,
-                                  int B, int D) {
+                                  bf16* __restrict__ d_zl, int64_t cs, float* __restrict__ db_gl,
+                                  int l0, int B, int D) {
   pdl_wait();
   __shared__ float2 part[16][32];  // as blk_gx_bwd_kernel: 32 pairs by up to 16 rows
   const int j = blockIdx.x * 32 + threadIdx.x;
@@ -1111,15 +1119,16 @@ __global__ void blk_gl_bwd_kernel(const float* __restrict__ d_lr, const bf16* __
     const float2 bias = reinterpret_cast<const float2*>(b_gl + (int64_t)l * D)[j];
     for (int b = threadIdx.y; b < B; b += blockDim.y) {
       const int64_t rb = (int64_t)i * B + b;
+      const int64_t cr = (int64_t)i * cs + (int64_t)b * D;
       const float2 dl = reinterpret_cast<const float2*>(d_lr + rb * D)[j];
-      const float2 z = __bfloat1622float2(reinterpret_cast<const __nv_bfloat162*>(zl + rb * D)[j]);
-      const float2 lp = __bfloat1622float2(reinterpret_cast<const __nv_bfloat162*>(lat + rb * D)[j]);
+      const float2 z = __bfloat1622float2(reinterpret_cast<const __nv_bfloat162*>(zl + cr)[j]);
+      const float2 lp = __bfloat1622float2(reinterpret_cast<const __nv_bfloat162*>(lat + cr)[j]);
       const float s0 = sigm(z.x + bias.x), s1 = sigm(z.y + bias.y);
       const float2 o = reinterpret_cast<const float2*>(d_lp + rb * D)[j];
       const float2 dlp = make_float2(o.x + dl.x * s0, o.y + dl.y * s1);
-      reinterpret_cast<__nv_bfloat162*>(d_lp_h + rb * D)[j] = __floats2bfloat162_rn(dlp.x, dlp.y);
+      reinterpret_cast<__nv_bfloat162*>(d_lp_h + cr)[j] = __floats2bfloat162_rn(dlp.x, dlp.y);
       const float dz0 = dl.x * lp.x * s0 * (1.f - s0), dz1 = dl.y * lp.y * s1 * (1.f - s1);
-      reinterpret_cast<__nv_bfloat162*>(d_zl + rb * D)[j] = __floats2bfloat162_rn(dz0, dz1);
+      reinterpret_cast<__nv_bfloat162*>(d_zl + cr)[j] = __floats2bfloat162_rn(dz0, dz1);
       acc.x += dz0;
       acc.y += dz1;
     }
@@ -1135,16 +1144,6 @@ __global__ void blk_gl_bwd_kernel(const float* __restrict__ d_lr, const bf16* __
     float2* db = reinterpret_cast<float2*>(db_gl + (int64_t)l * D) + j;
     const float2 o = *db;
     *db = make_float2(o.x + sum.x, o.y + sum.y);
-  }
-}
-
-__global__ void blk_cast_kernel(const float* __restrict__ src, bf16* __restrict__ dst,
-                                int64_t pairs) {
-  pdl_wait();
-  for (int64_t e = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; e < pairs;
-       e += (int64_t)gridDim.x * blockDim.x) {
-    const float2 v = reinterpret_cast<const float2*>(src)[e];
-    reinterpret_cast<__nv_bfloat162*>(dst)[e] = __floats2bfloat162_rn(v.x, v.y);
   }
 }
 
@@ -1356,16 +1355,30 @@ int block_grid_bwd(const flb_block_weights* W, const void* x, const void* grids,
     const Tick tk = tick_of(T, Li, Si);
     const int n = tk.n, l0 = tk.l0;
     if (n == 0) continue;
-    if (saved) {  // the forward's intermediates of the tick, restored instead of recomputed
-      const CopySegs cs = make_segs({{PL_LN_LEFT, {w.f.ln, BD}},
-                                     {PL_LN_DIAG, {w.f.ln + n * BD, BD}},
-                                     {PL_LAT, {w.f.lat, BD}},
-                                     {PL_TOK, {w.f.tok, 3 * BD}},
-                                     {PL_ZL, {w.f.zl, BD}},
-                                     {PL_ZX, {w.f.zx, BD}},
-                                     {PL_QKV, {w.f.qkv, 9 * BD}},
-                                     {PL_ATT, {w.f.att, 3 * BD}}});
-      if ((st = launch_cells_copy(planes, cs, 1, T, l0, n, Li, Si, Bi, Di, s)) != FLB_OK) return st;
+    // The tick's forward intermediates and its gradient operands, cell i of the tick at
+    // base + i * units * cs: with the forward's intermediates kept, the planes themselves (a
+    // tick's cells lie 2S - 1 cells apart there; nothing is copied in or out), else the work
+    // buffers the recomputed forward fills (cs = B x D)
+    int64_t cs = BD;
+    const bf16 *f_lat = w.f.lat, *f_tok = w.f.tok, *f_zl = w.f.zl, *f_zx = w.f.zx,
+               *f_qkv = w.f.qkv;
+    bf16 *d_o = w.d_o, *d_qkv = w.d_qkv, *d_zx = w.d_zx, *d_zl = w.d_zl, *d_lp_h = w.d_lp_h,
+         *d_fp_h = w.d_fp_h;
+    if (saved) {
+      cs = (2 * S - 1) * BD;
+      const int64_t c0 = (int64_t)l0 * S + (T - l0) / 2;  // flat index of the tick's first cell
+      auto at = [&](int p) { return planes + plane_offset(p, L * S, BD) + c0 * plane_units(p) * BD; };
+      f_lat = at(PL_LAT);
+      f_tok = at(PL_TOK);
+      f_zl = at(PL_ZL);
+      f_zx = at(PL_ZX);
+      f_qkv = at(PL_QKV);
+      d_o = at(PL_DO);
+      d_qkv = at(PL_DQKV);
+      d_zx = at(PL_DZX);
+      d_zl = at(PL_DZL);
+      d_lp_h = at(PL_DLP);
+      d_fp_h = at(PL_DFP);
     } else if ((st = tick_forward(hb, Side{side, hs}, W, xb, g, port_stride, w.f, T, l0, n, Li, Si,
                                   Bi, Di, Hi, eps, s)) != FLB_OK) {
       return st;
@@ -1375,7 +1388,7 @@ int block_grid_bwd(const flb_block_weights* W, const void* x, const void* grids,
     const dim3 pair_grid((unsigned)((D / 2 + 31) / 32), (unsigned)n);
     const dim3 pair_block(32, (unsigned)std::min<int64_t>(B, 16));
     if ((ce = launch_pdl(blk_bwd_out_kernel, ew_grid, dim3(128), 0, s, w.dG, per_port, ext3, g,
-                         port_stride, w.f.lat, w.f.tok, w.d_o, w.d_top, w.d_lp, w.d_fp, T, l0,
+                         port_stride, f_lat, f_tok, d_o, cs, w.d_top, w.d_lp, w.d_fp, T, l0,
                          Si, Bi, Di)) != cudaSuccess)
       return check_cuda(ce, "block_grid_bwd launch");
     const bf16* Wo = reinterpret_cast<const bf16*>(W->w_o) + (int64_t)l0 * DD;
@@ -1385,7 +1398,7 @@ int block_grid_bwd(const flb_block_weights* W, const void* x, const void* grids,
     const bf16* Wpl = reinterpret_cast<const bf16*>(W->w_prior_lat) + (int64_t)l0 * DD;
     const bf16* Wpf = reinterpret_cast<const bf16*>(W->w_prior_fdbk) + (int64_t)l0 * DD;
     // output projection
-    if ((st = gemm_rm(hb, false, false, 3 * Bi, Di, Di, w.d_o, Di, 3 * BD, Wo, Di, 2 * DD, w.d_att,
+    if ((st = gemm_rm(hb, false, false, 3 * Bi, Di, Di, d_o, Di, 3 * cs, Wo, Di, 2 * DD, w.d_att,
                       Di, 3 * BD, n, 0.f, CUDA_R_16BF)) != FLB_OK)
       return st;
     if (!saved && (st = fork(0)) != FLB_OK) return st;
@@ -1393,11 +1406,11 @@ int block_grid_bwd(const flb_block_weights* W, const void* x, const void* grids,
                       G->w_o + (int64_t)l0 * DD, Di, 2 * DD, n, 1.f)) != FLB_OK)
       return st;
     if ((ce = launch_pdl(blk_attn3_bwd_kernel, dim3((n * Bi * Hi + 7) / 8), dim3(256), 0, s,
-                         w.f.qkv, W->v_a, w.d_att, w.d_qkv, G->v_a, l0, n, Bi, Di, Hi)) !=
+                         f_qkv, W->v_a, w.d_att, d_qkv, cs, G->v_a, l0, n, Bi, Di, Hi)) !=
         cudaSuccess)
       return check_cuda(ce, "block_grid_bwd launch");
     // q | k | v projections
-    if ((st = gemm_rm(hb, false, false, 3 * Bi, Di, 3 * Di, w.d_qkv, 3 * Di, 9 * BD, Wqkv, Di,
+    if ((st = gemm_rm(hb, false, false, 3 * Bi, Di, 3 * Di, d_qkv, 3 * Di, 9 * cs, Wqkv, Di,
                       6 * DD, w.dT, Di, 3 * BD, n, 0.f)) != FLB_OK)
       return st;
     if (!saved && (st = fork(1)) != FLB_OK) return st;
@@ -1405,11 +1418,11 @@ int block_grid_bwd(const flb_block_weights* W, const void* x, const void* grids,
                       3 * BD, G->w_qkv + (int64_t)l0 * 3 * DD, Di, 6 * DD, n, 1.f)) != FLB_OK)
       return st;
     // sensory gate
-    if ((ce = launch_pdl(blk_gx_bwd_kernel, pair_grid, pair_block, 0, s, w.dT, w.f.zx, W->b_gate_x,
-                         g, xb, w.d_top, w.dG, dx, w.d_zx, w.d_lr, w.d_fp, G->b_gate_x, T, l0, Si,
-                         Bi, Di)) != cudaSuccess)
+    if ((ce = launch_pdl(blk_gx_bwd_kernel, pair_grid, pair_block, 0, s, w.dT, f_zx, W->b_gate_x,
+                         g, xb, w.d_top, w.dG, dx, d_zx, w.d_lr, w.d_fp, d_fp_h, cs,
+                         G->b_gate_x, T, l0, Si, Bi, Di)) != cudaSuccess)
       return check_cuda(ce, "block_grid_bwd launch");
-    if ((st = gemm_rm(hb, false, false, Bi, Di, Di, w.d_zx, Di, BD, Wgx, Di, 2 * DD, w.d_lr, Di, BD,
+    if ((st = gemm_rm(hb, false, false, Bi, Di, Di, d_zx, Di, cs, Wgx, Di, 2 * DD, w.d_lr, Di, BD,
                       n, 1.f)) != FLB_OK)
       return st;
     if (!saved && (st = fork(2)) != FLB_OK) return st;
@@ -1417,34 +1430,30 @@ int block_grid_bwd(const flb_block_weights* W, const void* x, const void* grids,
                       G->w_gate_x + (int64_t)l0 * DD, Di, 2 * DD, n, 1.f)) != FLB_OK)
       return st;
     // lateral gate
-    if ((ce = launch_pdl(blk_gl_bwd_kernel, pair_grid, pair_block, 0, s, w.d_lr, w.f.zl,
-                         W->b_gate_l, w.f.lat, w.d_lp, w.d_lp_h, w.d_zl, G->b_gate_l, l0, Bi,
+    if ((ce = launch_pdl(blk_gl_bwd_kernel, pair_grid, pair_block, 0, s, w.d_lr, f_zl,
+                         W->b_gate_l, f_lat, w.d_lp, d_lp_h, d_zl, cs, G->b_gate_l, l0, Bi,
                          Di)) != cudaSuccess)
       return check_cuda(ce, "block_grid_bwd launch");
-    if ((st = gemm_rm(hb, false, false, Bi, Di, Di, w.d_zl, Di, BD, Wgl, Di, 2 * DD, w.d_fp, Di, BD,
-                      n, 1.f)) != FLB_OK)
+    // d_fdbk_prior = bf16(d_zL G_L + its bf16 partial from the sensory-gate backward)
+    if ((st = gemm_rm(hb, false, false, Bi, Di, Di, d_zl, Di, cs, Wgl, Di, 2 * DD, d_fp_h, Di, cs,
+                      n, 1.f, CUDA_R_16BF)) != FLB_OK)
       return st;
     if (!saved && (st = fork(3)) != FLB_OK) return st;
     if (!saved && (st = gemm_rm(hs, true, false, Di, Di, Bi, w.d_zl, Di, BD, w.f.tok + 2 * D, 3 * Di, 3 * BD,
                       G->w_gate_l + (int64_t)l0 * DD, Di, 2 * DD, n, 1.f)) != FLB_OK)
       return st;
-    if ((ce = launch_pdl(blk_cast_kernel,
-                         dim3((unsigned)std::min<int64_t>((n * BD / 2 + 255) / 256, ew)),
-                         dim3(256), 0, s, w.d_fp, w.d_fp_h, (int64_t)(n * BD / 2))) !=
-        cudaSuccess)
-      return check_cuda(ce, "block_grid_bwd launch");
     // priors (with the intermediates kept, the lateral prior's input gradient runs on the side
     // stream beside the z_l / cast / feedback-prior chain; joined before the LayerNorm backward)
     if (saved) {
       if ((st = fork(4)) != FLB_OK) return st;
-      if ((st = gemm_rm(hs, false, false, Bi, Di, Di, w.d_lp_h, Di, BD, Wpl, Di, 2 * DD, w.dA, Di,
+      if ((st = gemm_rm(hs, false, false, Bi, Di, Di, d_lp_h, Di, cs, Wpl, Di, 2 * DD, w.dA, Di,
                         BD, n, 0.f)) != FLB_OK)
         return st;
     } else if ((st = gemm_rm(hb, false, false, Bi, Di, Di, w.d_lp_h, Di, BD, Wpl, Di, 2 * DD, w.dA,
                              Di, BD, n, 0.f)) != FLB_OK) {
       return st;
     }
-    if ((st = gemm_rm(hb, false, false, Bi, Di, Di, w.d_fp_h, Di, BD, Wpf, Di, 2 * DD,
+    if ((st = gemm_rm(hb, false, false, Bi, Di, Di, d_fp_h, Di, cs, Wpf, Di, 2 * DD,
                       w.dA + n * BD, Di, BD, n, 0.f)) != FLB_OK)
       return st;
     if (!saved && (st = fork(4)) != FLB_OK) return st;
@@ -1460,18 +1469,8 @@ int block_grid_bwd(const flb_block_weights* W, const void* x, const void* grids,
                          G->ln_lat_w, G->ln_lat_b, G->ln_fdbk_w, G->ln_fdbk_b, T, l0, n, Li, Si,
                          Bi, Di, eps)) != cudaSuccess)
       return check_cuda(ce, "block_grid_bwd launch");
-    if (saved) {  // the gradients that meet the weights, for the GEMMs after the loop
-      const CopySegs cs = make_segs({{PL_DO, {w.d_o, 3 * BD}},
-                                     {PL_DQKV, {w.d_qkv, 9 * BD}},
-                                     {PL_DZX, {w.d_zx, BD}},
-                                     {PL_DZL, {w.d_zl, BD}},
-                                     {PL_DLP, {w.d_lp_h, BD}},
-                                     {PL_DFP, {w.d_fp_h, BD}}});
-      if ((st = launch_cells_copy(planes, cs, 0, T, l0, n, Li, Si, Bi, Di, s)) != FLB_OK) return st;
-    } else if ((st = join()) != FLB_OK) {
-      return st;
-    }
-    launches += 10;  // own kernels (4 recompute + 6 backward)
+    if (!saved && (st = join()) != FLB_OK) return st;
+    launches += saved ? 5 : 9;  // own kernels: 5 backward (+ 4 of the recomputed forward)
   }
   if (saved) {
     // Weight gradients: per layer, one GEMM over all of its cells (K = S x rows), from the
