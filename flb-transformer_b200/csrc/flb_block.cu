@@ -1147,11 +1147,14 @@ __global__ void blk_gl_bwd_kernel(const float* __restrict__ d_lr, const bf16* __
   }
 }
 
-// LayerNorm backward: one block per (which, cell). Phase 1, a warp per batch row: the row's
-// mean, 1/std and the two reductions of the input gradient (c1 = mean of g*gamma, c2 = mean of
-// g*gamma*xhat). Phase 2, threads over feature pairs looping over the rows (coalesced, no
-// atomics): dgamma / dbeta of the cell's layer, and the input gradient routed to the producer's
-// port gradient (left -> port 1 of (l, t-1), bottom-left -> port 2 of (l+1, t-1)).
+// LayerNorm backward: block per (32 feature pairs, which, cell), threads (pair, batch row).
+// Phase 1, a warp per batch row over the whole row: the row's mean, 1/std and the two
+// reductions of the input gradient (c1 = mean of g*gamma, c2 = mean of g*gamma*xhat); every
+// block of a cell recomputes them for its rows (~77 KB of L2 reads at d_model 768, batch 16),
+// which spreads the kernel over (D/64) x 2 x cells blocks instead of one per cell. Phase 2, a
+// thread per (feature pair, row), coalesced, no atomics: the input gradient routed to the
+// producer's port gradient (left -> port 1 of (l, t-1), bottom-left -> port 2 of (l+1, t-1)),
+// and dgamma / dbeta of the cell's layer summed over the rows in a fixed order.
 __global__ void blk_ln_bwd_kernel(const bf16* __restrict__ grids, int64_t port_stride,
                                   const float* __restrict__ dA, const float* __restrict__ lw0,
                                   const float* __restrict__ lw1, float* __restrict__ dG,
@@ -1161,9 +1164,10 @@ __global__ void blk_ln_bwd_kernel(const bf16* __restrict__ grids, int64_t port_s
                                   int B, int D, float eps) {
   pdl_wait();
   extern __shared__ float stat[];  // [B][4]: mean, rstd, c1, c2
-  const int which = blockIdx.x / n, i = blockIdx.x % n;
+  __shared__ float2 part_g[16][32], part_b[16][32];
+  const int which = blockIdx.y / n, i = blockIdx.y % n;
   const int l = l0 + 2 * i, t = (T - l) / 2;
-  const int warps = blockDim.x >> 5, warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int warps = blockDim.y, warp = threadIdx.y, lane = threadIdx.x;
   const float* gamma = (which ? lw1 : lw0) + (int64_t)l * D;
   const bool has_src = t > 0 && (which == 0 || l + 1 < L);
   const int64_t src_cell = which == 0 ? cell_row(l, t - 1, S) : cell_row(l + 1, t - 1, S);
@@ -1222,10 +1226,11 @@ __global__ void blk_ln_bwd_kernel(const bf16* __restrict__ grids, int64_t port_s
   __syncthreads();
   float* dw = (which ? dw1 : dw0) + (int64_t)l * D;
   float* db = (which ? db1 : db0) + (int64_t)l * D;
-  for (int jp = threadIdx.x; jp < D / 2; jp += blockDim.x) {
+  const int jp = blockIdx.x * 32 + lane;
+  float2 dgam = make_float2(0.f, 0.f), dbet = make_float2(0.f, 0.f);
+  if (jp < D / 2) {
     const float2 gm = reinterpret_cast<const float2*>(gamma)[jp];
-    float2 dgam = make_float2(0.f, 0.f), dbet = make_float2(0.f, 0.f);
-    for (int b = 0; b < B; ++b) {
+    for (int b = warp; b < B; b += warps) {
       const float mean = stat[4 * b], rstd = stat[4 * b + 1], c1 = stat[4 * b + 2],
                   c2 = stat[4 * b + 3];
       const float2 xx = has_src ? __bfloat1622float2(
@@ -1243,6 +1248,17 @@ __global__ void blk_ln_bwd_kernel(const bf16* __restrict__ grids, int64_t port_s
         *o = make_float2(v.x + rstd * (g.x * gm.x - c1 - xh0 * c2),
                          v.y + rstd * (g.y * gm.y - c1 - xh1 * c2));
       }
+    }
+  }
+  part_g[warp][lane] = dgam;
+  part_b[warp][lane] = dbet;
+  __syncthreads();
+  if (jp < D / 2 && warp == 0) {
+    for (int y = 1; y < warps; ++y) {
+      dgam.x += part_g[y][lane].x;
+      dgam.y += part_g[y][lane].y;
+      dbet.x += part_b[y][lane].x;
+      dbet.y += part_b[y][lane].y;
     }
     float2* pw = reinterpret_cast<float2*>(dw) + jp;
     float2* pb = reinterpret_cast<float2*>(db) + jp;
@@ -1464,7 +1480,8 @@ int block_grid_bwd(const flb_block_weights* W, const void* x, const void* grids,
                       G->w_prior_fdbk + (int64_t)l0 * DD, Di, 2 * DD, n, 1.f)) != FLB_OK)
       return st;
     if (saved && (st = join()) != FLB_OK) return st;
-    if ((ce = launch_pdl(blk_ln_bwd_kernel, dim3(2 * n), dim3(512), 4 * B * sizeof(float), s, g,
+    if ((ce = launch_pdl(blk_ln_bwd_kernel, dim3((unsigned)((D / 2 + 31) / 32), (unsigned)(2 * n)),
+                         pair_block, 4 * B * sizeof(float), s, g,
                          port_stride, w.dA, W->ln_lat_w, W->ln_fdbk_w, w.dG, per_port,
                          G->ln_lat_w, G->ln_lat_b, G->ln_fdbk_w, G->ln_fdbk_b, T, l0, n, Li, Si,
                          Bi, Di, eps)) != cudaSuccess)
