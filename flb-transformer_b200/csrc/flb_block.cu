@@ -24,7 +24,6 @@
 #include <cuda_bf16.h>
 
 #include <algorithm>
-#include <initializer_list>
 #include <utility>
 #include <mutex>
 
@@ -83,20 +82,12 @@ __device__ __forceinline__ int64_t cell_row(int l, int t, int S) { return (int64
 //    One warp per row, the row held in registers as 16-byte chunks (D <= 1024).
 constexpr int kMaxChunks = 4;  // per lane: 4 x 8 bf16 -> D <= 32 * 32 = 1024
 
-__global__ void blk_ln_kernel(const bf16* __restrict__ g_left, const bf16* __restrict__ g_diag,
-                              const float* __restrict__ lw0, const float* __restrict__ lb0,
-                              const float* __restrict__ lw1, const float* __restrict__ lb1,
-                              bf16* __restrict__ out, int T, int l0, int n, int L, int S, int B,
-                              int D, float eps) {
-  pdl_wait();
-  const int warps = blockDim.x >> 5, lane = threadIdx.x & 31;
-  const int row = blockIdx.x * warps + (threadIdx.x >> 5);
-  if (row >= 2 * n * B) return;
-  const int which = row / (n * B), i = (row / B) % n, b = row % B;
-  const int l = l0 + 2 * i, t = (T - l) / 2;
-  const bf16* src = nullptr;
-  if (which == 0 && t > 0) src = g_left + (cell_row(l, t - 1, S) * B + b) * D;
-  if (which == 1 && t > 0 && l + 1 < L) src = g_diag + (cell_row(l + 1, t - 1, S) * B + b) * D;
+// LayerNorm of one row by one warp (fp32 statistics over the bf16 values; src null = a zero
+// row, which normalises to beta), the row held in registers as 16-byte chunks (D <= 1024).
+__device__ __forceinline__ void ln_warp_row(const bf16* __restrict__ src,
+                                            const float* __restrict__ gamma,
+                                            const float* __restrict__ beta,
+                                            bf16* __restrict__ out, int lane, int D, float eps) {
   const int nch = D / 8;
   float v[kMaxChunks][8];
   float s = 0.f, ss = 0.f;
@@ -119,9 +110,9 @@ __global__ void blk_ln_kernel(const bf16* __restrict__ g_left, const bf16* __res
   ss = warp_sum(ss);
   const float mean = s / D;
   const float rstd = rsqrtf(fmaxf(ss / D - mean * mean, 0.f) + eps);
-  const float4* w4 = reinterpret_cast<const float4*>((which ? lw1 : lw0) + (int64_t)l * D);
-  const float4* b4 = reinterpret_cast<const float4*>((which ? lb1 : lb0) + (int64_t)l * D);
-  uint4* dst = reinterpret_cast<uint4*>(out + (int64_t)row * D);
+  const float4* w4 = reinterpret_cast<const float4*>(gamma);
+  const float4* b4 = reinterpret_cast<const float4*>(beta);
+  uint4* dst = reinterpret_cast<uint4*>(out);
 #pragma unroll
   for (int k = 0; k < kMaxChunks; ++k) {
     const int c = lane + 32 * k;
@@ -140,6 +131,48 @@ __global__ void blk_ln_kernel(const bf16* __restrict__ g_left, const bf16* __res
   }
 }
 
+__global__ void blk_ln_kernel(const bf16* __restrict__ g_left, const bf16* __restrict__ g_diag,
+                              const float* __restrict__ lw0, const float* __restrict__ lb0,
+                              const float* __restrict__ lw1, const float* __restrict__ lb1,
+                              bf16* __restrict__ out, int T, int l0, int n, int L, int S, int B,
+                              int D, float eps) {
+  pdl_wait();
+  const int warps = blockDim.x >> 5, lane = threadIdx.x & 31;
+  const int row = blockIdx.x * warps + (threadIdx.x >> 5);
+  if (row >= 2 * n * B) return;
+  const int which = row / (n * B), i = (row / B) % n, b = row % B;
+  const int l = l0 + 2 * i, t = (T - l) / 2;
+  const bf16* src = nullptr;
+  if (which == 0 && t > 0) src = g_left + (cell_row(l, t - 1, S) * B + b) * D;
+  if (which == 1 && t > 0 && l + 1 < L) src = g_diag + (cell_row(l + 1, t - 1, S) * B + b) * D;
+  ln_warp_row(src, (which ? lw1 : lw0) + (int64_t)l * D, (which ? lb1 : lb0) + (int64_t)l * D,
+              out + (int64_t)row * D, lane, D, eps);
+}
+
+// The training forward's LayerNorm planes (PL_LN_LEFT, PL_LN_DIAG: [which][cell][B][D], rows in
+// that order), all cells at once after the tick loop, from the port grids the forward wrote: the
+// same LayerNorms of the same bf16 values that the output kernels put in the ring for the
+// consumer ticks. One warp per row.
+__global__ void blk_ln_planes_kernel(const bf16* __restrict__ g_left, const bf16* __restrict__ g_diag,
+                                     const float* __restrict__ lw0, const float* __restrict__ lb0,
+                                     const float* __restrict__ lw1, const float* __restrict__ lb1,
+                                     bf16* __restrict__ out, int L, int S, int B, int D, float eps) {
+  pdl_wait();
+  const int warps = blockDim.x >> 5, lane = threadIdx.x & 31;
+  const int64_t row = (int64_t)blockIdx.x * warps + (threadIdx.x >> 5);
+  const int64_t per = (int64_t)L * S * B;
+  if (row >= 2 * per) return;
+  const int which = (int)(row / per);
+  const int64_t cell = (row - which * per) / B;
+  const int b = (int)(row % B);
+  const int l = (int)(cell / S), t = (int)(cell % S);
+  const bf16* src = nullptr;
+  if (which == 0 && t > 0) src = g_left + (cell_row(l, t - 1, S) * B + b) * D;
+  if (which == 1 && t > 0 && l + 1 < L) src = g_diag + (cell_row(l + 1, t - 1, S) * B + b) * D;
+  ln_warp_row(src, (which ? lw1 : lw0) + (int64_t)l * D, (which ? lb1 : lb0) + (int64_t)l * D,
+              out + row * D, lane, D, eps);
+}
+
 // the top neighbour of cell (l, t), batch row b: port 0 of row l-1, or x at position t for l = 0
 __device__ __forceinline__ const bf16* top_row(const bf16* g0, const bf16* x, int l, int t, int b,
                                                int S, int B, int D) {
@@ -152,21 +185,21 @@ __device__ __forceinline__ const bf16* top_row(const bf16* g0, const bf16* x, in
 __global__ void blk_gate_kernel(const bf16* __restrict__ z, const float* __restrict__ bias,
                                 const bf16* __restrict__ m, const bf16* __restrict__ g0,
                                 const bf16* __restrict__ x, int mode, bf16* __restrict__ dst,
-                                int T, int l0, int S, int B, int D) {
+                                int64_t cs, int T, int l0, int S, int B, int D) {
   pdl_wait();
   const int j = blockIdx.x * blockDim.x + threadIdx.x;
   if (j >= D / 2) return;
   const int rb = blockIdx.y;  // i * B + b
   const int i = rb / B, b = rb - i * B;
   const int l = l0 + 2 * i, t = (T - l) / 2;
-  const float2 zz = __bfloat1622float2(reinterpret_cast<const __nv_bfloat162*>(z + (int64_t)rb * D)[j]);
-  const bf16* mrow = mode == 0 ? m + (int64_t)rb * D : top_row(g0, x, l, t, b, S, B, D);
+  const int64_t cr = (int64_t)i * cs + (int64_t)b * D;  // row of a one-unit cell array
+  const float2 zz = __bfloat1622float2(reinterpret_cast<const __nv_bfloat162*>(z + cr)[j]);
+  const bf16* mrow = mode == 0 ? m + cr : top_row(g0, x, l, t, b, S, B, D);
   const float2 mm = __bfloat1622float2(reinterpret_cast<const __nv_bfloat162*>(mrow)[j]);
   const float2 bl = reinterpret_cast<const float2*>(bias + (int64_t)l * D)[j];
   const float s0 = 1.f / (1.f + __expf(-(zz.x + bl.x)));
   const float s1 = 1.f / (1.f + __expf(-(zz.y + bl.y)));
-  reinterpret_cast<__nv_bfloat162*>(dst + (int64_t)rb * 3 * D)[j] =
-      __floats2bfloat162_rn(mm.x * s0, mm.y * s1);
+  reinterpret_cast<__nv_bfloat162*>(dst + 3 * cr)[j] = __floats2bfloat162_rn(mm.x * s0, mm.y * s1);
 }
 
 // 6. additive attention over the 3 tokens, one warp per (cell, batch row, head). qkv rows are
@@ -178,14 +211,15 @@ __device__ __forceinline__ float ld_bf16_cg(const bf16* p) {
 }
 
 __device__ __forceinline__ void attn3_task(const bf16* __restrict__ qkv, const float* __restrict__ v_a,
-                                           bf16* __restrict__ att, int l0, int B, int D, int H,
-                                           int task, int lane) {
+                                           bf16* __restrict__ att, int64_t cs, int l0, int B,
+                                           int D, int H, int task, int lane) {
   const int h = task % H;
   const int64_t rb = task / H;  // i * B + b
   const int i = (int)(rb / B);
   const int dh = D / H;
   const float* w = v_a + ((int64_t)(l0 + 2 * i) * H + h) * dh;
-  const bf16* base = qkv + rb * 3 * (3 * D) + h * dh;  // token r row: base + r * 3D
+  const int64_t cr = (int64_t)i * cs + (rb - (int64_t)i * B) * D;  // one-unit row of (cell, b)
+  const bf16* base = qkv + 9 * cr + h * dh;  // token r row: base + r * 3D
   float s[3][3], vv[4][3];
 #pragma unroll
   for (int a = 0; a < 3; ++a)
@@ -227,7 +261,7 @@ __device__ __forceinline__ void attn3_task(const bf16* __restrict__ qkv, const f
 #pragma unroll
     for (int c = 0; c < 3; ++c) p[a][c] /= l;
   }
-  bf16* out = att + rb * 3 * D + h * dh;
+  bf16* out = att + 3 * cr + h * dh;
 #pragma unroll
   for (int kk = 0; kk < 4; ++kk) {
     const int d = lane + 32 * kk;
@@ -240,12 +274,13 @@ __device__ __forceinline__ void attn3_task(const bf16* __restrict__ qkv, const f
 }
 
 __global__ void blk_attn3_kernel(const bf16* __restrict__ qkv, const float* __restrict__ v_a,
-                                 bf16* __restrict__ att, int l0, int n, int B, int D, int H) {
+                                 bf16* __restrict__ att, int64_t cs, int l0, int n, int B, int D,
+                                 int H) {
   pdl_wait();
   const int warps = blockDim.x >> 5, lane = threadIdx.x & 31;
   const int task = blockIdx.x * warps + (threadIdx.x >> 5);
   if (task >= n * B * H) return;
-  attn3_task(qkv, v_a, att, l0, B, D, H, task, lane);
+  attn3_task(qkv, v_a, att, cs, l0, B, D, H, task, lane);
 }
 
 // 8. residuals and the auxiliary loss into the four port grids, with the next ticks'
@@ -278,7 +313,7 @@ __device__ __forceinline__ void ln_chunk_store(const float (&v)[8], float mean, 
 }
 
 __global__ void blk_out_ln_kernel(const bf16* __restrict__ o, const bf16* __restrict__ lat_prior,
-                                  const bf16* __restrict__ tok, const bf16* __restrict__ x,
+                                  const bf16* __restrict__ tok, int64_t cs, const bf16* __restrict__ x,
                                   bf16* __restrict__ grids, int64_t port_stride,
                                   bf16* __restrict__ lnr, const float* __restrict__ lw0,
                                   const float* __restrict__ lb0, const float* __restrict__ lw1,
@@ -324,8 +359,9 @@ __global__ void blk_out_ln_kernel(const bf16* __restrict__ o, const bf16* __rest
     ld8(o + (r3 + 1) * D, o1);
     ld8(o + (r3 + 2) * D, o2);
     ld8(top_row(grids, x, l, t, b, S, B, D), tp);
-    ld8(lat_prior + (int64_t)row * D, lp);
-    ld8(tok + (r3 + 2) * D, fp);
+    const int64_t cr = (int64_t)i * cs + (int64_t)b * D;  // row of a one-unit cell array
+    ld8(lat_prior + cr, lp);
+    ld8(tok + 3 * cr + 2 * D, fp);
     uint32_t px[4], pl[4], pf[4], pa[4];
 #pragma unroll
     for (int e = 0; e < 4; ++e) {
@@ -402,10 +438,12 @@ __global__ void blk_ln_init_kernel(bf16* __restrict__ lnr, const float* __restri
 
 // Planes of a training step's per-cell tensors, kept in one buffer (flb_block_grid_saved_bytes):
 // plane p holds, for every grid cell (l*S + t) in order, plane_units(p) units of B x D bf16. The forward
-// fills planes 0-7 with its tick intermediates [ln_left | ln_diag | lat_prior | tokens x' lat'
-// fdbk_prior | z_l | z_x | q|k|v | att], which the backward reads in place of recomputing its
-// ticks' forward stages; the backward's kernels and GEMMs write planes 8-13, the gradients that
-// meet the weights [d_o | d_q|k|v | d_z_x | d_z_l | d_lat_prior | d_fdbk_prior], directly. A tick's
+// fills planes 0-7 with its intermediates [ln_left | ln_diag | lat_prior | tokens x' lat'
+// fdbk_prior | z_l | z_x | q|k|v | att] (its GEMMs and kernels write planes 2-7 in place, one
+// launch after the tick loop writes the LayerNorm planes 0-1 from the port grids), which the
+// backward reads in place of recomputing its ticks' forward stages; the backward's kernels and
+// GEMMs write planes 8-13, the gradients that meet the weights [d_o | d_q|k|v | d_z_x | d_z_l |
+// d_lat_prior | d_fdbk_prior], directly. Nothing is copied between planes and tick buffers. A tick's
 // cells lie 2S - 1 cells apart in a plane (one stride per strided-batched GEMM), and a layer's
 // cells are consecutive, so each weight gradient is one GEMM per layer over all of its cells at
 // the end.
@@ -420,62 +458,6 @@ __host__ __device__ inline int64_t plane_offset(int p, int64_t cells, int64_t BD
   int64_t u = 0;
   for (int q = 0; q < p; ++q) u += plane_units(q);
   return u * cells * BD;
-}
-
-// Copy of some planes' cells of one tick to or from the tick buffers: segment k is plane
-// `plane[k]`, whose cell i lies in the tick buffers at tick[k] + i * cell_stride[k] (U units
-// contiguous). dir 0: tick buffers -> planes, 1: planes -> tick buffers. Grid: x over 16-byte
-// chunks of the segments' units, y over the tick's cells.
-constexpr int kMaxSegs = 8;
-struct CopySegs {
-  int count, total_units;
-  int plane[kMaxSegs], unit0[kMaxSegs];
-  bf16* tick[kMaxSegs];
-  int64_t cell_stride[kMaxSegs];
-};
-
-__global__ void blk_cells_copy_kernel(bf16* __restrict__ planes, CopySegs cs, int dir, int T,
-                                      int l0, int S, int64_t cells, int B, int D) {
-  pdl_wait();
-  const int i = blockIdx.y;
-  const int l = l0 + 2 * i, t = (T - l) / 2;
-  const int64_t BD = (int64_t)B * D;
-  const int64_t e0 = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) * 8;
-  if (e0 >= cs.total_units * BD) return;
-  const int unit = (int)(e0 / BD);  // B * D is a multiple of 8: a chunk lies in one unit
-  int k = 0;
-  while (k + 1 < cs.count && unit >= cs.unit0[k + 1]) ++k;
-  const int p = cs.plane[k];
-  const int64_t in = e0 - (int64_t)cs.unit0[k] * BD;  // within the segment's units of a cell
-  uint4* pl = reinterpret_cast<uint4*>(planes + plane_offset(p, cells, BD) +
-                                       cell_row(l, t, S) * plane_units(p) * BD + in);
-  uint4* tb = reinterpret_cast<uint4*>(cs.tick[k] + i * cs.cell_stride[k] + in);
-  if (dir == 0) *pl = *tb;
-  else *tb = *pl;
-}
-
-CopySegs make_segs(std::initializer_list<std::pair<int, std::pair<bf16*, int64_t>>> list) {
-  CopySegs cs{};
-  int u = 0;
-  for (const auto& e : list) {
-    cs.plane[cs.count] = e.first;
-    cs.unit0[cs.count] = u;
-    cs.tick[cs.count] = e.second.first;
-    cs.cell_stride[cs.count] = e.second.second;
-    u += plane_units(e.first);
-    ++cs.count;
-  }
-  cs.total_units = u;
-  return cs;
-}
-
-int launch_cells_copy(bf16* planes, const CopySegs& cs, int dir, int T, int l0, int n, int L, int S,
-                      int B, int D, cudaStream_t s) {
-  const int64_t chunks = (int64_t)cs.total_units * B * D / 8;
-  const dim3 grid((unsigned)((chunks + 255) / 256), (unsigned)n);
-  return check_cuda(launch_pdl(blk_cells_copy_kernel, grid, dim3(256), 0, s, planes, cs, dir, T,
-                               l0, S, (int64_t)L * S, B, D),
-                    "block_grid intermediates copy");
 }
 
 constexpr size_t kBlkBlasWs = 32u << 20;
@@ -677,8 +659,12 @@ int side_stream(SideStream** out) {
 // Forward buffers of one tick (bf16): LayerNorm outputs [2][n][B][D], lat_prior [n][B][D],
 // tokens [n][B][3][D] (x', lat', fdbk_prior), gate pre-activations [n][B][D] (the forward reuses
 // one buffer for both), q|k|v [n][3B][3D], attention output [n][3B][D].
+// Cell i of the tick at base + i * units * cs: cs = B x D in the work buffers, or (2S - 1) x B x D
+// when the pointers are the tick's first cell in the kept planes (the training forward writes
+// its intermediates there in place). ln is always a work buffer.
 struct TickBufs {
   bf16 *ln, *lat, *tok, *zl, *zx, *qkv, *att;
+  int64_t cs;
 };
 
 // stages 1-6 of a tick (everything up to the attention output)
@@ -723,53 +709,54 @@ int tick_forward(cublasHandle_t hb, const Side& side, const flb_block_weights* W
   const bf16* Wqkv = reinterpret_cast<const bf16*>(W->w_qkv) + (int64_t)l0 * 3 * DD;
   // priors: lat_prior -> b.lat (side stream: first needed by the lateral gate kernel);
   // fdbk_prior -> token slot 2 (row pitch 3D)
+  const int64_t cs = b.cs;
   if ((st = gemm_rm(side.h, false, true, B, D, D, ln_left, D, ln_stride, Wpl, D, 2 * DD, b.lat, D,
-                    BD, n, 0.f, CUDA_R_16BF)) != FLB_OK)
+                    cs, n, 0.f, CUDA_R_16BF)) != FLB_OK)
     return st;
   e = cudaEventRecord(side.ss->fwd_join, side.ss->s);
   if (e != cudaSuccess) return check_cuda(e, "block_grid tick join");
   if (w_glpf) {
     // fdbk_prior on the side stream (first needed by the q|k|v GEMM); z_l from the folded weights
     if ((st = gemm_rm(side.h, false, true, B, D, D, ln_diag, D, ln_stride, Wpf, D, 2 * DD,
-                      b.tok + 2 * D, 3 * D, 3 * BD, n, 0.f, CUDA_R_16BF)) != FLB_OK)
+                      b.tok + 2 * D, 3 * D, 3 * cs, n, 0.f, CUDA_R_16BF)) != FLB_OK)
       return st;
     e = cudaEventRecord(side.ss->fwd_join2, side.ss->s);
     if (e != cudaSuccess) return check_cuda(e, "block_grid tick join");
     if ((st = gemm_rm(hb, false, true, B, D, D, ln_diag, D, ln_stride, w_glpf + (int64_t)l0 * DD, D,
-                      2 * DD, b.zl, D, BD, n, 0.f, CUDA_R_16BF)) != FLB_OK)
+                      2 * DD, b.zl, D, cs, n, 0.f, CUDA_R_16BF)) != FLB_OK)
       return st;
   } else {
     if ((st = gemm_rm(hb, false, true, B, D, D, ln_diag, D, ln_stride, Wpf, D, 2 * DD, b.tok + 2 * D,
-                      3 * D, 3 * BD, n, 0.f, CUDA_R_16BF)) != FLB_OK)
+                      3 * D, 3 * cs, n, 0.f, CUDA_R_16BF)) != FLB_OK)
       return st;
     // lateral gate
-    if ((st = gemm_rm(hb, false, true, B, D, D, b.tok + 2 * D, 3 * D, 3 * BD, Wgl, D, 2 * DD, b.zl,
-                      D, BD, n, 0.f, CUDA_R_16BF)) != FLB_OK)
+    if ((st = gemm_rm(hb, false, true, B, D, D, b.tok + 2 * D, 3 * D, 3 * cs, Wgl, D, 2 * DD, b.zl,
+                      D, cs, n, 0.f, CUDA_R_16BF)) != FLB_OK)
       return st;
   }
   e = cudaStreamWaitEvent(s, side.ss->fwd_join, 0);
   if (e != cudaSuccess) return check_cuda(e, "block_grid tick join");
   const dim3 ew_grid((unsigned)((D / 2 + 127) / 128), (unsigned)(n * B));
   e = launch_pdl(blk_gate_kernel, ew_grid, dim3(128), 0, s, b.zl, W->b_gate_l, b.lat, g, xb, 0,
-                 b.tok + D, T, l0, S, B, D);
+                 b.tok + D, cs, T, l0, S, B, D);
   if (e != cudaSuccess) return check_cuda(e, "block_grid gate launch");
   // sensory gate
-  if ((st = gemm_rm(hb, false, true, B, D, D, b.tok + D, 3 * D, 3 * BD, Wgx, D, 2 * DD, b.zx, D, BD,
+  if ((st = gemm_rm(hb, false, true, B, D, D, b.tok + D, 3 * D, 3 * cs, Wgx, D, 2 * DD, b.zx, D, cs,
                     n, 0.f, CUDA_R_16BF)) != FLB_OK)
     return st;
   e = launch_pdl(blk_gate_kernel, ew_grid, dim3(128), 0, s, b.zx, W->b_gate_x,
-                 static_cast<const bf16*>(nullptr), g, xb, 1, b.tok, T, l0, S, B, D);
+                 static_cast<const bf16*>(nullptr), g, xb, 1, b.tok, cs, T, l0, S, B, D);
   if (e != cudaSuccess) return check_cuda(e, "block_grid gate launch");
   if (w_glpf) {
     e = cudaStreamWaitEvent(s, side.ss->fwd_join2, 0);
     if (e != cudaSuccess) return check_cuda(e, "block_grid tick join");
   }
   // q | k | v of the 3 tokens: [n, 3B, D] x [3D, D]^T
-  if ((st = gemm_rm(hb, false, true, 3 * B, 3 * D, D, b.tok, D, 3 * BD, Wqkv, D, 6 * DD, b.qkv,
-                    3 * D, 9 * BD, n, 0.f, CUDA_R_16BF)) != FLB_OK)
+  if ((st = gemm_rm(hb, false, true, 3 * B, 3 * D, D, b.tok, D, 3 * cs, Wqkv, D, 6 * DD, b.qkv,
+                    3 * D, 9 * cs, n, 0.f, CUDA_R_16BF)) != FLB_OK)
     return st;
   e = launch_pdl(blk_attn3_kernel, dim3((n * B * H + 7) / 8), dim3(256), 0, s, b.qkv, W->v_a,
-                 b.att, l0, n, B, D, H);
+                 b.att, cs, l0, n, B, D, H);
   return check_cuda(e, "block_grid attention launch");
 }
 
@@ -800,7 +787,8 @@ int block_grid_fwd_ex(const flb_block_weights* W, const void* x, void* grids, in
   const long long DD = D * D, BD = B * D;
   const int Li = (int)L, Si = (int)S, Bi = (int)B, Di = (int)D, Hi = (int)H;
   const int ticks = (int)(L + 2 * S - 2);
-  const TickBufs tb{w.ln, w.lat, w.tok, w.z, w.zx, w.qkv, w.att};
+  const TickBufs work{w.ln, w.lat, w.tok, w.z, w.zx, w.qkv, w.att, BD};
+  bf16* planes = reinterpret_cast<bf16*>(saved);
   // inference: fold the lateral gate onto the feedback prior once per call, G_L P_fb per layer
   if ((st = gemm_rm(hb, false, false, Di, Di, Di, W->w_gate_l, Di, DD, W->w_prior_fdbk, Di, DD,
                     w.glpf, Di, DD, Li, 0.f, CUDA_R_16BF)) != FLB_OK)
@@ -817,35 +805,39 @@ int block_grid_fwd_ex(const flb_block_weights* W, const void* x, void* grids, in
     const Tick tk = tick_of(T, Li, Si);
     const int n = tk.n, l0 = tk.l0;
     if (n == 0) continue;
+    // training: the tick's intermediates go straight to their planes (cell i of the tick
+    // 2S - 1 cells after cell i - 1), where the backward reads them
+    TickBufs tb = work;
+    if (planes) {
+      const int64_t c0 = (int64_t)l0 * S + (T - l0) / 2;  // flat index of the tick's first cell
+      auto at = [&](int p) { return planes + plane_offset(p, L * S, BD) + c0 * plane_units(p) * BD; };
+      tb = TickBufs{w.ln, at(PL_LAT), at(PL_TOK), at(PL_ZL), at(PL_ZX), at(PL_QKV), at(PL_ATT),
+                    (2 * S - 1) * BD};
+    }
     if ((st = tick_forward(hb, side, W, xb, g, port_stride, tb, T, l0, n, Li, Si, Bi, Di, Hi, eps,
                            s, w.glpf, w.lnr)) != FLB_OK)
       return st;
     const bf16* Wo = reinterpret_cast<const bf16*>(W->w_o) + (int64_t)l0 * DD;
-    if ((st = gemm_rm(hb, false, true, 3 * Bi, Di, Di, w.att, Di, 3 * BD, Wo, Di, 2 * DD, w.o, Di,
-                      3 * BD, n, 0.f, CUDA_R_16BF)) != FLB_OK)
+    if ((st = gemm_rm(hb, false, true, 3 * Bi, Di, Di, tb.att, Di, 3 * tb.cs, Wo, Di, 2 * DD, w.o,
+                      Di, 3 * BD, n, 0.f, CUDA_R_16BF)) != FLB_OK)
       return st;
     // residuals, aux and the next ticks' LayerNorms: a warp per (cell, batch row)
     const int out_threads = std::max(32, (Di / 8 + 31) / 32 * 32);
     cudaError_t e = launch_pdl(blk_out_ln_kernel, dim3((unsigned)(n * Bi)), dim3(out_threads), 0,
-                               s, w.o, w.lat, w.tok, xb, g, port_stride, w.lnr, W->ln_lat_w,
+                               s, w.o, tb.lat, tb.tok, tb.cs, xb, g, port_stride, w.lnr, W->ln_lat_w,
                                W->ln_lat_b, W->ln_fdbk_w, W->ln_fdbk_b, eps, T, l0, n, Li, Si, Bi, Di);
     if (e != cudaSuccess) return check_cuda(e, "block_grid output launch");
-    launches += 5;  // own kernels (the GEMMs are cuBLAS's)
-    if (saved) {  // the tick's intermediates, for the backward
-      const long long LBD = (long long)L * BD;
-      bf16* ln_left = w.lnr + (long long)(T % 3) * 2 * LBD + (long long)l0 * BD;
-      const CopySegs cs = make_segs({{PL_LN_LEFT, {ln_left, 2 * BD}},
-                                     {PL_LN_DIAG, {ln_left + LBD, 2 * BD}},
-                                     {PL_LAT, {w.lat, BD}},
-                                     {PL_TOK, {w.tok, 3 * BD}},
-                                     {PL_ZL, {w.z, BD}},
-                                     {PL_ZX, {w.zx, BD}},
-                                     {PL_QKV, {w.qkv, 9 * BD}},
-                                     {PL_ATT, {w.att, 3 * BD}}});
-      if ((st = launch_cells_copy(reinterpret_cast<bf16*>(saved), cs, 0, T, l0, n, Li, Si, Bi, Di, s)) != FLB_OK)
-        return st;
-      ++launches;
-    }
+    launches += 4;  // own kernels: two gates, attention, output (the GEMMs are cuBLAS's)
+  }
+  if (planes) {
+    // the LayerNorm planes of every cell, from the port grids the ticks wrote
+    const int64_t rows = 2 * L * S * B;
+    cudaError_t e = launch_pdl(blk_ln_planes_kernel, dim3((unsigned)((rows + 7) / 8)), dim3(256), 0,
+                               s, g + port_stride, g + 2 * port_stride, W->ln_lat_w, W->ln_lat_b,
+                               W->ln_fdbk_w, W->ln_fdbk_b, planes + plane_offset(PL_LN_LEFT, L * S, BD),
+                               Li, Si, Bi, Di, eps);
+    if (e != cudaSuccess) return check_cuda(e, "block_grid LayerNorm planes launch");
+    ++launches;
   }
   count_launches(launches);
   return check_cuda(cudaGetLastError(), "flb block grid launch");
@@ -1295,6 +1287,7 @@ size_t block_bwd_ws_layout(int64_t L, int64_t S, int64_t B, int64_t D, BlockBwdW
   t.f.zx = (bf16*)take(rowh);
   t.f.qkv = (bf16*)take(9 * rowh);
   t.f.att = (bf16*)take(3 * rowh);
+  t.f.cs = B * D;
   t.d_o = (bf16*)take(3 * rowh);
   t.d_att = (bf16*)take(3 * rowh);
   t.d_qkv = (bf16*)take(9 * rowh);

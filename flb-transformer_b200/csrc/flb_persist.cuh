@@ -560,7 +560,7 @@ flb_persist_fwd_kernel(const __grid_constant__ PsMaps maps, const PsArgs p) {
           // stage 4: the 3-token attention, one warp per (cell, batch row, head)
           const int tasks = tk.n * kPsB * p.H;
           for (int task = c * kPsCompute + warp; task < tasks; task += G * kPsCompute)
-            attn3_task(p.qkv, p.v_a, p.att, tk.l0, kPsB, p.D, p.H, task, lane);
+            attn3_task(p.qkv, p.v_a, p.att, (int64_t)kPsB * p.D, tk.l0, kPsB, p.D, p.H, task, lane);
         } else {
           // tile ranges of stages 1, 2, 3, (4), 5
           const int lo = st == 0 ? 0 : st == 1 ? 3 * nF : st == 2 ? 4 * nF : 7 * nF;
