@@ -369,7 +369,7 @@ def grid_row_bands(world, rank, device, steps=10, warmup=3):
             "cells_per_s": R * C / (ms * 1e-3)}
 
 
-def extra_grid(device, steps=3, warmup=1, with_cpu=True):
+def extra_grid(device, steps=20, warmup=3, with_cpu=True):
     try:
         from wavefront.grid_layer import wavefront_grid_layer, grid_inputs
     except ImportError:
@@ -439,8 +439,10 @@ def extra_engine(device, steps=2, warmup=1):
     tick.load_state_dict(fast.state_dict())
     x = torch.randn(B, C, H, device=device).bfloat16()
     res, fast_out = {}, None
-    for name, layers, n in (("persistent", fast, steps), ("per_diagonal", tick, 1),
-                            ("per_diagonal_graphed", tick, steps)):
+    # (the persistent path: milliseconds per step, so 3 warm-up and 10x the timed steps)
+    for name, layers, n, nw in (("persistent", fast, 10 * steps, max(3, warmup)),
+                                ("per_diagonal", tick, 1, warmup),
+                                ("per_diagonal_graphed", tick, steps, warmup)):
         eng = WavefrontEngine(cfg, layers).to(device)
         run = eng.graphed(x) if name == "per_diagonal_graphed" else eng
 
@@ -450,7 +452,7 @@ def extra_engine(device, steps=2, warmup=1):
             g = run(xx)
             (g[0].float().sum() + g[1][-1].float().sum()).backward()
             return g[0].detach(), xx.grad
-        for _ in range(warmup):
+        for _ in range(nw):
             step()
         res[name] = time_steps(step, n, 1) / n
         if name == "persistent":
