@@ -81,7 +81,7 @@ size_t block_grid_bwd_workspace_bytes(int64_t L, int64_t S, int64_t B, int64_t D
 int block_grid_bwd(const flb_block_weights* W, const void* x, const void* grids,
                    const void* const* dgrids, float* dx, const flb_block_grads* G, int64_t L,
                    int64_t S, int64_t B, int64_t D, int64_t H, float eps, void* ws,
-                   size_t ws_bytes, cudaStream_t s, const void* saved);
+                   size_t ws_bytes, cudaStream_t s, void* saved);
 size_t grid_workspace_bytes(int64_t R, int64_t C, int64_t B, int64_t H, int64_t G, int has_U);
 int grid_fwd(const void* x, int x_layout, const void* W_l, const void* W_t, const void* U,
              const float* bias, const void* top, void* h_out, int64_t R, int64_t C, int64_t B,
@@ -370,7 +370,7 @@ int flb_block_grid_bwd_saved(const flb_block_weights* weights, const void* x, co
                              const void* dgrid3, float* dx, const flb_block_grads* grads,
                              int64_t L, int64_t S, int64_t batch, int64_t D, int64_t heads,
                              float ln_eps, void* workspace, size_t workspace_bytes,
-                             const void* saved, size_t saved_bytes, void* stream) {
+                             void* saved, size_t saved_bytes, void* stream) {
   if (!saved || saved_bytes < block_grid_saved_bytes(L, S, batch, D))
     return fail(FLB_ERR_WORKSPACE, "block_grid_bwd_saved: saved buffer smaller than flb_block_grid_saved_bytes()");
   if ((uintptr_t)saved & 15u) return fail(FLB_ERR_ALIGN, "block_grid_bwd_saved: saved must be 16-byte aligned");

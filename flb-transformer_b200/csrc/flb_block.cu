@@ -1322,8 +1322,8 @@ size_t block_grid_bwd_workspace_bytes(int64_t L, int64_t S, int64_t B, int64_t D
 int block_grid_bwd(const flb_block_weights* W, const void* x, const void* grids,
                    const void* const* dgrids, float* dx, const flb_block_grads* G, int64_t L,
                    int64_t S, int64_t B, int64_t D, int64_t H, float eps, void* ws,
-                   size_t ws_bytes, cudaStream_t s, const void* saved) {
-  bf16* planes = const_cast<bf16*>(reinterpret_cast<const bf16*>(saved));  // null: recompute
+                   size_t ws_bytes, cudaStream_t s, void* saved) {
+  bf16* planes = reinterpret_cast<bf16*>(saved);  // null: recompute
   BlockBwdWs w;
   block_bwd_ws_layout(L, S, B, D, &w, ws);
   SideStream* side;

@@ -367,14 +367,16 @@ int flb_block_grid_bwd(const flb_block_weights* weights, const void* x, const vo
                        float ln_eps, void* workspace, size_t workspace_bytes, void* stream);
 
 /* flb_block_grid_bwd with the intermediates flb_block_grid_fwd_save kept (same `grids`, weights
- * and x as that forward): each tick restores its cells' intermediates with one copy instead of
- * recomputing the forward stages. */
+ * and x as that forward): each tick reads its cells' intermediates in `saved` in place instead of
+ * recomputing the forward stages, and writes the gradients that meet the weights into `saved`
+ * (its other planes), from which every weight gradient is formed after the tick loop; `saved`
+ * is therefore written. */
 int flb_block_grid_bwd_saved(const flb_block_weights* weights, const void* x, const void* grids,
                              const void* dgrid0, const void* dgrid1, const void* dgrid2,
                              const void* dgrid3, float* dx, const flb_block_grads* grads,
                              int64_t L, int64_t S, int64_t batch, int64_t D, int64_t heads,
                              float ln_eps, void* workspace, size_t workspace_bytes,
-                             const void* saved, size_t saved_bytes, void* stream);
+                             void* saved, size_t saved_bytes, void* stream);
 
 /* Failure-detection check of the grid kernels' bounded dependency waits (no reference
  * counterpart). Runs flb_grid_fwd with the flag of cell (drop_row, drop_col) never released and
