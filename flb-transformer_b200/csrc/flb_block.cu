@@ -1036,8 +1036,8 @@ __global__ void blk_gx_bwd_kernel(const float* __restrict__ dT, const bf16* __re
                                   float* __restrict__ dG0, float* __restrict__ dx,
                                   bf16* __restrict__ d_zx, float* __restrict__ d_lr,
                                   const float* __restrict__ d_fp, bf16* __restrict__ d_fp_h,
-                                  int64_t cs, float* __restrict__ db_gx, int T, int l0, int S,
-                                  int B, int D) {
+                                  int64_t cs, bf16* __restrict__ dcat, float* __restrict__ db_gx,
+                                  int T, int l0, int S, int B, int D) {
   pdl_wait();
   // block: 32 feature pairs (x) by up to 16 batch rows (y); the bias gradient is summed over
   // the rows in a fixed order (deterministic)
@@ -1073,11 +1073,13 @@ __global__ void blk_gx_bwd_kernel(const float* __restrict__ dT, const bf16* __re
       reinterpret_cast<float2*>(d_lr + rb * D)[j] =
           reinterpret_cast<const float2*>(dT + (rb * 3 + 1) * D)[j];
       // d_fdbk_prior so far (residual + aux, then the q|k|v token's share), in bf16: the
-      // operand of the G_L GEMM that adds d_zL G_L in place (no separate cast)
+      // operand of the G_L GEMM that adds d_zL G_L in place (no separate cast); with dcat also
+      // the first half of the feedback LayerNorm's input-gradient operand
       const float2 dtf = reinterpret_cast<const float2*>(dT + (rb * 3 + 2) * D)[j];
       const float2 o = reinterpret_cast<const float2*>(d_fp + rb * D)[j];
-      reinterpret_cast<__nv_bfloat162*>(d_fp_h + cr)[j] =
-          __floats2bfloat162_rn(o.x + dtf.x, o.y + dtf.y);
+      const __nv_bfloat162 fp2 = __floats2bfloat162_rn(o.x + dtf.x, o.y + dtf.y);
+      reinterpret_cast<__nv_bfloat162*>(d_fp_h + cr)[j] = fp2;
+      if (dcat) reinterpret_cast<__nv_bfloat162*>(dcat + rb * 2 * D)[j] = fp2;
     }
   }
   part[threadIdx.y][threadIdx.x] = acc;
@@ -1098,8 +1100,8 @@ __global__ void blk_gx_bwd_kernel(const float* __restrict__ dT, const bf16* __re
 __global__ void blk_gl_bwd_kernel(const float* __restrict__ d_lr, const bf16* __restrict__ zl,
                                   const float* __restrict__ b_gl, const bf16* __restrict__ lat,
                                   float* __restrict__ d_lp, bf16* __restrict__ d_lp_h,
-                                  bf16* __restrict__ d_zl, int64_t cs, float* __restrict__ db_gl,
-                                  int l0, int B, int D) {
+                                  bf16* __restrict__ d_zl, int64_t cs, bf16* __restrict__ dcat,
+                                  float* __restrict__ db_gl, int l0, int B, int D) {
   pdl_wait();
   __shared__ float2 part[16][32];  // as blk_gx_bwd_kernel: 32 pairs by up to 16 rows
   const int j = blockIdx.x * 32 + threadIdx.x;
@@ -1120,7 +1122,9 @@ __global__ void blk_gl_bwd_kernel(const float* __restrict__ d_lr, const bf16* __
       const float2 dlp = make_float2(o.x + dl.x * s0, o.y + dl.y * s1);
       reinterpret_cast<__nv_bfloat162*>(d_lp_h + cr)[j] = __floats2bfloat162_rn(dlp.x, dlp.y);
       const float dz0 = dl.x * lp.x * s0 * (1.f - s0), dz1 = dl.y * lp.y * s1 * (1.f - s1);
-      reinterpret_cast<__nv_bfloat162*>(d_zl + cr)[j] = __floats2bfloat162_rn(dz0, dz1);
+      const __nv_bfloat162 dz2 = __floats2bfloat162_rn(dz0, dz1);
+      reinterpret_cast<__nv_bfloat162*>(d_zl + cr)[j] = dz2;
+      if (dcat) reinterpret_cast<__nv_bfloat162*>(dcat + rb * 2 * D + D)[j] = dz2;
       acc.x += dz0;
       acc.y += dz1;
     }
@@ -1263,6 +1267,9 @@ __global__ void blk_ln_bwd_kernel(const bf16* __restrict__ grids, int64_t port_s
 struct BlockBwdWs {
   TickBufs f;
   bf16 *d_o, *d_att, *d_qkv, *d_zx, *d_zl, *d_lp_h, *d_fp_h;
+  // with the intermediates kept: [d_fdbk_prior partial | d_z_l] rows of a tick (pitch 2D), and
+  // per layer [P_fb ; G_L P_fb] ([2D, D]), the operands of the feedback LayerNorm's input gradient
+  bf16 *dcat, *wcat;
   float *dT, *d_top, *d_lp, *d_fp, *d_lr, *dA, *dG, *dx;
   void* blas;
   void* blas_side;
@@ -1295,6 +1302,8 @@ size_t block_bwd_ws_layout(int64_t L, int64_t S, int64_t B, int64_t D, BlockBwdW
   t.d_zl = (bf16*)take(rowh);
   t.d_lp_h = (bf16*)take(rowh);
   t.d_fp_h = (bf16*)take(rowh);
+  t.dcat = (bf16*)take(2 * rowh);
+  t.wcat = (bf16*)take((size_t)L * 2 * D * D * sizeof(bf16));
   t.dT = (float*)take(3 * rowf);
   t.d_top = (float*)take(rowf);
   t.d_lp = (float*)take(rowf);
@@ -1360,6 +1369,15 @@ int block_grid_bwd(const flb_block_weights* W, const void* x, const void* grids,
   if (ce != cudaSuccess) return check_cuda(ce, "block_grid_bwd dx reset");
   const bf16* ext3 = (const bf16*)dgrids[3];
   int launches = 1;
+  if (saved) {
+    // per layer [P_fb ; G_L P_fb] ([2D, D] bf16): P_fb copied in, the product below it
+    ce = cudaMemcpy2DAsync(w.wcat, 2 * DD * sizeof(bf16), W->w_prior_fdbk, DD * sizeof(bf16),
+                           DD * sizeof(bf16), (size_t)L, cudaMemcpyDeviceToDevice, s);
+    if (ce != cudaSuccess) return check_cuda(ce, "block_grid_bwd weight copy");
+    if ((st = gemm_rm(hb, false, false, Di, Di, Di, W->w_gate_l, Di, DD, W->w_prior_fdbk, Di, DD,
+                      w.wcat + DD, Di, 2 * DD, Li, 0.f, CUDA_R_16BF)) != FLB_OK)
+      return st;
+  }
   for (int T = ticks - 1; T >= 0; --T) {
     const Tick tk = tick_of(T, Li, Si);
     const int n = tk.n, l0 = tk.l0;
@@ -1429,7 +1447,7 @@ int block_grid_bwd(const flb_block_weights* W, const void* x, const void* grids,
     // sensory gate
     if ((ce = launch_pdl(blk_gx_bwd_kernel, pair_grid, pair_block, 0, s, w.dT, f_zx, W->b_gate_x,
                          g, xb, w.d_top, w.dG, dx, d_zx, w.d_lr, w.d_fp, d_fp_h, cs,
-                         G->b_gate_x, T, l0, Si, Bi, Di)) != cudaSuccess)
+                         saved ? w.dcat : nullptr, G->b_gate_x, T, l0, Si, Bi, Di)) != cudaSuccess)
       return check_cuda(ce, "block_grid_bwd launch");
     if ((st = gemm_rm(hb, false, false, Bi, Di, Di, d_zx, Di, cs, Wgx, Di, 2 * DD, w.d_lr, Di, BD,
                       n, 1.f)) != FLB_OK)
@@ -1440,12 +1458,14 @@ int block_grid_bwd(const flb_block_weights* W, const void* x, const void* grids,
       return st;
     // lateral gate
     if ((ce = launch_pdl(blk_gl_bwd_kernel, pair_grid, pair_block, 0, s, w.d_lr, f_zl,
-                         W->b_gate_l, f_lat, w.d_lp, d_lp_h, d_zl, cs, G->b_gate_l, l0, Bi,
-                         Di)) != cudaSuccess)
+                         W->b_gate_l, f_lat, w.d_lp, d_lp_h, d_zl, cs, saved ? w.dcat : nullptr,
+                         G->b_gate_l, l0, Bi, Di)) != cudaSuccess)
       return check_cuda(ce, "block_grid_bwd launch");
-    // d_fdbk_prior = bf16(d_zL G_L + its bf16 partial from the sensory-gate backward)
-    if ((st = gemm_rm(hb, false, false, Bi, Di, Di, d_zl, Di, cs, Wgl, Di, 2 * DD, d_fp_h, Di, cs,
-                      n, 1.f, CUDA_R_16BF)) != FLB_OK)
+    // d_fdbk_prior = bf16(d_zL G_L + its bf16 partial from the sensory-gate backward); with the
+    // intermediates kept it is formed after the tick loop for all cells at once (the tick's
+    // chain needs only its product with P_fb, below)
+    if (!saved && (st = gemm_rm(hb, false, false, Bi, Di, Di, d_zl, Di, cs, Wgl, Di, 2 * DD, d_fp_h,
+                                Di, cs, n, 1.f, CUDA_R_16BF)) != FLB_OK)
       return st;
     if (!saved && (st = fork(3)) != FLB_OK) return st;
     if (!saved && (st = gemm_rm(hs, true, false, Di, Di, Bi, w.d_zl, Di, BD, w.f.tok + 2 * D, 3 * Di, 3 * BD,
@@ -1462,9 +1482,16 @@ int block_grid_bwd(const flb_block_weights* W, const void* x, const void* grids,
                              Di, BD, n, 0.f)) != FLB_OK) {
       return st;
     }
-    if ((st = gemm_rm(hb, false, false, Bi, Di, Di, d_fp_h, Di, cs, Wpf, Di, 2 * DD,
-                      w.dA + n * BD, Di, BD, n, 0.f)) != FLB_OK)
+    if (saved) {
+      // d_LN_diag = d_fdbk_prior P_fb = [partial | d_zL] [P_fb ; G_L P_fb]: one K = 2D GEMM
+      if ((st = gemm_rm(hb, false, false, Bi, Di, 2 * Di, w.dcat, 2 * Di, 2 * BD,
+                        w.wcat + (int64_t)l0 * 2 * DD, Di, 4 * DD, w.dA + n * BD, Di, BD, n,
+                        0.f)) != FLB_OK)
+        return st;
+    } else if ((st = gemm_rm(hb, false, false, Bi, Di, Di, d_fp_h, Di, cs, Wpf, Di, 2 * DD,
+                             w.dA + n * BD, Di, BD, n, 0.f)) != FLB_OK) {
       return st;
+    }
     if (!saved && (st = fork(4)) != FLB_OK) return st;
     if (!saved && (st = gemm_rm(hs, true, false, Di, Di, Bi, w.d_lp_h, Di, BD, w.f.ln, Di, BD,
                       G->w_prior_lat + (int64_t)l0 * DD, Di, 2 * DD, n, 1.f)) != FLB_OK)
@@ -1490,6 +1517,10 @@ int block_grid_bwd(const flb_block_weights* W, const void* x, const void* grids,
     auto pl = [&](int p) { return planes + plane_offset(p, LS, BD); };
     const long long c1 = (long long)S * BD, c3 = 3 * c1, c9 = 9 * c1;  // a layer's cells, per plane
     const int K1 = (int)(S * B), K3 = 3 * K1;
+    // d_fdbk_prior of every cell = bf16(its partial + d_zL G_L), per layer over all its rows
+    if ((st = gemm_rm(hb, false, false, K1, Di, Di, pl(PL_DZL), Di, c1, W->w_gate_l, Di, DD,
+                      pl(PL_DFP), Di, c1, Li, 1.f, CUDA_R_16BF)) != FLB_OK)
+      return st;
     if ((st = gemm_rm(hb, true, false, Di, Di, K3, pl(PL_DO), Di, c3, pl(PL_ATT), Di, c3, G->w_o, Di,
                       DD, Li, 1.f)) != FLB_OK)
       return st;
